@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the sgemm/dgemm hot path on B200 — prints ONE JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
+
+Metric: sgemm/dgemm TFLOP/s and % of FP32/FP64 peak, FLOPs
+counted as the reference counts them, 2*m*n*k + 2*m*n
+(benchmarks/sgemm/wgblas/sgemm.js:72-73).
+
+Workloads:
+  sgemm4096   configs[1]: sgemm 4096^3 column-major TN, alpha=1, beta=0, A,B ~ N(0,1), C=0
+              (the default at N=1)
+  dgemm4096   configs[2]: dgemm 4096^3 column-major NT, alpha=-0.75, beta=1.25, U[-1,1]
+  sgemm512    configs[0]: sgemm 512^3 NN, alpha=1.5, beta=0.5, U[-1,1]
+  ragged      configs[3]: sgemm 1000x1023x777, lda=1024 ldb=800 ldc=1040, NN
+A step is one sgemm/dgemm call on operands resident in HBM; L2 is flushed
+(a 512 MB device write) between steps, outside the per-step CUDA events.
+With --gpus N>1 (torchrun), every rank runs the same workload on its own GPU
+(independent replicas; value = sum over ranks of their work / max rank time).
+
+--impl reference times the reference's arithmetic on the host cores instead:
+the CPU oracle's restatement of the reference's fp32 shader arithmetic
+(oracle/, "port"; the reference itself runs only through WebGPU, which has no
+stack on these boxes), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "sgemm/dgemm TFLOP/s & % of FP32/FP64 peak at 4096³ (1 GPU), 16384³ at 1/2/4/8"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+WORKLOADS = {
+    "sgemm4096": dict(routine="sgemm", config_index=1, transA=1, transB=0, m=4096, n=4096, k=4096,
+                      lda=4096, ldb=4096, ldc=4096, alpha=1.0, beta=0.0, data="normal"),
+    "dgemm4096": dict(routine="dgemm", config_index=2, transA=0, transB=1, m=4096, n=4096, k=4096,
+                      lda=4096, ldb=4096, ldc=4096, alpha=-0.75, beta=1.25, data="uniform"),
+    "sgemm512": dict(routine="sgemm", config_index=0, transA=0, transB=0, m=512, n=512, k=512,
+                     lda=512, ldb=512, ldc=512, alpha=1.5, beta=0.5, data="uniform"),
+    "ragged": dict(routine="sgemm", config_index=3, transA=0, transB=0, m=1000, n=1023, k=777,
+                   lda=1024, ldb=800, ldc=1040, alpha=0.3, beta=-2.0, data="uniform"),
+}
+
+
+def flops(w):
+    return 2.0 * w["m"] * w["n"] * w["k"] + 2.0 * w["m"] * w["n"]
+
+
+def stored(w):
+    a = (w["k"], w["m"]) if w["transA"] else (w["m"], w["k"])
+    b = (w["n"], w["k"]) if w["transB"] else (w["k"], w["n"])
+    return a, b
+
+
+def host_inputs(wg, w, pinned=False):
+    """Seeded column-major operands at the workload's leading dimensions."""
+    (ar, ac), (br, bc) = stored(w)
+    dt = np.float64 if w["routine"] == "dgemm" else np.float32
+    sizes = (w["lda"] * ac, w["ldb"] * bc, w["ldc"] * w["n"])
+    out = []
+    for seed, size in zip((1, 2, 3), sizes):
+        arr = wg.pinned_empty(size, dt) if pinned else np.empty(size, dt)
+        if w["data"] == "normal" and seed != 3:
+            (wg.randomNormalFloat64Array if dt == np.float64 else wg.randomNormalFloat32Array)(size, seed, out=arr)
+        elif w["data"] == "normal":
+            arr[:] = 0
+        else:
+            wg.fill_uniform(arr, -1.0, 1.0, seed)
+        out.append(arr)
+    return out
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.path) as fh:
+                for line in fh:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                        rows.append(parts)
+        finally:
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            return json.load(fh), "measured (MEASURED_PEAKS.json)"
+    return FALLBACK_PEAKS, "fallback (profiling recipe)"
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def gemm_enqueue(wg, dev, w, GA, GB, GC):
+    """One step on resident operands, queued on the device stream (no host sync)."""
+    nat = wg._native
+    fn = nat.lib.wg_dgemm if w["routine"] == "dgemm" else nat.lib.wg_sgemm
+    nat.check(fn(dev.handle, w["transA"], w["transB"], w["m"], w["n"], w["k"], w["alpha"], GA._buf, 0, w["lda"],
+                 GB._buf, 0, w["ldb"], w["beta"], GC._buf, 0, w["ldc"], None))
+
+
+def time_resident(wg, dev, w, steps, warmup, world, flush):
+    """Device-timed steps on resident operands: returns (ms_per_step list, profile, launches)."""
+    import torch
+
+    A, B, C = host_inputs(wg, w)
+    (ar, ac), (br, bc) = stored(w)
+    GA = wg.GpuMatrix.from_(dev, A, ar, ac, w["lda"], "column-major")
+    GB = wg.GpuMatrix.from_(dev, B, br, bc, w["ldb"], "column-major")
+    GC = wg.GpuMatrix.from_(dev, C, w["m"], w["n"], w["ldc"], "column-major")
+    stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                flush.add_(1.0)
+                gemm_enqueue(wg, dev, w, GA, GB, GC)
+            dev.synchronize()
+            dev.check()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            barrier(world)
+            dev.synchronize()
+            dev.profile_read()
+            dev.set_profiling(True)
+            launches0 = dev.kernel_launches()
+            t0 = time.perf_counter()
+            for i in range(steps):
+                flush.add_(1.0)  # writes 512 MB: evicts the operands from the 126 MB L2
+                starts[i].record(stream)
+                gemm_enqueue(wg, dev, w, GA, GB, GC)
+                ends[i].record(stream)
+            dev.synchronize()
+            wall = time.perf_counter() - t0
+            launches = dev.kernel_launches() - launches0
+            dev.set_profiling(False)
+            prof = dev.profile_read()
+            dev.check()
+            ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    finally:
+        for g in (GA, GB, GC):
+            g.destroy()
+    return ms, prof, launches, wall
+
+
+def time_e2e(wg, dev, w, steps, warmup):
+    """The same metric through the public API on page-locked host arrays: every step
+    uploads op(A), op(B) (and C when beta != 0), computes, and reads C back."""
+    A, B, C = host_inputs(wg, w, pinned=True)
+    out = wg.pinned_empty(C.size, C.dtype)
+    fn = wg.dgemm if w["routine"] == "dgemm" else wg.sgemm
+    tA = "transpose" if w["transA"] else "no-transpose"
+    tB = "transpose" if w["transB"] else "no-transpose"
+    args = (tA, tB, w["m"], w["n"], w["k"], w["alpha"], A, w["lda"], B, w["ldb"], w["beta"], C, w["ldc"],
+            "column-major")
+    for _ in range(max(1, warmup // 2)):
+        fn(dev, *args, out=out)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        fn(dev, *args, out=out)
+        times.append(time.perf_counter() - t0)
+    (ar, ac), (br, bc) = stored(w)
+    item = C.dtype.itemsize
+    h2d = (ar * ac + br * bc + (w["m"] * w["n"] if w["beta"] != 0 else 0)) * item
+    d2h = w["m"] * w["n"] * item
+    sec = statistics.mean(times)
+    return {"value": flops(w) / sec / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": sec * 1e3, "api": f"wgblas_b200.{w['routine']}"}
+
+
+def cpu_baseline(w, target_s=12.0):
+    """The oracle's restatement of the reference's arithmetic on the host cores, on a
+    slab of C's columns sized for about target_s seconds, scaled to TFLOP/s."""
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as o
+
+    o.build()
+    threads = o.default_threads()
+    (ar, ac), (br, bc) = stored(w)
+    m, k = w["m"], w["k"]
+    dt = np.float64 if w["routine"] == "dgemm" else np.float32
+    rng = np.random.default_rng(0)
+    A = rng.uniform(-1, 1, w["lda"] * ac).astype(dt)
+
+    def run(ns):
+        B = rng.uniform(-1, 1, (w["ldb"] * (ns if not w["transB"] else bc))).astype(dt)
+        ldb = w["ldb"]
+        C = np.zeros(w["ldc"] * ns, dt)
+        t0 = time.perf_counter()
+        if w["routine"] == "dgemm":
+            o.dgemm_dd(w["transA"], w["transB"], m, ns, k, w["alpha"], A, w["lda"], B, ldb, w["beta"], C, w["ldc"],
+                       threads=threads)
+        else:
+            o.sgemm(w["transA"], w["transB"], m, ns, k, w["alpha"], A, w["lda"], B, ldb, w["beta"], C, w["ldc"],
+                    variant=1, threads=threads)
+        return time.perf_counter() - t0
+
+    ns = max(1, min(w["n"], threads))
+    t = run(ns)
+    while t < 1.0 and ns < w["n"]:
+        ns = min(w["n"], ns * 4)
+        t = run(ns)
+    if t < target_s and ns < w["n"]:
+        ns = min(w["n"], max(ns, int(ns * target_s / max(t, 1e-3))))
+        t = run(ns)
+    f = 2.0 * m * ns * k + 2.0 * m * ns
+    kind = "double-double restatement" if w["routine"] == "dgemm" else "fp32 FMA restatement"
+    return {"value": f / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{ns} of {w['n']} columns of C ({m}x{ns}x{k}), {kind} of the reference's shader "
+                      f"arithmetic (oracle/oracle.c), {t:.1f} s", "seconds": t}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    w = WORKLOADS[pick_workload(args, world)]
+    vals = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(w, target_s=max(2.0, 60.0 / (args.warmup + args.steps)))
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    value = statistics.mean(vals)
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": flops(w) / (value * 1e12) * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64 (double-double)" if w["routine"] == "dgemm" else "f32",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": config_of(w, args.workload),
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
+                             "sample": cb["sample"]},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def pick_workload(args, world):
+    return "sgemm4096" if args.workload == "auto" else args.workload
+
+
+def config_of(w, name):
+    return {"workload": f"configs[{w['config_index']}] {w['routine']} {w['m']}x{w['n']}x{w['k']} "
+                        f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major",
+            "m": w["m"], "n": w["n"], "k": w["k"], "lda": w["lda"], "ldb": w["ldb"], "ldc": w["ldc"],
+            "alpha": w["alpha"], "beta": w["beta"], "inputs": "N(0,1) seeded" if w["data"] == "normal" else "U[-1,1] seeded",
+            "l2": "flushed between steps (512 MB device write outside the step events)"}
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["auto"] + sorted(WORKLOADS), default="auto")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extra", action="store_true", help="skip the secondary workloads and probes")
+    args = p.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+
+    sys.path.insert(0, ROOT)
+    import wgblas_b200 as wg
+
+    dev = wg.init(device=local)
+    torch.cuda.set_device(local)
+    w = WORKLOADS[pick_workload(args, world)]
+    flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=f"cuda:{local}")  # 512 MB
+
+    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    smi_index = phys[local] if len(phys) > local and phys[local].strip() else str(local)
+    with Clocks(smi_index) as clk:
+        ms, prof, launches, wall = time_resident(wg, dev, w, args.steps, args.warmup, world, flush)
+    clocks = clk.summary()
+    step_ms = statistics.mean(ms)
+    step_ms_max = max_over_ranks(step_ms, world)
+    value = flops(w) * world / (step_ms_max * 1e-3) / 1e12
+
+    peaks, peak_src = measured_peaks()
+    extra = {}
+    fp32_peak = fp64_peak = hbm = None
+    if not args.no_extra and rank == 0:
+        fp32_peak = dev.probe_peak("fp32")
+        fp64_peak = dev.probe_peak("fp64")
+        hbm = dev.probe_peak("hbm")
+        extra["probes"] = {"fp32_ffma_tflops": fp32_peak, "fp64_dfma_tflops": fp64_peak, "hbm_copy_gbs": hbm,
+                           "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
+        extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
+        for name in ("dgemm4096", "sgemm512", "ragged"):
+            if name == pick_workload(args, world):
+                continue
+            wx = WORKLOADS[name]
+            msx, profx, _, _ = time_resident(wg, dev, wx, max(3, args.steps // 2), 3, 1, flush)
+            tf = flops(wx) / (statistics.mean(msx) * 1e-3) / 1e12
+            pk = fp64_peak if wx["routine"] == "dgemm" else fp32_peak
+            extra[name] = {"tflops": tf, "ms_per_step": statistics.mean(msx),
+                           f"pct_of_{'fp64' if wx['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf / pk,
+                           "kernels": {k: v[1] / max(v[0], 1) for k, v in profx.items()}}
+
+    # Roofline of the dominant kernel, from the per-kernel events of the timed region.
+    dom = max(prof.items(), key=lambda kv: kv[1][1]) if prof else ("?", (1, step_ms))
+    dom_ms = dom[1][1] / max(dom[1][0], 1)
+    achieved = flops(w) / (dom_ms * 1e-3) / 1e12
+    if dom[0].startswith("sgemm_tf32x3"):
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) * 0.5 / 3.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": None,
+                "peak_basis": f"{peak_src} bf16 dense x 0.5 (tf32 rate) / 3 products = 3xTF32 ceiling in fp32 FLOPs"}
+    else:
+        peak = (fp64_peak if w["routine"] == "dgemm" else fp32_peak) or None
+        roof = {"bound": "fp64-simt" if w["routine"] == "dgemm" else "fp32-simt", "achieved": achieved,
+                "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None, "traffic": None,
+                "peak_basis": "FMA-chain probe measured in this run (no FP32/FP64 SIMT figure in MEASURED_PEAKS.json)"}
+    roof["kernel"] = dom[0]
+    roof["kernel_ms"] = dom_ms
+    roof["kernels"] = {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in prof.items()}
+
+    e2e = time_e2e(wg, dev, w, max(3, args.steps // 2), args.warmup) if rank == 0 else None
+    cb = None if (args.no_cpu_baseline or rank != 0 or world > 1) else cpu_baseline(w)
+    barrier(world)
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f64" if w["routine"] == "dgemm" else "f32",
+                "data": "synthetic (seeded mulberry32)", "config": config_of(w, args.workload),
+                "roofline": roof, "cpu_baseline": cb, "e2e": e2e,
+                "gpu_launches": int(max_over_ranks(launches, world) * world) if world > 1 else int(launches),
+                "clocks": clocks, "wall_s_timed_region": wall, "extra": extra}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

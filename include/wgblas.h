@@ -1,0 +1,210 @@
+/*
+ * wgblas-b200 C ABI — the drop-in boundary under wgblas's JavaScript API for
+ * the level-3 GEMM path (sgemm / dgemm), built for B200 (sm_100a).
+ *
+ * Every function returns a wg_status; on failure wg_last_error() gives the
+ * message (per calling thread). No torch or CUDA types appear in signatures:
+ * streams are passed as void*.
+ *
+ * GEMM calls use the column-major BLAS frame (Fortran BLAS convention):
+ *   C[i + j*ldc] := alpha * sum_p op(A)(i,p) * op(B)(p,j) + beta * C[i + j*ldc]
+ *   op(A)(i,p) = transA ? A[p + i*lda] : A[i + p*lda]        (i < m, p < k)
+ *   op(B)(p,j) = transB ? B[j + p*ldb] : B[p + j*ldb]        (p < k, j < n)
+ * The language layer maps wgblas's row-major default and per-matrix layouts
+ * onto this frame, as src/sgemm/sgemm.mjs:151-167 maps them onto its row-major
+ * kernel frame.
+ *
+ * BLAS rules kept from the reference:
+ *   - m == 0 or n == 0 returns without touching C (src/sgemm/sgemm.mjs:83);
+ *   - alpha == 0 reads neither A nor B, so NaN/Inf there cannot reach C
+ *     (src/shaders/sgemm_large.wgsl:299-303);
+ *   - beta == 0 does not read C, so NaN/Inf already in C are overwritten
+ *     (sgemm_large.wgsl:296-298);
+ *   - sgemm with k == 0 still writes alpha*0 + beta*C (tests/sgemm/src/test.sgemm.js:304-351);
+ *   - dgemm returns C untouched when (alpha == 0 or k == 0) and beta == 1
+ *     (src/dgemm/dgemm.mjs:177-179);
+ *   - elements of C outside the m x n block (leading-dimension padding) are
+ *     never written.
+ */
+#ifndef WGBLAS_H
+#define WGBLAS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WG_ABI_VERSION 1
+
+typedef enum wg_status {
+  WG_OK = 0,
+  WG_ERR_INVALID_ARGUMENT = 1, /* a size, stride, pointer or flag is out of range */
+  WG_ERR_OUT_OF_MEMORY = 2,    /* device or pinned host allocation failed */
+  WG_ERR_CUDA = 3,             /* a CUDA runtime or driver call failed */
+  WG_ERR_NO_DEVICE = 4,        /* no CUDA device, or the ordinal does not exist */
+  WG_ERR_KERNEL_TIMEOUT = 5,   /* a bounded device-side wait gave up (see wg_device_check) */
+  WG_ERR_NCCL = 6,             /* a collective failed or timed out */
+  WG_ERR_NOT_SUPPORTED = 7     /* the device is not sm_100 or the feature is absent */
+} wg_status;
+
+typedef struct wg_device wg_device;
+typedef struct wg_buffer wg_buffer;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *wg_last_error(void);
+/* WG_ABI_VERSION of the loaded library. */
+int wg_abi_version(void);
+
+/* ---- devices: replace src/init.mjs:31-143 (init / cleanup / gpuName) ------ */
+
+/* Number of visible CUDA devices (0 when none). */
+wg_status wg_device_count(int *count);
+
+#define WG_DEVICE_TIMING 1u /* benchmark mode: GEMM calls can report gpu_ms */
+
+/* Opens a handle on CUDA device `ordinal` with its own non-blocking stream.
+ * Several handles may name the same ordinal (src/init.mjs:14-29 creates one
+ * device per option set); each has its own stream. */
+wg_status wg_device_open(int ordinal, unsigned flags, wg_device **out);
+/* Waits for the handle's work, then releases its stream and workspace
+ * (src/init.mjs:110-131). Buffers allocated on it must be freed first or are
+ * leaked. */
+wg_status wg_device_close(wg_device *dev);
+/* Device name, as gpuName() reports it (src/init.mjs:133-143). */
+wg_status wg_device_name(const wg_device *dev, char *buf, size_t len);
+typedef struct wg_device_props {
+  int ordinal;
+  int sm_count;
+  int cc_major, cc_minor;
+  size_t total_mem;
+  unsigned flags;
+} wg_device_props;
+wg_status wg_device_props_get(const wg_device *dev, wg_device_props *props);
+/* The stream all of this handle's work is ordered on (a cudaStream_t). */
+wg_status wg_device_stream(const wg_device *dev, void **stream);
+/* Orders this handle's work on a caller-owned cudaStream_t instead; NULL
+ * restores the handle's own stream. */
+wg_status wg_device_set_stream(wg_device *dev, void *stream);
+/* Waits until the handle's stream is idle. */
+wg_status wg_device_sync(wg_device *dev);
+/* Waits, then reports (and clears) a device-side error word: WG_ERR_KERNEL_TIMEOUT
+ * when a kernel's bounded wait gave up since the last check. */
+wg_status wg_device_check(wg_device *dev);
+
+/* Counters of the sgemm dispatcher since the handle was opened (synchronises). */
+typedef struct wg_sgemm_stats {
+  uint64_t calls;           /* sgemm calls that reached a kernel */
+  uint64_t tf32x3_launches; /* calls dispatched to the 3xTF32 tensor-core kernel */
+  uint64_t simt_launches;   /* calls dispatched straight to the FFMA kernel */
+  uint64_t fallbacks;       /* 3xTF32 calls that found non-finite or out-of-range
+                               operands on the device and ran the FFMA kernel instead */
+} wg_sgemm_stats;
+wg_status wg_device_sgemm_stats(wg_device *dev, wg_sgemm_stats *stats);
+
+/* sgemm kernel choice: AUTO picks by shape and alignment; the others force one
+ * kernel (tests and benchmarks). */
+#define WG_SGEMM_AUTO 0
+#define WG_SGEMM_SIMT 1
+#define WG_SGEMM_TF32X3 2
+wg_status wg_device_set_sgemm_path(wg_device *dev, int path);
+
+/* Per-kernel device time of this handle's own launches, for benchmarks and
+ * roofline reports. While profiling is on, every kernel the library launches
+ * on the handle is bracketed by CUDA events on its stream. */
+wg_status wg_device_set_profiling(wg_device *dev, int on);
+typedef struct wg_kernel_profile {
+  char name[48];     /* kernel family, e.g. "sgemm_simt", "sgemm_tf32x3_mma" */
+  uint64_t launches; /* launches since the last read */
+  double total_ms;   /* summed device time of those launches */
+} wg_kernel_profile;
+/* Waits for the handle's work, fills up to `max` entries, sets *count, and
+ * resets the accumulators. */
+wg_status wg_device_profile_read(wg_device *dev, wg_kernel_profile *out, int max, int *count);
+/* Kernels the library has launched on this handle since it was opened. */
+wg_status wg_device_kernel_launches(const wg_device *dev, uint64_t *launches);
+
+/* ---- roofline probes: benchmarks/roofline (FMA peak and bandwidth) ------- */
+#define WG_PROBE_FP32_FMA 0 /* value: TFLOP/s of FFMA chains on every SM */
+#define WG_PROBE_FP64_FMA 1 /* value: TFLOP/s of DFMA chains on every SM */
+#define WG_PROBE_HBM_COPY 2 /* value: GB/s (read + write) of a 2 GiB device copy */
+wg_status wg_probe_peak(wg_device *dev, int kind, double *value);
+
+/* ---- device buffers: replace the storage of GpuMatrix / GpuVector ------- */
+/* (src/classes/GpuMatrix.mjs:43-207, src/util/buffer.mjs:58-78,134-227)     */
+
+wg_status wg_buffer_alloc(wg_device *dev, size_t bytes, wg_buffer **out);
+wg_status wg_buffer_free(wg_buffer *buf);
+wg_status wg_buffer_size(const wg_buffer *buf, size_t *bytes);
+wg_status wg_buffer_device_ptr(const wg_buffer *buf, void **ptr);
+/* Copies `bytes` from host memory into the buffer at byte `offset`, ordered on
+ * the device stream; returns once the host memory may be reused. */
+wg_status wg_buffer_upload(wg_buffer *buf, size_t offset, const void *host, size_t bytes);
+/* Copies from the buffer to host memory; returns when the data has arrived. */
+wg_status wg_buffer_download(const wg_buffer *buf, size_t offset, void *host, size_t bytes);
+/* Strided forms: `rows` chunks of `width` bytes, `spitch`/`dpitch` bytes apart
+ * (GpuMatrix.read() strips lda padding this way, src/classes/GpuMatrix.mjs:193-201). */
+wg_status wg_buffer_upload_2d(wg_buffer *buf, size_t offset, size_t dpitch, const void *host,
+                              size_t spitch, size_t width, size_t rows);
+wg_status wg_buffer_download_2d(const wg_buffer *buf, size_t offset, size_t spitch, void *host,
+                                size_t dpitch, size_t width, size_t rows);
+
+/* Page-locked host memory: copies from/to it run at full PCIe rate and
+ * asynchronously. */
+wg_status wg_host_alloc(size_t bytes, void **ptr);
+wg_status wg_host_free(void *ptr);
+
+/* ---- GEMM on device buffers: replace src/sgemm/sgemm.mjs:25-269 and ----- */
+/* ---- src/dgemm/dgemm.mjs:23-318 with their WGSL kernels -------------------- */
+/* off* are element offsets into the buffers. gpu_ms, when non-NULL on a
+ * handle opened with WG_DEVICE_TIMING, receives the kernel time measured with
+ * CUDA events (the reference's gpuTimeMs, src/util/benchmark.mjs:93-103); the
+ * call then waits for completion. Otherwise the call returns once the work is
+ * queued on the device stream. */
+wg_status wg_sgemm(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                   float alpha, const wg_buffer *A, int64_t offA, int64_t lda,
+                   const wg_buffer *B, int64_t offB, int64_t ldb, float beta,
+                   wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms);
+wg_status wg_dgemm(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                   double alpha, const wg_buffer *A, int64_t offA, int64_t lda,
+                   const wg_buffer *B, int64_t offB, int64_t ldb, double beta,
+                   wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms);
+
+/* GEMM on raw device pointers already on this handle's device, ordered on its
+ * stream (interop with other CUDA code). Same semantics as wg_sgemm. */
+wg_status wg_sgemm_dev(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                       float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                       float beta, float *C, int64_t ldc);
+wg_status wg_dgemm_dev(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                       double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
+                       double beta, double *C, int64_t ldc);
+
+/* GEMM on host arrays — the typed-array path of sgemm()/dgemm()
+ * (src/sgemm/sgemm.mjs:179-262): uploads op(A), op(B) and (when beta != 0) the
+ * m x n block of C, runs the kernel, and writes the m x n block of the result
+ * into C_out (which may be C_in; its other elements are not touched). Returns
+ * when C_out holds the result. Page-locked host arrays (wg_host_alloc) are
+ * copied asynchronously at full rate. */
+wg_status wg_sgemm_host(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                        float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                        float beta, const float *C_in, float *C_out, int64_t ldc, float *gpu_ms);
+wg_status wg_dgemm_host(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                        double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
+                        double beta, const double *C_in, double *C_out, int64_t ldc,
+                        float *gpu_ms);
+
+/* ---- seeded inputs: src/random/random.mjs:4-26 ------------------------------ */
+/* randomFloat32Array(n, low, high, seed) / randomFloat64Array: mulberry32 draws
+ * u in [0, 1), out[i] = low + u*(high-low) formed in double. */
+void wg_random_f32(float *out, int64_t n, double low, double high, uint32_t seed);
+void wg_random_f64(double *out, int64_t n, double low, double high, uint32_t seed);
+/* Standard normal draws: Box-Muller over the same mulberry32 stream (an
+ * addition; the reference has no normal generator). */
+void wg_random_normal_f32(float *out, int64_t n, uint32_t seed);
+void wg_random_normal_f64(double *out, int64_t n, uint32_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WGBLAS_H */

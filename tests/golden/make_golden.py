@@ -1,0 +1,196 @@
+"""Generates the golden fixtures in tests/golden/ from the reference's own test data.
+
+Run once in a checkout that has the reference tree (its path is the first
+argument, default ../reference relative to the repo's parent); the outputs are
+committed so the tests never read the reference at run time.
+
+Outputs
+-------
+gemm_edge_cases.json
+    Every case of the reference's tests/{sgemm,dgemm}/edge-cases.json and
+    edge-cases-column-major.json (inputs copied as data), each with the exact
+    expected C. The reference checks these bit for bit against stdlib
+    (tests/sgemm/src/test.sgemm.js:126-164,354-394; tests/dgemm/src/test.dgemm.js).
+    Their values are small integers, so the expected output is computed here
+    with exact rational arithmetic and then checked to be representable in f32:
+    any correct GEMM must reproduce it exactly.
+dd_lanes.json
+    The lane cases of tests/shaders/src/test.dekker.js:98-138 (inputs and the
+    expected result of twoSum, twoProdBit, ddAdd and ddMul per lane), restated
+    with the same rules: exact results for the error-free transforms, hi+lo
+    within 2^-40 of the f64 value for the double-double ops, and (value, 0) for
+    a non-finite hi.
+validation_params.json
+    The parameter specs the reference's sgemm/dgemm validation tests load
+    (tests/validation/params/{device,trans,layout,m,n,k,alpha,beta,A,B,C,ld}.json,
+    read by tests/sgemm/src/test.sgemm.js:23-56), copied as data: the invalid
+    values with their expected error substrings and the edge values that must
+    not throw. tests/validation_runner.py replays them.
+mulberry32.json
+    The first draws of mulberry32 (src/random/random.mjs:4-12) for the seeds the
+    reference's GEMM tests use, computed by a second, independent restatement of
+    the JS integer arithmetic in pure Python (arbitrary-precision ints masked to
+    32 bits). The C oracle and the product library are both checked against it.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+from fractions import Fraction
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def f32(x: float) -> float:
+    """Math.fround: round to nearest f32, overflowing to +-Infinity."""
+    with np.errstate(over="ignore"):
+        return float(np.float32(x))
+
+
+def op_elem(M, ld, layout, trans, row, col):
+    """op(M)[row, col] for a matrix stored in `layout` (tests/sgemm/helpers.js:8-11)."""
+    sr, sc = (col, row) if trans == "transpose" else (row, col)
+    return M[sc * ld + sr] if layout == "column-major" else M[sr * ld + sc]
+
+
+def c_index(ldc, layout, row, col):
+    return col * ldc + row if layout == "column-major" else row * ldc + col
+
+
+def exact_gemm(case):
+    layout = case.get("layout", "row-major")
+    m, n, k = case["m"], case["n"], case["k"]
+    alpha, beta = Fraction(case["alpha"]), Fraction(case["beta"])
+    out = list(case["C"])
+    for i in range(m):
+        for j in range(n):
+            acc = Fraction(0)
+            for p in range(k):
+                acc += Fraction(op_elem(case["A"], case["lda"], layout, case["transA"], i, p)) * \
+                    Fraction(op_elem(case["B"], case["ldb"], layout, case["transB"], p, j))
+            ci = c_index(case["ldc"], layout, i, j)
+            val = alpha * acc + (beta * Fraction(case["C"][ci]) if beta != 0 else 0)
+            fv = float(val)
+            if Fraction(fv) != val or f32(fv) != fv:
+                raise ValueError(f"{case['label']}: result {val} is not exact in f32")
+            out[ci] = fv
+    return out
+
+
+def edge_cases(ref):
+    cases = []
+    for routine in ("sgemm", "dgemm"):
+        for fname in ("edge-cases.json", "edge-cases-column-major.json"):
+            with open(os.path.join(ref, "tests", routine, fname)) as fh:
+                for tc in json.load(fh):
+                    case = {k: tc[k] for k in ("label", "transA", "transB", "m", "n", "k", "alpha",
+                                                "A", "lda", "B", "ldb", "beta", "C", "ldc")}
+                    case["layout"] = tc.get("layout", "row-major")
+                    case["routine"] = routine
+                    case["source"] = f"tests/{routine}/{fname}"
+                    case["expected"] = exact_gemm(case)
+                    cases.append(case)
+    return cases
+
+
+# ---- double-double lane cases (tests/shaders/src/test.dekker.js:98-138) ----
+
+def dd_lanes():
+    inf = math.inf
+    nan = math.nan
+    raw = [
+        ("finite", [1.5, -7.25, 1e10, 3], [3 * 2**-30, 0.1, -3.3e9, 1 / 3]),
+        ("Inf next to finite", [1.5, inf, -7.25, -inf], [0.1, 1, 2**-29, 2]),
+        ("NaN next to finite", [nan, 1.5, 3, nan], [1, 0.1, 2**-29, 2]),
+        ("overflow next to finite", [3e38, 1.5, -3e38, 2], [3e38, 0.25, -3e38, 1e-3]),
+    ]
+
+    def low(h):
+        return f32(h * 2**-26) if math.isfinite(h) else 0.0
+
+    def exact(v):
+        h = f32(v)
+        return {"hi": h, "lo": (v - h) if math.isfinite(h) else 0.0}
+
+    def dd(v):
+        h = f32(v)
+        if math.isfinite(h):
+            return {"value": v, "rel": 2**-40}
+        return {"hi": h, "lo": 0.0}
+
+    out = []
+    for label, a_hi, b_hi in raw:
+        ah = [f32(x) for x in a_hi]
+        bh = [f32(x) for x in b_hi]
+        al = [low(x) for x in ah]
+        bl = [low(x) for x in bh]
+        lanes = []
+        for l in range(4):
+            a, b = ah[l], bh[l]
+            av, bv = a + al[l], b + bl[l]
+            lanes.append({
+                "a_hi": a, "a_lo": al[l], "b_hi": b, "b_lo": bl[l],
+                "twoSum": exact(a + b),
+                "twoProdBit": exact(a * b),
+                "ddAdd": dd(av + bv),
+                "ddMul": dd(av * bv),
+            })
+        out.append({"label": label, "lanes": lanes})
+    return out
+
+
+# ---- mulberry32, second restatement ----
+
+def mulberry32_draws(seed: int, count: int):
+    a = seed & 0xFFFFFFFF
+    out = []
+    for _ in range(count):
+        a = (a + 0x6D2B79F5) & 0xFFFFFFFF
+        t = ((a ^ (a >> 15)) * (1 | a)) & 0xFFFFFFFF
+        t = ((t + (((t ^ (t >> 7)) * (61 | t)) & 0xFFFFFFFF)) & 0xFFFFFFFF) ^ t
+        out.append(((t ^ (t >> 14)) & 0xFFFFFFFF) / 4294967296.0)
+    return out
+
+
+def _dump(obj, name):
+    def enc(v):
+        if isinstance(v, float):
+            if math.isnan(v):
+                return "NaN"
+            if math.isinf(v):
+                return "Infinity" if v > 0 else "-Infinity"
+        if isinstance(v, dict):
+            return {k: enc(x) for k, x in v.items()}
+        if isinstance(v, list):
+            return [enc(x) for x in v]
+        return v
+
+    with open(os.path.join(HERE, name), "w") as fh:
+        json.dump(enc(obj), fh, indent=1)
+        fh.write("\n")
+
+
+def validation_params(ref):
+    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld"]
+    out = {}
+    for name in names:
+        with open(os.path.join(ref, "tests", "validation", "params", f"{name}.json")) as fh:
+            out[name] = json.load(fh)
+    return out
+
+
+def main():
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.path.join(HERE, "..", "..", "..", "reference")
+    _dump(edge_cases(ref), "gemm_edge_cases.json")
+    _dump(dd_lanes(), "dd_lanes.json")
+    _dump(validation_params(ref), "validation_params.json")
+    seeds = [0, 1, 2, 3, 42, 100, 111, 112, 113, 200, 300]
+    _dump({"draws": 16, "seeds": {str(s): mulberry32_draws(s, 16) for s in seeds}}, "mulberry32.json")
+
+
+if __name__ == "__main__":
+    main()

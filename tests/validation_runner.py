@@ -1,0 +1,140 @@
+"""Replays the reference's spec-driven argument validation for sgemm / dgemm.
+
+Follows tests/helpers/validation.js (runValidation, :455-560): a baseline
+argument set is built from the specs in tests/golden/validation_params.json
+(the reference's tests/validation/params/*.json); each invalid entry replaces
+exactly one argument and must raise an error whose message contains the
+entry's text, and each edge entry must not raise. The spec set per routine is
+the one tests/sgemm/src/test.sgemm.js:23-56 and tests/dgemm/src/test.dgemm.js:36-88
+assemble.
+"""
+from __future__ import annotations
+
+import copy
+import math
+
+import numpy as np
+
+from conftest import load_golden
+
+SPECIALS = {
+    "NaN": math.nan, "Infinity": math.inf, "-Infinity": -math.inf, "null": None,
+    "undefined": None, "string": "100", "array": [], "object": {}, "number": 42,
+}
+_UNDEF = object()
+
+
+def _derive64(spec):
+    """derive64 (tests/helpers/validation.js:90-140) for the array specs B and C."""
+    out = copy.deepcopy(spec)
+    out["type"] = "float64array" if spec["type"] != "float" else "float64"
+    for e in out.get("invalid", []):
+        if isinstance(e.get("error"), str):
+            e["error"] = e["error"].replace("Float32Array", "Float64Array")
+    if spec["type"] == "float32array":
+        out["invalid"].append({"scenario": "wrongDtypeGpuMatrix",
+                               "error": "must be a Float64Array-backed GpuMatrix",
+                               "label": "GpuMatrix backed by the wrong dtype (Float32Array)"})
+    return out
+
+
+def build_specs(routine: str) -> dict:
+    P = load_golden("validation_params.json", decode=False)
+    n_spec = copy.deepcopy(P["n"])
+    n_spec["baseline"] = 2
+    n_spec["edge"] = [e for e in n_spec["edge"] if e.get("value") != -1]
+    n_spec["invalid"] = n_spec["invalid"] + [
+        {"value": -1, "error": "m, n, and k must be non-negative", "label": "negative"}]
+    m_spec = copy.deepcopy(P["m"])
+    m_spec["baseline"] = 2
+    a_base = copy.deepcopy(P["A"])
+    lvl3 = a_base.pop("level-3")
+    a_spec = {**a_base, **lvl3}
+    specs = {
+        "device": P["device"], "transA": P["trans"], "transB": P["trans"], "layout": P["layout"],
+        "m": m_spec, "n": n_spec, "k": P["k"], "alpha": P["alpha"], "beta": P["beta"],
+        "A": a_spec, "lda": P["ld"], "B": P["B"], "ldb": P["ld"], "C": P["C"], "ldc": P["ld"],
+    }
+    if routine == "dgemm":
+        a64 = copy.deepcopy(a_spec)
+        a64["type"] = "float64array"
+        for e in a64["invalid"]:
+            e["error"] = e["error"].replace("Float32Array", "Float64Array")
+        a64["invalid"].append({"scenario": "wrongDtypeGpuMatrix",
+                               "error": "must be a Float64Array-backed GpuMatrix",
+                               "label": "GpuMatrix backed by the wrong dtype (Float32Array)"})
+        specs["A"] = a64
+        specs["B"] = _derive64(P["B"])
+        specs["C"] = _derive64(P["C"])
+    return specs
+
+
+def _dtype(spec_type):
+    return np.float64 if spec_type == "float64array" else np.float32
+
+
+def _matrix_len(depends_on, dims):
+    """ndArrayLen for a matrix spec (tests/helpers/validation.js:192-253)."""
+    ld_key = next(d for d in depends_on if d.startswith("ld"))
+    trans_key = next((d for d in depends_on if d.startswith("trans")), None)
+    cm = dims.get("layout") == "column-major"
+    if trans_key and "k" in depends_on:
+        d1, d2 = [d for d in depends_on if d in ("m", "n", "k")]
+        rows, cols = (dims[d2], dims[d1]) if cm else (dims[d1], dims[d2])
+        no_t = dims.get(trans_key, "no-transpose") == "no-transpose"
+        outer, inner = (rows, cols) if no_t else (cols, rows)
+    else:  # plain m x n (C)
+        outer, inner = (dims["n"], dims["m"]) if cm else (dims["m"], dims["n"])
+    return max(0, (outer - 1) * dims[ld_key] + inner)
+
+
+def baselines(specs, device):
+    b = {}
+    for name, spec in specs.items():
+        if "baseline" in spec:
+            v = spec["baseline"]
+            b[name] = np.array(v, _dtype(spec["type"])) if isinstance(v, list) else v
+    b["device"] = device
+    for name, spec in specs.items():
+        if spec.get("type") in ("float32array", "float64array") and name not in b:
+            dims = dict(b, lda=specs["lda"]["range"]["max"])
+            b[name] = np.ones(_matrix_len(spec["dependsOn"], dims), _dtype(spec["type"]))
+    return b
+
+
+def resolve(entry, name, spec, base, make_wrong_dtype_matrix=None):
+    if "scenario" in entry:
+        sc = entry["scenario"]
+        if sc == "wrongDtypeGpuMatrix":
+            return make_wrong_dtype_matrix() if make_wrong_dtype_matrix else _UNDEF
+        n = _matrix_len(spec["dependsOn"], base)
+        if sc == "minimal":
+            return np.ones(n, _dtype(spec["type"]))
+        if sc == "tooShort":
+            return np.ones(max(0, n - 1), _dtype(spec["type"]))
+        raise ValueError(sc)
+    if "special" in entry:
+        return SPECIALS[entry["special"]]
+    v = entry["value"]
+    if isinstance(v, list) and spec.get("type") in ("float32array", "float64array"):
+        return np.array(v, _dtype(spec["type"]))
+    return v
+
+
+def cases(routine, device, kind, make_wrong_dtype_matrix=None):
+    """Yields (label, args, expected_error_or_None) for kind 'invalid' or 'edge'."""
+    specs = build_specs(routine)
+    base = baselines(specs, device)
+    for name, spec in specs.items():
+        for entry in spec.get(kind, []):
+            v = resolve(entry, name, spec, base, make_wrong_dtype_matrix)
+            if v is _UNDEF:
+                continue
+            args = dict(base)
+            args[name] = v
+            yield f"{name} {kind}: {entry.get('label', entry)}", args, entry.get("error")
+
+
+def call(fn, a):
+    return fn(a["device"], a["transA"], a["transB"], a["m"], a["n"], a["k"], a["alpha"], a["A"],
+              a["lda"], a["B"], a["ldb"], a["beta"], a["C"], a["ldc"], a["layout"])

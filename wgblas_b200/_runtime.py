@@ -1,0 +1,224 @@
+"""Device runtime: ``init`` / ``cleanup`` / ``gpuName`` on CUDA devices.
+
+Mirrors src/init.mjs:31-182. A ``Device`` stands where the reference hands out
+a ``GPUDevice``: ``init()`` caches one handle per option set and the first one
+becomes the primary device that ``getDevice()`` returns; ``cleanup(device)``
+releases one handle (promoting a survivor to primary) and ``cleanup()`` all of
+them. Several handles may sit on one GPU, each with its own CUDA stream, as
+the reference creates one GPUDevice per option set (src/init.mjs:14-29).
+
+Device choice: ``init(device=k)`` opens CUDA ordinal k. Without it the
+ordinal comes from ``WGBLAS_CUDA_DEVICES`` (a comma list; the first entry for
+"high-performance", the last for "low-power"), else "high-performance" maps to
+ordinal 0 and "low-power" to the last visible ordinal — so the reference's
+two-device example (examples/init-two-gpus/init-two-gpus.js) lands on two
+GPUs when there are two.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+import warnings
+
+from . import _native as nat
+
+
+class Error(Exception):
+    """Raised with the reference's error messages (its ``throw new Error(msg)``)."""
+
+
+class Device:
+    """A CUDA device handle: the counterpart of the reference's GPUDevice."""
+
+    __slots__ = ("_handle", "ordinal", "benchmark", "options", "_name", "__weakref__")
+
+    def __init__(self, handle, ordinal, benchmark, options, name):
+        self._handle = handle
+        self.ordinal = ordinal
+        self.benchmark = benchmark
+        self.options = options
+        self._name = name
+
+    @property
+    def handle(self):
+        if self._handle is None:
+            raise Error("device has been destroyed — call init() again.")
+        return self._handle
+
+    @property
+    def destroyed(self) -> bool:
+        return self._handle is None
+
+    def stream(self) -> int:
+        """The cudaStream_t (as an int) this device's work is ordered on."""
+        s = ct.c_void_p()
+        nat.check(nat.lib.wg_device_stream(self.handle, ct.byref(s)))
+        return s.value or 0
+
+    def set_stream(self, stream: int | None) -> None:
+        """Orders this device's work on a caller-owned stream (None: its own)."""
+        nat.check(nat.lib.wg_device_set_stream(self.handle, ct.c_void_p(stream or None)))
+
+    def synchronize(self) -> None:
+        nat.check(nat.lib.wg_device_sync(self.handle))
+
+    def check(self) -> None:
+        """Raises if a kernel's bounded device-side wait gave up since the last check."""
+        nat.check(nat.lib.wg_device_check(self.handle))
+
+    def props(self) -> dict:
+        p = nat.DeviceProps()
+        nat.check(nat.lib.wg_device_props_get(self.handle, ct.byref(p)))
+        return {f: getattr(p, f) for f, _ in p._fields_}
+
+    def sgemm_stats(self) -> dict:
+        s = nat.SgemmStats()
+        nat.check(nat.lib.wg_device_sgemm_stats(self.handle, ct.byref(s)))
+        return {f: int(getattr(s, f)) for f, _ in s._fields_}
+
+    def set_sgemm_path(self, path: str) -> None:
+        """'auto' (default), 'simt' (FFMA kernel) or 'tf32x3' (tensor-core kernel)."""
+        code = {"auto": nat.WG_SGEMM_AUTO, "simt": nat.WG_SGEMM_SIMT, "tf32x3": nat.WG_SGEMM_TF32X3}[path]
+        nat.check(nat.lib.wg_device_set_sgemm_path(self.handle, code))
+
+    def set_profiling(self, on: bool) -> None:
+        nat.check(nat.lib.wg_device_set_profiling(self.handle, int(bool(on))))
+
+    def profile_read(self) -> dict:
+        """{kernel family: (launches, total_ms)} since the last read (synchronises)."""
+        arr = (nat.KernelProfile * 32)()
+        n = ct.c_int(0)
+        nat.check(nat.lib.wg_device_profile_read(self.handle, arr, 32, ct.byref(n)))
+        return {arr[i].name.decode(): (int(arr[i].launches), float(arr[i].total_ms)) for i in range(n.value)}
+
+    def kernel_launches(self) -> int:
+        v = ct.c_uint64(0)
+        nat.check(nat.lib.wg_device_kernel_launches(self.handle, ct.byref(v)))
+        return int(v.value)
+
+    def probe_peak(self, kind: str) -> float:
+        """Roofline probe: 'fp32' / 'fp64' FMA TFLOP/s or 'hbm' copy GB/s."""
+        code = {"fp32": nat.WG_PROBE_FP32_FMA, "fp64": nat.WG_PROBE_FP64_FMA, "hbm": nat.WG_PROBE_HBM_COPY}[kind]
+        v = ct.c_double(0)
+        nat.check(nat.lib.wg_probe_peak(self.handle, code, ct.byref(v)))
+        return float(v.value)
+
+    def __repr__(self):
+        state = "destroyed" if self.destroyed else f"cuda:{self.ordinal}"
+        return f"<wgblas Device {state} {self.options}>"
+
+
+_devices: dict[str, Device] = {}
+_primary: Device | None = None
+
+
+def _options_key(o) -> str:
+    return f"{o['powerPreference']}::{o['benchmark']}::{o['device']}"
+
+
+def _ordinal_for(power_preference: str, explicit) -> int:
+    count = nat.device_count()
+    if count == 0:
+        raise Error("No CUDA device found.")
+    if explicit is not None:
+        if not isinstance(explicit, int) or isinstance(explicit, bool) or not 0 <= explicit < count:
+            raise Error(f"device must be a CUDA ordinal in [0, {count}).")
+        return explicit
+    env = os.environ.get("WGBLAS_CUDA_DEVICES")
+    if env:
+        ords = [int(x) for x in env.split(",") if x.strip()]
+        ords = [o for o in ords if 0 <= o < count] or [0]
+        return ords[-1] if power_preference == "low-power" else ords[0]
+    return count - 1 if power_preference == "low-power" else 0
+
+
+def init(powerPreference: str = "high-performance", benchmark: bool = False,
+         dumpShaders: bool = False, device: int | None = None) -> Device:
+    """Returns the cached device for this option set, creating it on first use
+    (src/init.mjs:31-107). ``benchmark=True`` makes GEMM calls return
+    ``gpuTimeMs``; ``dumpShaders`` has no CUDA counterpart and only warns."""
+    global _primary
+    options = {"powerPreference": powerPreference, "benchmark": bool(benchmark), "device": device}
+    key = _options_key(options)
+    cached = _devices.get(key)
+    if cached is not None:
+        return cached
+    if dumpShaders:
+        warnings.warn("dumpShaders has no effect on the CUDA backend (there are no WGSL shaders).")
+    ordinal = _ordinal_for(powerPreference, device)
+    h = nat.c_dev_p()
+    nat.check(nat.lib.wg_device_open(ordinal, nat.WG_DEVICE_TIMING if benchmark else 0, ct.byref(h)))
+    buf = ct.create_string_buffer(256)
+    nat.check(nat.lib.wg_device_name(h, buf, 256))
+    dev = Device(h, ordinal, bool(benchmark), options, buf.value.decode())
+    _devices[key] = dev
+    if _primary is None:
+        _primary = dev
+    return dev
+
+
+def cleanup(device: Device | None = None) -> None:
+    """Releases one device, or every device when called without one
+    (src/init.mjs:110-131). Unknown or released devices are a no-op."""
+    global _primary
+    if device is None:
+        for d in list(_devices.values()):
+            _close(d)
+        _devices.clear()
+        _primary = None
+        return
+    if not isinstance(device, Device) or device.destroyed:
+        return
+    key = next((k for k, v in _devices.items() if v is device), None)
+    if key is None:
+        return
+    del _devices[key]
+    _close(device)
+    if _primary is device:
+        _primary = next(iter(_devices.values()), None)
+
+
+def _close(d: Device) -> None:
+    if d._handle is not None:
+        nat.lib.wg_device_close(d._handle)
+        d._handle = None
+
+
+def gpuName(device: Device | None = None) -> dict:
+    """``{description, device}`` for a device (src/init.mjs:133-143)."""
+    device = _primary if device is None else device
+    if not isinstance(device, Device) or device.destroyed or device not in _devices.values():
+        raise Error("CUDA device not initialized — call init() first.")
+    return {"description": f"cuda:{device.ordinal}", "device": device._name or "unknown"}
+
+
+def getDevice() -> Device:
+    """The device from the first init() (src/init.mjs:163-168)."""
+    if _primary is None:
+        raise Error("CUDA device not initialized — call init() first.")
+    return _primary
+
+
+def isBenchmarkEnabled(device: Device | None = None) -> bool:
+    device = _primary if device is None else device
+    return bool(device is not None and not device.destroyed and device.benchmark)
+
+
+def require_gpu_device(device) -> None:
+    """requireGpuDevice (src/util/device.mjs:14-17)."""
+    if not isinstance(device, Device) or device.destroyed:
+        raise Error("device must be a GPUDevice.")
+
+
+def require_same_device(device: Device, routine: str, operands: dict) -> None:
+    """requireSameDevice (src/util/device.mjs:37-49)."""
+    from .classes import GpuMatrix, GpuVector
+
+    for name, value in operands.items():
+        if not isinstance(value, (GpuMatrix, GpuVector)):
+            continue
+        if value.device is not device:
+            raise Error(
+                f"{routine}: {name} belongs to a different GPUDevice than the one passed in. "
+                "GPU buffers cannot be shared across devices — recreate the operand on this "
+                "device, or call the routine with the device that owns it.")

@@ -1,0 +1,53 @@
+"""Builds libwgblas_b200.so (the C ABI of include/wgblas.h) in-tree with nvcc for sm_100a.
+
+Usage: python wgblas_b200/build.py [--force] [-v]   (runs without importing the package)
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+ROOT = os.path.dirname(HERE)
+LIB = os.path.join(HERE, "libwgblas_b200.so")
+BUILD_DIR = os.path.join(HERE, "_build")
+
+SOURCES = ["runtime.cu", "gemm.cu", "gemm_simt.cu", "sgemm_tf32x3.cu", "probe.cu"]
+HEADERS = ["internal.h", "tcgen05.cuh"]
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
+         "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
+
+
+def _stale(target: str, deps) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.exists(d) and os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "wgblas.h")]
+    objs = []
+    for src in SOURCES:
+        path = os.path.join(CSRC, src)
+        obj = os.path.join(BUILD_DIR, src.replace(".cu", ".o"))
+        objs.append(obj)
+        if force or _stale(obj, [path] + headers):
+            cmd = [NVCC, *ARCH, *FLAGS, "-c", path, "-o", obj]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            subprocess.run(cmd, check=True)
+    if force or _stale(LIB, objs):
+        subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB, *objs], check=True)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(LIB)

@@ -1,0 +1,297 @@
+// sgemm / dgemm entry points of the C ABI: argument checks, kernel choice,
+// event timing and the host-array path.
+//
+// Replaces the dispatch half of src/sgemm/sgemm.mjs:25-269 and
+// src/dgemm/dgemm.mjs:23-318 (tile selection, upload, one compute pass,
+// readback). Argument-shape errors that the JavaScript layer reports with its
+// own messages (src/sgemm/sgemm.mjs:46-149) are re-checked here in the
+// column-major frame so that a C caller gets WG_ERR_INVALID_ARGUMENT instead of
+// an out-of-bounds access.
+#include <cstring>
+
+#include "internal.h"
+
+namespace {
+
+// Rows and columns of the stored matrix behind op(X) (column-major frame).
+struct Stored {
+  int64_t rows, cols;
+};
+
+bool fits(int64_t off, int64_t ld, Stored s, size_t elems) {
+  if (s.rows == 0 || s.cols == 0) return off >= 0 && (unsigned __int128)off <= elems;
+  __int128 last = (__int128)off + (__int128)(s.cols - 1) * ld + s.rows;
+  return off >= 0 && last <= (__int128)elems;
+}
+
+wg_status check_dims(int transA, int transB, int64_t m, int64_t n, int64_t k, int64_t lda,
+                     int64_t ldb, int64_t ldc) {
+  if ((transA != 0 && transA != 1) || (transB != 0 && transB != 1))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "transA and transB must be 0 (no-transpose) or 1 (transpose)");
+  if (m < 0 || n < 0 || k < 0) return wg_fail(WG_ERR_INVALID_ARGUMENT, "m, n, and k must be non-negative.");
+  if (lda <= 0 || ldb <= 0 || ldc <= 0)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "lda, ldb, and ldc must be positive.");
+  const int64_t lim = (int64_t)1 << 31;
+  if (m >= lim || n >= lim || k >= lim || lda >= ((int64_t)1 << 40) || ldb >= ((int64_t)1 << 40) ||
+      ldc >= ((int64_t)1 << 40))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "dimensions must be below 2^31 and leading dimensions below 2^40");
+  if (lda < (transA ? k : m))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "lda must be >= rows of A as stored.");
+  if (ldb < (transB ? n : k))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "ldb must be >= rows of B as stored.");
+  if (ldc < m) return wg_fail(WG_ERR_INVALID_ARGUMENT, "ldc must be >= rows of C as stored.");
+  return WG_OK;
+}
+
+Stored stored_a(int transA, int64_t m, int64_t k) { return transA ? Stored{k, m} : Stored{m, k}; }
+Stored stored_b(int transB, int64_t n, int64_t k) { return transB ? Stored{n, k} : Stored{k, n}; }
+
+// Whether the device can run the sm_100a kernels in this library at all.
+wg_status check_arch(const wg_device *d) {
+  if (d->cc_major != 10)
+    return wg_fail(WG_ERR_NOT_SUPPORTED,
+                   "device %d (%s, sm_%d%d) is not a Blackwell sm_100 device; this library is built "
+                   "for sm_100a only", d->ordinal, d->name, d->cc_major, d->cc_minor);
+  return WG_OK;
+}
+
+template <typename T>
+wg_status gemm_launch(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                      const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+
+// sgemm kernel choice. The 3xTF32 tensor-core kernel needs enough k to amortise
+// its split pass and gives no benefit on tiny grids; everything else, and any
+// call whose operands fail the split's range check on the device, runs the
+// FFMA kernel.
+template <>
+wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                             float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                             float beta, float *C, int64_t ldc) {
+  cudaStream_t s = d->stream;
+  if (alpha == 0.0f || k == 0) {
+    wg_launch_scope scope(d, "scale");
+    WG_CUDA(wg_launch_scale<float>(s, m, n, alpha, beta, C, ldc));
+    return WG_OK;
+  }
+  d->stats.calls++;
+  bool tc = false;
+  if (d->sgemm_path == WG_SGEMM_TF32X3) {
+    if (!wg_tf32x3_supported(d, m, n, k))
+      return wg_fail(WG_ERR_NOT_SUPPORTED, "the 3xTF32 kernel does not support m=%lld n=%lld k=%lld",
+                     (long long)m, (long long)n, (long long)k);
+    tc = true;
+  } else if (d->sgemm_path == WG_SGEMM_AUTO) {
+    tc = wg_tf32x3_supported(d, m, n, k) && k >= 64 && (double)m * (double)n >= 256.0 * 256.0;
+  }
+  if (tc) {
+    void *ws = nullptr;
+    wg_status st = wg_workspace(d, wg_tf32x3_workspace_bytes(m, n, k), &ws);
+    if (st != WG_OK) return st;
+    st = wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws);
+    if (st != WG_OK) return st;
+    d->stats.tf32x3_launches++;
+    return WG_OK;
+  }
+  d->stats.simt_launches++;
+  wg_launch_scope scope(d, "sgemm_simt");
+  WG_CUDA(wg_launch_gemm_simt<float>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
+                                     d->dwords, 0u));
+  return WG_OK;
+}
+
+template <>
+wg_status gemm_launch<double>(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                              double alpha, const double *A, int64_t lda, const double *B,
+                              int64_t ldb, double beta, double *C, int64_t ldc) {
+  cudaStream_t s = d->stream;
+  if (alpha == 0.0 || k == 0) {
+    wg_launch_scope scope(d, "scale");
+    WG_CUDA(wg_launch_scale<double>(s, m, n, alpha, beta, C, ldc));
+    return WG_OK;
+  }
+  wg_launch_scope scope(d, "dgemm_simt");
+  WG_CUDA(wg_launch_gemm_simt<double>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C,
+                                      ldc, d->dwords, 0u));
+  return WG_OK;
+}
+
+// dgemm's quick return (src/dgemm/dgemm.mjs:177-179); sgemm has none.
+template <typename T>
+bool quick_return(int64_t k, T alpha, T beta);
+template <>
+bool quick_return<float>(int64_t, float, float) { return false; }
+template <>
+bool quick_return<double>(int64_t k, double alpha, double beta) {
+  return (alpha == 0.0 || k == 0) && beta == 1.0;
+}
+
+template <typename T>
+wg_status gemm_timed(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                     const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
+                     float *gpu_ms) {
+  const bool timing = gpu_ms && (d->flags & WG_DEVICE_TIMING);
+  if (timing) WG_CUDA(cudaEventRecord(d->ev_start, d->stream));
+  wg_status st = gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+  if (st != WG_OK) return st;
+  if (timing) {
+    WG_CUDA(cudaEventRecord(d->ev_stop, d->stream));
+    WG_CUDA(cudaEventSynchronize(d->ev_stop));
+    WG_CUDA(cudaEventElapsedTime(gpu_ms, d->ev_start, d->ev_stop));
+  }
+  return WG_OK;
+}
+
+template <typename T>
+wg_status gemm_buffers(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                       const wg_buffer *A, int64_t offA, int64_t lda, const wg_buffer *B, int64_t offB,
+                       int64_t ldb, T beta, wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms) {
+  if (gpu_ms) *gpu_ms = 0.0f;
+  if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  wg_status st = check_dims(transA, transB, m, n, k, lda, ldb, ldc);
+  if (st != WG_OK) return st;
+  if (m == 0 || n == 0) return WG_OK;  // src/sgemm/sgemm.mjs:83
+  if (quick_return<T>(k, alpha, beta)) return WG_OK;
+  if (!A || !B || !C) return wg_fail(WG_ERR_INVALID_ARGUMENT, "A, B and C must be buffers");
+  for (const wg_buffer *b : {A, B, (const wg_buffer *)C})
+    if (b->dev->ordinal != d->ordinal)
+      return wg_fail(WG_ERR_INVALID_ARGUMENT,
+                     "a buffer belongs to device %d, not to device %d that the call runs on",
+                     b->dev->ordinal, d->ordinal);
+  const bool reads_ab = k > 0 && alpha != T(0);
+  if (reads_ab && !fits(offA, lda, stored_a(transA, m, k), A->bytes / sizeof(T)))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "A does not have enough elements for the given dimensions and lda.");
+  if (reads_ab && !fits(offB, ldb, stored_b(transB, n, k), B->bytes / sizeof(T)))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "B does not have enough elements for the given dimensions and ldb.");
+  if (!fits(offC, ldc, Stored{m, n}, C->bytes / sizeof(T)))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "C does not have enough elements for the given dimensions and ldc.");
+  st = check_arch(d);
+  if (st != WG_OK) return st;
+  wg_device_guard guard(d->ordinal);
+  return gemm_timed<T>(d, transA, transB, m, n, k, alpha, (const T *)A->ptr + offA, lda,
+                       (const T *)B->ptr + offB, ldb, beta, (T *)C->ptr + offC, ldc, gpu_ms);
+}
+
+template <typename T>
+wg_status gemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                   const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc) {
+  if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  wg_status st = check_dims(transA, transB, m, n, k, lda, ldb, ldc);
+  if (st != WG_OK) return st;
+  if (m == 0 || n == 0 || quick_return<T>(k, alpha, beta)) return WG_OK;
+  if ((k > 0 && alpha != T(0) && (!A || !B)) || !C)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "operand pointer is NULL");
+  st = check_arch(d);
+  if (st != WG_OK) return st;
+  wg_device_guard guard(d->ordinal);
+  return gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+// Copies the rows x cols block of a column-major host matrix (leading dimension
+// ld) into a dense device matrix, or back.
+template <typename T>
+cudaError_t h2d_block(T *dst, const T *src, int64_t ld, Stored s, cudaStream_t st) {
+  if (s.rows == 0 || s.cols == 0) return cudaSuccess;
+  return cudaMemcpy2DAsync(dst, s.rows * sizeof(T), src, ld * sizeof(T), s.rows * sizeof(T), s.cols,
+                           cudaMemcpyHostToDevice, st);
+}
+
+template <typename T>
+wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                    const T *A, int64_t lda, const T *B, int64_t ldb, T beta, const T *C_in, T *C_out,
+                    int64_t ldc, float *gpu_ms) {
+  if (gpu_ms) *gpu_ms = 0.0f;
+  if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  wg_status st = check_dims(transA, transB, m, n, k, lda, ldb, ldc);
+  if (st != WG_OK) return st;
+  if (!C_out) return wg_fail(WG_ERR_INVALID_ARGUMENT, "C_out is NULL");
+  if (m == 0 || n == 0) return WG_OK;
+  const bool reads_ab = k > 0 && alpha != T(0);
+  const bool reads_c = beta != T(0);
+  if ((reads_ab && (!A || !B)) || (reads_c && !C_in))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "operand pointer is NULL");
+  if (quick_return<T>(k, alpha, beta)) {
+    // C is returned as it came in (src/dgemm/dgemm.mjs:179).
+    if (C_out != C_in)
+      for (int64_t j = 0; j < n; j++) memcpy(C_out + j * ldc, C_in + j * ldc, m * sizeof(T));
+    return WG_OK;
+  }
+  st = check_arch(d);
+  if (st != WG_OK) return st;
+  wg_device_guard guard(d->ordinal);
+  cudaStream_t s = d->stream;
+  const Stored sa = stored_a(transA, m, k), sb = stored_b(transB, n, k);
+  const size_t na = reads_ab ? (size_t)(sa.rows * sa.cols) : 0;
+  const size_t nb = reads_ab ? (size_t)(sb.rows * sb.cols) : 0;
+  const size_t nc = (size_t)(m * n);
+  T *dA = nullptr, *dB = nullptr, *dC = nullptr;
+  // Stream-ordered temporaries from the device's memory pool, released in
+  // stream order like the reference's `finally` (src/sgemm/sgemm.mjs:263-268).
+  cudaError_t e = cudaMallocAsync((void **)&dC, nc * sizeof(T), s);
+  if (e == cudaSuccess && na) e = cudaMallocAsync((void **)&dA, na * sizeof(T), s);
+  if (e == cudaSuccess && nb) e = cudaMallocAsync((void **)&dB, nb * sizeof(T), s);
+  if (e == cudaSuccess && na) e = h2d_block(dA, A, lda, sa, s);
+  if (e == cudaSuccess && nb) e = h2d_block(dB, B, ldb, sb, s);
+  if (e == cudaSuccess && reads_c) e = h2d_block(dC, C_in, ldc, Stored{m, n}, s);
+  if (e == cudaSuccess) {
+    st = gemm_timed<T>(d, transA, transB, m, n, k, alpha, dA, sa.rows > 0 ? sa.rows : 1, dB,
+                       sb.rows > 0 ? sb.rows : 1, beta, dC, m, gpu_ms);
+    if (st == WG_OK)
+      e = cudaMemcpy2DAsync(C_out, ldc * sizeof(T), dC, m * sizeof(T), m * sizeof(T), n,
+                            cudaMemcpyDeviceToHost, s);
+  }
+  if (dA) cudaFreeAsync(dA, s);
+  if (dB) cudaFreeAsync(dB, s);
+  if (dC) cudaFreeAsync(dC, s);
+  cudaError_t e2 = cudaStreamSynchronize(s);
+  if (st != WG_OK) return st;
+  if (e == cudaSuccess) e = e2;
+  if (e != cudaSuccess)
+    return wg_fail(e == cudaErrorMemoryAllocation ? WG_ERR_OUT_OF_MEMORY : WG_ERR_CUDA,
+                   "host-array GEMM failed: %s", cudaGetErrorString(e));
+  return WG_OK;
+}
+
+}  // namespace
+
+extern "C" wg_status wg_sgemm(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                              float alpha, const wg_buffer *A, int64_t offA, int64_t lda,
+                              const wg_buffer *B, int64_t offB, int64_t ldb, float beta, wg_buffer *C,
+                              int64_t offC, int64_t ldc, float *gpu_ms) {
+  return gemm_buffers<float>(d, transA, transB, m, n, k, alpha, A, offA, lda, B, offB, ldb, beta, C,
+                             offC, ldc, gpu_ms);
+}
+
+extern "C" wg_status wg_dgemm(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                              double alpha, const wg_buffer *A, int64_t offA, int64_t lda,
+                              const wg_buffer *B, int64_t offB, int64_t ldb, double beta, wg_buffer *C,
+                              int64_t offC, int64_t ldc, float *gpu_ms) {
+  return gemm_buffers<double>(d, transA, transB, m, n, k, alpha, A, offA, lda, B, offB, ldb, beta, C,
+                              offC, ldc, gpu_ms);
+}
+
+extern "C" wg_status wg_sgemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                  float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                                  float beta, float *C, int64_t ldc) {
+  return gemm_dev<float>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+extern "C" wg_status wg_dgemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                  double alpha, const double *A, int64_t lda, const double *B,
+                                  int64_t ldb, double beta, double *C, int64_t ldc) {
+  return gemm_dev<double>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+extern "C" wg_status wg_sgemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                   float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                                   float beta, const float *C_in, float *C_out, int64_t ldc,
+                                   float *gpu_ms) {
+  return gemm_host<float>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C_in, C_out, ldc, gpu_ms);
+}
+
+extern "C" wg_status wg_dgemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                   double alpha, const double *A, int64_t lda, const double *B,
+                                   int64_t ldb, double beta, const double *C_in, double *C_out,
+                                   int64_t ldc, float *gpu_ms) {
+  return gemm_host<double>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C_in, C_out, ldc,
+                           gpu_ms);
+}

@@ -1,0 +1,121 @@
+// Internal declarations shared by the wgblas-b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/wgblas.h"
+
+// Device-side status words, one small array per device handle.
+enum {
+  WG_DW_ERROR = 0,     // bitmask of WG_DERR_* set by kernels whose bounded waits gave up
+  WG_DW_FALLBACK = 1,  // epoch of the latest sgemm call whose operands ruled out 3xTF32
+  WG_DW_FALLBACKS = 2, // number of FFMA fallbacks run because of WG_DW_FALLBACK
+  WG_DW_COUNT = 8
+};
+// Bits of WG_DW_ERROR.
+enum {
+  WG_DERR_TMA_WAIT = 1u,  // producer or consumer gave up waiting on a pipeline stage
+  WG_DERR_MMA_WAIT = 2u,  // the epilogue gave up waiting for the accumulator
+  WG_DERR_TMEM = 4u       // TMEM allocation returned an unusable address
+};
+
+struct wg_device {
+  int ordinal;
+  unsigned flags;
+  cudaStream_t own_stream;
+  cudaStream_t stream;  // the stream work is ordered on (own_stream or the caller's)
+  cudaEvent_t ev_start, ev_stop;
+  int sm_count;
+  int cc_major, cc_minor;
+  size_t total_mem;
+  char name[256];
+  void *ws;          // grow-only scratch for the 3xTF32 operand split
+  size_t ws_bytes;
+  unsigned *dwords;  // WG_DW_COUNT device words
+  uint32_t epoch;    // sgemm call counter, tags WG_DW_FALLBACK
+  int sgemm_path;
+  wg_sgemm_stats stats;
+  uint64_t launches;  // kernels launched on this handle
+  // profiling: event pairs waiting to be summed, and per-family totals
+  bool profiling;
+  struct pending_t { int family; cudaEvent_t e0, e1; };
+  std::vector<pending_t> pending;
+  std::vector<cudaEvent_t> event_pool;
+  std::vector<std::string> families;
+  std::vector<uint64_t> fam_launches;
+  std::vector<double> fam_ms;
+};
+
+// Brackets one kernel launch for per-kernel profiling and counts it.
+struct wg_launch_scope {
+  wg_device *d;
+  int slot;
+  wg_launch_scope(wg_device *dev, const char *family);
+  ~wg_launch_scope();
+};
+
+struct wg_buffer {
+  wg_device *dev;
+  void *ptr;
+  size_t bytes;
+};
+
+// Records a message for wg_last_error() on this thread and returns `st`.
+wg_status wg_fail(wg_status st, const char *fmt, ...);
+
+#define WG_CUDA(call)                                                                   \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return wg_fail(e_ == cudaErrorMemoryAllocation ? WG_ERR_OUT_OF_MEMORY : WG_ERR_CUDA, \
+                     "%s failed: %s", #call, cudaGetErrorString(e_));                   \
+  } while (0)
+
+// Makes `ordinal` current for the lifetime of the guard.
+struct wg_device_guard {
+  int prev;
+  bool changed;
+  explicit wg_device_guard(int ordinal) : prev(-1), changed(false) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != ordinal) {
+      cudaSetDevice(ordinal);
+      changed = true;
+    }
+  }
+  ~wg_device_guard() {
+    if (changed) cudaSetDevice(prev);
+  }
+};
+
+// Returns at least `bytes` of device scratch owned by the handle (stream-ordered reuse).
+wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);
+
+// ---- kernel launchers (gemm_simt.cu, sgemm_tf32x3.cu) ----
+
+// C = alpha*op(A)op(B) + beta*C on the FFMA / DFMA pipes, sequential k per element.
+// When only_if_epoch != 0 every CTA first reads dwords[WG_DW_FALLBACK] and exits
+// unless it equals only_if_epoch (the device-side fallback of the 3xTF32 path).
+template <typename T>
+cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t m, int64_t n,
+                                int64_t k, T alpha, const T *A, int64_t lda, const T *B,
+                                int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
+                                uint32_t only_if_epoch);
+
+// C = (alpha == 0 ? 0 : alpha*0) + beta*C elementwise — the k == 0 / alpha == 0 cases.
+template <typename T>
+cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T beta, T *C,
+                            int64_t ldc);
+
+// Bytes of scratch the 3xTF32 path needs for this shape.
+size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
+// True when the 3xTF32 path supports this shape on this device.
+bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
+// Splits op(A), op(B) into tf32 hi/lo operands in `ws`, then runs the tcgen05 kernel.
+// Operands outside the split's exact range make the kernel exit and the FFMA
+// kernel (launched right after, gated on the same epoch) compute C instead.
+wg_status wg_sgemm_tf32x3(wg_device *dev, int transA, int transB, int64_t m, int64_t n,
+                          int64_t k, float alpha, const float *A, int64_t lda, const float *B,
+                          int64_t ldb, float beta, float *C, int64_t ldc, void *ws);

@@ -1,0 +1,108 @@
+// Roofline probes: FP32 FFMA and FP64 DFMA peak rate and HBM copy bandwidth,
+// measured with CUDA events on the device handle's stream.
+//
+// The FMA probes follow the idea of the reference's benchmarks/roofline/wgblas/fma.js:1-72
+// (independent multiply-add chains per thread, enough threads to fill every
+// SM, a long loop so the issue rate is all that is measured); the copy probe
+// streams a buffer much larger than L2 through 16-byte loads and stores.
+#include "internal.h"
+
+namespace {
+
+constexpr int CHAINS = 8;
+
+__device__ __forceinline__ float fma_t(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_t(double a, double b, double c) { return __fma_rn(a, b, c); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) fma_probe_kernel(T x, T y, int iters, T *sink) {
+  T a[CHAINS];
+#pragma unroll
+  for (int c = 0; c < CHAINS; c++) a[c] = T(threadIdx.x + c) * T(1e-3);
+  for (int i = 0; i < iters; i++) {
+#pragma unroll
+    for (int c = 0; c < CHAINS; c++) a[c] = fma_t(a[c], x, y);
+  }
+  T s = T(0);
+#pragma unroll
+  for (int c = 0; c < CHAINS; c++) s += a[c];
+  if (s == T(-12345.678)) sink[threadIdx.x] = s;  // never true; keeps the chains live
+}
+
+__global__ void copy_probe_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+template <typename T>
+wg_status fma_probe(wg_device *d, double *tflops) {
+  const int blocks = d->sm_count * 8, threads = 256, iters = 1 << 14;
+  T *sink = nullptr;
+  WG_CUDA(cudaMallocAsync((void **)&sink, threads * sizeof(T), d->stream));
+  cudaEvent_t e0, e1;
+  WG_CUDA(cudaEventCreate(&e0));
+  WG_CUDA(cudaEventCreate(&e1));
+  float best = 1e30f;
+  for (int rep = 0; rep < 4; rep++) {
+    cudaEventRecord(e0, d->stream);
+    fma_probe_kernel<T><<<blocks, threads, 0, d->stream>>>(T(0.999999), T(1e-7), iters, sink);
+    cudaEventRecord(e1, d->stream);
+    WG_CUDA(cudaEventSynchronize(e1));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (rep > 0 && ms < best) best = ms;  // the first launch warms clocks and caches
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFreeAsync(sink, d->stream);
+  WG_CUDA(cudaStreamSynchronize(d->stream));
+  const double flops = 2.0 * CHAINS * (double)iters * blocks * threads;
+  *tflops = flops / (best * 1e-3) / 1e12;
+  return WG_OK;
+}
+
+wg_status copy_probe(wg_device *d, double *gbs) {
+  const size_t bytes = (size_t)1 << 31;  // 2 GiB each way, far above the 126 MB L2
+  const size_t n = bytes / sizeof(float4);
+  float4 *src = nullptr, *dst = nullptr;
+  WG_CUDA(cudaMallocAsync((void **)&src, bytes, d->stream));
+  cudaError_t e = cudaMallocAsync((void **)&dst, bytes, d->stream);
+  if (e != cudaSuccess) {
+    cudaFreeAsync(src, d->stream);
+    return wg_fail(WG_ERR_OUT_OF_MEMORY, "copy probe allocation failed: %s", cudaGetErrorString(e));
+  }
+  WG_CUDA(cudaMemsetAsync(src, 0, bytes, d->stream));
+  cudaEvent_t e0, e1;
+  WG_CUDA(cudaEventCreate(&e0));
+  WG_CUDA(cudaEventCreate(&e1));
+  float best = 1e30f;
+  for (int rep = 0; rep < 4; rep++) {
+    cudaEventRecord(e0, d->stream);
+    copy_probe_kernel<<<d->sm_count * 16, 512, 0, d->stream>>>(src, dst, n);
+    cudaEventRecord(e1, d->stream);
+    WG_CUDA(cudaEventSynchronize(e1));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (rep > 0 && ms < best) best = ms;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFreeAsync(src, d->stream);
+  cudaFreeAsync(dst, d->stream);
+  WG_CUDA(cudaStreamSynchronize(d->stream));
+  *gbs = 2.0 * (double)bytes / (best * 1e-3) / 1e9;
+  return WG_OK;
+}
+
+}  // namespace
+
+extern "C" wg_status wg_probe_peak(wg_device *d, int kind, double *value) {
+  if (!d || !value) return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
+  wg_device_guard guard(d->ordinal);
+  switch (kind) {
+    case WG_PROBE_FP32_FMA: return fma_probe<float>(d, value);
+    case WG_PROBE_FP64_FMA: return fma_probe<double>(d, value);
+    case WG_PROBE_HBM_COPY: return copy_probe(d, value);
+    default: return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown probe %d", kind);
+  }
+}
