@@ -1,9 +1,375 @@
-// 3xTF32 tensor-core sgemm (tcgen05 + TMEM + TMA) — placeholder until the kernel lands.
-#include "internal.h"
+// 3xTF32 sgemm on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Every fp32 operand x is split into two TF32 values, hi = rna_tf32(x) and
+// lo = rna_tf32(x - hi) (x - hi is exact), and the product is taken as
+//   A*B ~= A_hi*B_hi + A_hi*B_lo + A_lo*B_hi
+// with fp32 accumulation in TMEM: the representation error is ~3*2^-22 of each
+// |a||b| and the dropped lo*lo term ~2^-22, inside the north-star bound
+// 2*K*2^-24*(|A||B| + |C|) for K >= 6 (the dispatcher uses it for K >= 64).
+// The alpha/beta epilogue is the reference's (src/shaders/sgemm_large.wgsl:299-304)
+// in fp32 with the beta term fused.
+//
+// Two launches per call:
+//  1. tf32x3_pack: reads op(A) and op(B) in any transpose / leading dimension,
+//     writes K-major, zero-padded hi and lo operands to the scratch workspace,
+//     and flags (dwords[WG_DW_FALLBACK] = epoch) any element that is not finite
+//     or whose magnitude lies outside [2^-50, 2^50] — there the split loses its
+//     accuracy (subnormal lo parts) or IEEE semantics (Inf*0 in a cross term).
+//  2. tf32x3_mma: one 128 x BN tile of C per CTA; warp 0 streams the four
+//     operand tiles of each k-block into a STAGES-deep shared-memory ring with
+//     TMA (no multicast), warp 1 issues three tcgen05.mma.kind::tf32 per 8-wide
+//     k step into a TMEM accumulator, warps 2-5 read TMEM with tcgen05.ld and
+//     store C column by column (32 rows = 128 contiguous bytes per warp store).
+//     If the flag carries this call's epoch the kernel exits at once, and the
+//     FFMA kernel launched after it (gated on the same epoch) computes C.
+#include <cuda.h>
 
-size_t wg_tf32x3_workspace_bytes(int64_t, int64_t, int64_t) { return 0; }
-bool wg_tf32x3_supported(const wg_device *, int64_t, int64_t, int64_t) { return false; }
-wg_status wg_sgemm_tf32x3(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *, int64_t,
-                          const float *, int64_t, float, float *, int64_t, void *) {
-  return wg_fail(WG_ERR_NOT_SUPPORTED, "3xTF32 kernel not built");
+#include "internal.h"
+#include "tcgen05.cuh"
+
+namespace {
+
+constexpr int BM = 128;              // UMMA M (cta_group::1), TMEM lanes
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr long long WAIT_BUDGET = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
+
+// Kernel shape: BN columns of C per CTA, BK floats of K per pipeline stage
+// (BK * 4 bytes = the swizzle span: 128 -> SWIZZLE_128B, 64 -> SWIZZLE_64B).
+template <int BN_, int BK_, int STAGES_>
+struct Shape {
+  static constexpr int BN = BN_, BK = BK_, STAGES = STAGES_;
+  static constexpr int ROW_BYTES = BK * 4;
+  static constexpr int A_TILE = BM * BK * 4;  // bytes of one A operand tile
+  static constexpr int B_TILE = BN * BK * 4;
+  static constexpr int STAGE = 2 * A_TILE + 2 * B_TILE;  // A_hi, A_lo, B_hi, B_lo
+  static constexpr int TMEM_COLS = BN;  // fp32 accumulator: 128 lanes x BN columns
+  static constexpr size_t SMEM = 1024 /*alignment slack*/ + (size_t)STAGES * STAGE + 256 /*barriers*/;
+  static_assert(A_TILE % 1024 == 0 && B_TILE % 1024 == 0, "tiles must keep 1024-byte alignment");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128 is a multiple of 16 up to 256");
+  static_assert(ROW_BYTES == 64 || ROW_BYTES == 128, "swizzle span");
+};
+
+using Sh = Shape<256, 16, 4>;  // 48 KB stages, four deep
+
+// Round to nearest TF32 (10 explicit mantissa bits), ties away from zero, on
+// the bit pattern of a finite float: add half of the dropped 13-bit field and
+// truncate. Magnitudes here stay far below the overflow boundary.
+__device__ __forceinline__ float rna_tf32(float x) {
+  uint32_t u = __float_as_uint(x);
+  return __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
+}
+
+// An operand the split represents to ~2^-22 relative accuracy with normal
+// lo parts: zero, or a finite value with 2^-50 <= |x| <= 2^50.
+__device__ __forceinline__ bool split_ok(float x) {
+  const float ax = fabsf(x);
+  return x == 0.0f || (ax >= 0x1p-50f && ax <= 0x1p50f);
+}
+
+struct PackArgs {
+  const float *src;
+  int64_t ld;
+  int kcontig;    // 1: element (r, p) at src[r*ld + p]; 0: at src[r + p*ld]
+  int64_t rows;   // real rows (m for A, n for B)
+  int64_t rows_p; // padded rows
+  float *hi, *lo; // rows_p x kp, row-major (K contiguous)
+  int64_t tiles_r;
+};
+
+// One 32 x 32 (rows x k) tile per 256-thread block; blocks [0, tilesA) pack A,
+// the rest pack B. Writes are 128-byte rows of K; reads are coalesced along
+// whichever dimension the source stores contiguously (through shared memory
+// when that is the row dimension).
+__global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64_t k, int64_t kp,
+                                                   int64_t tiles_a, unsigned *dwords, uint32_t epoch) {
+  __shared__ float tile[32][33];
+  const bool is_a = blockIdx.x < tiles_a;
+  const PackArgs &P = is_a ? a : b;
+  const int64_t t = is_a ? blockIdx.x : blockIdx.x - tiles_a;
+  const int64_t tiles_k = kp / 32;
+  const int64_t r0 = (t / tiles_k) * 32, p0 = (t % tiles_k) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // ty in [0, 8)
+  bool bad = false;
+  float v[4];
+  if (P.kcontig) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int64_t r = r0 + ty + 8 * i, p = p0 + tx;
+      v[i] = (r < P.rows && p < k) ? P.src[r * P.ld + p] : 0.0f;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int64_t p = p0 + ty + 8 * i, r = r0 + tx;
+      tile[ty + 8 * i][tx] = (r < P.rows && p < k) ? P.src[r + p * P.ld] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = tile[tx][ty + 8 * i];
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t r = r0 + ty + 8 * i, p = p0 + tx;
+    const float x = v[i];
+    bad |= !split_ok(x);
+    const float h = rna_tf32(x);
+    const float l = rna_tf32(x - h);
+    P.hi[r * kp + p] = h;
+    P.lo[r * kp + p] = l;
+  }
+  if (__any_sync(0xffffffffu, bad) && tx == 0) *(volatile unsigned *)(dwords + WG_DW_FALLBACK) = epoch;
+}
+
+struct MmaArgs {
+  int64_t m, n, k;
+  float alpha, beta;
+  float *C;
+  int64_t ldc;
+  unsigned *dwords;
+  uint32_t epoch;
+};
+
+template <class S>
+__global__ void __launch_bounds__(THREADS, 1)
+tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+           const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+           const MmaArgs args) {
+  // Operands ruled out by the pack pass: the FFMA kernel queued next computes C.
+  if (*(volatile unsigned *)(args.dwords + WG_DW_FALLBACK) == args.epoch) return;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = wgtc::smem_addr(smem_raw);
+  uint8_t *smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned ring
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S::STAGES * S::STAGE);
+  uint64_t *empty = full + S::STAGES;
+  uint64_t *accum = empty + S::STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * S::BN;
+  const int nk = (int)((args.k + S::BK - 1) / S::BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; s++) {
+      wgtc::mbar_init(&full[s], 1);
+      wgtc::mbar_init(&empty[s], 1);
+    }
+    wgtc::mbar_init(accum, 1);
+    *abort_flag = 0;
+    wgtc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    wgtc::prefetch_tensormap(&map_ahi);
+    wgtc::prefetch_tensormap(&map_alo);
+    wgtc::prefetch_tensormap(&map_bhi);
+    wgtc::prefetch_tensormap(&map_blo);
+  }
+  if (warp == 1) {
+    wgtc::tmem_alloc(tmem_slot, S::TMEM_COLS);
+    wgtc::tmem_relinquish();
+  }
+  wgtc::tc_fence_before();
+  __syncthreads();
+  wgtc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    int issued = 0;
+    for (int kb = 0; kb < nk; kb++) {
+      const int s = kb % S::STAGES;
+      const uint32_t ph = (uint32_t)(kb / S::STAGES) & 1u;
+      if (!wgtc::mbar_wait_bounded(&empty[s], ph ^ 1u, WAIT_BUDGET) || *abort_flag) {
+        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t *st = smem + (size_t)s * S::STAGE;
+      wgtc::mbar_arrive_expect_tx(&full[s], S::STAGE);
+      const int kc = kb * S::BK;
+      wgtc::tma_load_2d(st, &map_ahi, &full[s], kc, (int)m0);
+      wgtc::tma_load_2d(st + S::A_TILE, &map_alo, &full[s], kc, (int)m0);
+      wgtc::tma_load_2d(st + 2 * S::A_TILE, &map_bhi, &full[s], kc, (int)n0);
+      wgtc::tma_load_2d(st + 2 * S::A_TILE + S::B_TILE, &map_blo, &full[s], kc, (int)n0);
+      issued = kb + 1;
+    }
+    // Let every copy this thread issued land before the CTA can exit.
+    for (int kb = issued - S::STAGES > 0 ? issued - S::STAGES : 0; kb < issued; kb++)
+      wgtc::mbar_wait_bounded(&full[kb % S::STAGES], (uint32_t)(kb / S::STAGES) & 1u, WAIT_BUDGET);
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = wgtc::idesc_tf32(BM, S::BN);
+    bool ok = true;
+    for (int kb = 0; kb < nk && ok; kb++) {
+      const int s = kb % S::STAGES;
+      const uint32_t ph = (uint32_t)(kb / S::STAGES) & 1u;
+      if (!wgtc::mbar_wait_bounded(&full[s], ph, WAIT_BUDGET) || *abort_flag) {
+        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      wgtc::tc_fence_after();
+      const uint32_t st = wgtc::smem_addr(smem + (size_t)s * S::STAGE);
+      const uint32_t a_hi = st, a_lo = st + S::A_TILE, b_hi = st + 2 * S::A_TILE,
+                     b_lo = st + 2 * S::A_TILE + S::B_TILE;
+#pragma unroll
+      for (int kk = 0; kk < S::BK / 8; kk++) {
+        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle span
+        const uint64_t dah = wgtc::smem_desc_kmajor(a_hi + off, S::ROW_BYTES);
+        const uint64_t dal = wgtc::smem_desc_kmajor(a_lo + off, S::ROW_BYTES);
+        const uint64_t dbh = wgtc::smem_desc_kmajor(b_hi + off, S::ROW_BYTES);
+        const uint64_t dbl = wgtc::smem_desc_kmajor(b_lo + off, S::ROW_BYTES);
+        const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+        wgtc::mma_tf32(tmem, dal, dbh, idesc, acc0);  // small terms first
+        wgtc::mma_tf32(tmem, dah, dbl, idesc, 1u);
+        wgtc::mma_tf32(tmem, dah, dbh, idesc, 1u);
+      }
+      wgtc::mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+    }
+    wgtc::mma_commit(accum);  // accumulator complete (or abandoned) once all MMAs finish
+  } else if (warp >= 2) {
+    // ---- epilogue: TMEM -> registers -> C ----
+    // tcgen05.ld is warp-collective: decide per warp, not per thread.
+    const bool ready = __all_sync(0xffffffffu, wgtc::mbar_wait_bounded(accum, 0, WAIT_BUDGET));
+    if (!ready && lane == 0) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+    wgtc::tc_fence_after();
+    const bool aborted = __any_sync(0xffffffffu, *abort_flag != 0);
+    if (ready && !aborted) {
+      const int q = warp & 3;  // TMEM lane quarter this warp may access
+      const int64_t row = m0 + q * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+      const float alpha = args.alpha, beta = args.beta;
+      for (int c = 0; c < S::BN; c += 32) {
+        uint32_t r[32];
+        wgtc::tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
+        wgtc::tmem_ld_wait();
+        if (row < args.m) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const int64_t col = n0 + c + j;
+            if (col < args.n) {
+              float *cp = args.C + row + col * args.ldc;
+              const float acc = __uint_as_float(r[j]);
+              const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc);
+              *cp = (beta != 0.0f) ? __fmaf_rn(beta, *cp, s) : s;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  wgtc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    wgtc::tc_fence_after();
+    wgtc::tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+// ---- host side ------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// Tensor map of a rows x kp row-major fp32 operand, boxes of box_rows x BK.
+bool make_map(CUtensorMap *map, float *ptr, int64_t rows, int64_t kp, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kp * sizeof(float)};
+  cuuint32_t box[2] = {(cuuint32_t)Sh::BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = Sh::ROW_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct Layout {
+  int64_t mp, np, kp;
+  size_t a_bytes, b_bytes, total;
+};
+
+Layout layout_of(int64_t m, int64_t n, int64_t k) {
+  Layout L;
+  L.mp = (m + BM - 1) / BM * BM;
+  L.np = (n + Sh::BN - 1) / Sh::BN * Sh::BN;
+  L.kp = (k + 31) / 32 * 32;  // the pack kernel's tile; a multiple of BK
+  L.a_bytes = (size_t)L.mp * L.kp * sizeof(float);
+  L.b_bytes = (size_t)L.np * L.kp * sizeof(float);
+  L.total = 2 * L.a_bytes + 2 * L.b_bytes;
+  return L;
+}
+
+}  // namespace
+
+size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) { return layout_of(m, n, k).total; }
+
+bool wg_tf32x3_supported(const wg_device *d, int64_t m, int64_t n, int64_t k) {
+  if (d->cc_major != 10 || k < 8 || !encode_fn()) return false;
+  const Layout L = layout_of(m, n, k);
+  // TMA coordinates are 32-bit and the K extent's byte stride must fit the map.
+  return L.mp < ((int64_t)1 << 31) && L.np < ((int64_t)1 << 31) && L.kp < ((int64_t)1 << 31) &&
+         L.np / Sh::BN <= 65535;
+}
+
+wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
+                          const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C,
+                          int64_t ldc, void *ws) {
+  const Layout L = layout_of(m, n, k);
+  float *ahi = static_cast<float *>(ws);
+  float *alo = ahi + L.a_bytes / sizeof(float);
+  float *bhi = alo + L.a_bytes / sizeof(float);
+  float *blo = bhi + L.b_bytes / sizeof(float);
+  if (++d->epoch == 0) d->epoch = 1;
+  const uint32_t epoch = d->epoch;
+
+  // op(A)(i, p): K-contiguous when transA (A[p + i*lda]); op(B)(p, j) as row j of
+  // the N x K operand: K-contiguous when !transB (B[p + j*ldb]).
+  PackArgs pa{A, lda, transA ? 1 : 0, m, L.mp, ahi, alo, (L.mp / 32) * (L.kp / 32)};
+  PackArgs pb{B, ldb, transB ? 0 : 1, n, L.np, bhi, blo, (L.np / 32) * (L.kp / 32)};
+  const int64_t blocks = pa.tiles_r + pb.tiles_r;
+  {
+    wg_launch_scope scope(d, "sgemm_tf32x3_pack");
+    tf32x3_pack<<<(unsigned)blocks, 256, 0, d->stream>>>(pa, pb, k, L.kp, pa.tiles_r, d->dwords, epoch);
+    WG_CUDA(cudaGetLastError());
+  }
+
+  CUtensorMap maps[4];
+  if (!make_map(&maps[0], ahi, L.mp, L.kp, BM) || !make_map(&maps[1], alo, L.mp, L.kp, BM) ||
+      !make_map(&maps[2], bhi, L.np, L.kp, Sh::BN) || !make_map(&maps[3], blo, L.np, L.kp, Sh::BN))
+    return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
+  MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, epoch};
+  auto kern = tf32x3_mma<Sh>;
+  WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
+  dim3 grid((unsigned)(L.mp / BM), (unsigned)(L.np / Sh::BN));
+  {
+    wg_launch_scope scope(d, "sgemm_tf32x3_mma");
+    kern<<<grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
+    WG_CUDA(cudaGetLastError());
+  }
+  {
+    // Device-side fallback: exits at once unless the pack pass flagged this epoch.
+    wg_launch_scope scope(d, "sgemm_simt_fallback");
+    WG_CUDA(wg_launch_gemm_simt<float>(d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
+                                       d->dwords, epoch));
+  }
+  return WG_OK;
 }
