@@ -10,9 +10,6 @@ import pytest
 import validation_runner as vr
 
 
-class _UntouchableDevice:
-    pass
-
 
 @pytest.fixture(scope="module")
 def fake_device(wg):
