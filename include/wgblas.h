@@ -180,6 +180,23 @@ wg_status wg_dgemm_dev(wg_device *dev, int transA, int transB, int64_t m, int64_
                        double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
                        double beta, double *C, int64_t ldc);
 
+/* sgemm that allocates nothing — no counterpart in the reference. For callers
+ * that must not have the library call cudaMalloc for them (an application whose
+ * own allocator owns all device memory, a real-time loop that cannot stall on an
+ * allocation). It runs the 3xTF32 tensor-core kernels with their split-operand
+ * scratch in a fixed WG_NOALLOC_SCRATCH_BYTES array inside the library (held by
+ * every GPU that loads the library until exit); A, B and C are device pointers
+ * on this handle's device, ordered on its stream. It needs k >= 8 (alpha == 0 or
+ * k == 0 only scale C) and rejects, with WG_ERR_INVALID_ARGUMENT, shapes whose
+ * scratch 2*(round_up(m,128) + round_up(n,256))*round_up(k,32)*4 bytes exceeds
+ * the array. The first call on a device looks up the array's address and should
+ * come before any stream capture. All calls on a device share the array: calls
+ * that overlap on the GPU race, so order them on one stream. */
+#define WG_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+wg_status wg_sgemm_noalloc(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                           float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                           float beta, float *C, int64_t ldc);
+
 /* GEMM on host arrays — the typed-array path of sgemm()/dgemm()
  * (src/sgemm/sgemm.mjs:179-262): uploads op(A), op(B) and (when beta != 0) the
  * m x n block of C, runs the kernel, and writes the m x n block of the result

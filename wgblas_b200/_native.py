@@ -99,6 +99,8 @@ _sig("wg_sgemm_dev", _st, *_gemm_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void_
      ct.c_void_p, _i64)
 _sig("wg_dgemm_dev", _st, *_gemm_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double,
      ct.c_void_p, _i64)
+_sig("wg_sgemm_noalloc", _st, *_gemm_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_float,
+     ct.c_void_p, _i64)
 _sig("wg_sgemm_host", _st, *_gemm_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_float,
      ct.c_void_p, ct.c_void_p, _i64, _f32p)
 _sig("wg_dgemm_host", _st, *_gemm_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double,
