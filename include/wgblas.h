@@ -109,6 +109,12 @@ wg_status wg_device_sgemm_stats(wg_device *dev, wg_sgemm_stats *stats);
 #define WG_SGEMM_SIMT 1
 #define WG_SGEMM_TF32X3 2
 wg_status wg_device_set_sgemm_path(wg_device *dev, int path);
+/* dgemm kernel choice: AUTO picks by shape; SIMT forces the DFMA kernel (one
+ * sequential FMA chain per element), DMMA the FP64 tensor-core kernel. */
+#define WG_DGEMM_AUTO 0
+#define WG_DGEMM_SIMT 1
+#define WG_DGEMM_DMMA 2
+wg_status wg_device_set_dgemm_path(wg_device *dev, int path);
 
 /* Per-kernel device time of this handle's own launches, for benchmarks and
  * roofline reports. While profiling is on, every kernel the library launches

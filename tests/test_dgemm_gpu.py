@@ -188,3 +188,49 @@ def test_config3_4096_full_size_sampled(wg, device, oracle):
     t = oracle.dense(truth, n, len(cols))
     bound = oracle.dgemm_bound(n, len(cols), n, -0.75, absab, 1.25, Cs, n)
     assert np.all(np.abs(g - t) <= bound)
+
+
+# ---- the FP64 tensor-core (DMMA) kernel, forced on ------------------------------------
+
+@pytest.fixture
+def dmma(device):
+    device.set_dgemm_path("dmma")
+    yield device
+    device.set_dgemm_path("auto")
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 16), (200, 300, 77), (512, 512, 512), (1000, 1023, 777),
+                                   (129, 257, 40), (7, 9, 3)])
+@pytest.mark.parametrize("ta", [N, T])
+@pytest.mark.parametrize("tb", [N, T])
+def test_dmma_shapes_and_transposes(wg, device, oracle, dmma, shape, ta, tb):
+    m, n, k = shape
+    a_rows, a_cols = (m, k) if ta == N else (k, m)
+    b_rows, b_cols = (k, n) if tb == N else (n, k)
+    lda, ldb, ldc = a_rows + 3, b_rows + 1, m + 2
+    a = dict(transA=ta, transB=tb, m=m, n=n, k=k, alpha=-0.75, A=wg_random(lda * a_cols, 61), lda=lda,
+             B=wg_random(ldb * b_cols, 62), ldb=ldb, beta=1.25, C=wg_random(ldc * n, 63), ldc=ldc,
+             layout="column-major")
+    _check(oracle, _call(wg, device, a)["C"], a)
+
+
+@pytest.mark.parametrize("n", [7, 150])
+def test_dmma_ieee_specials(wg, device, oracle, dmma, n):
+    test_ieee_specials(wg, device, oracle, n)
+
+
+def test_dmma_same_sign_long_k(wg, device, oracle, dmma):
+    m = n = 192
+    k = 4096
+    A = wgblas_uniform(m * k, 0.0, 1.0, 71)
+    B = wgblas_uniform(k * n, 0.0, 1.0, 72)
+    C = wgblas_uniform(m * n, 0.0, 1.0, 73)
+    a = dict(transA=N, transB=N, m=m, n=n, k=k, alpha=1.0, A=A, lda=m, B=B, ldb=k, beta=1.0, C=C, ldc=m,
+             layout="column-major")
+    _check(oracle, _call(wg, device, a)["C"], a)
+
+
+def wgblas_uniform(n, low, high, seed):
+    import wgblas_b200
+
+    return wgblas_b200.randomFloat64Array(n, low, high, seed)

@@ -30,6 +30,7 @@ WG_ERR_NOT_SUPPORTED = 7
 
 WG_DEVICE_TIMING = 1
 WG_SGEMM_AUTO, WG_SGEMM_SIMT, WG_SGEMM_TF32X3 = 0, 1, 2
+WG_DGEMM_AUTO, WG_DGEMM_SIMT, WG_DGEMM_DMMA = 0, 1, 2
 
 c_dev_p = ct.c_void_p
 c_buf_p = ct.c_void_p
@@ -69,6 +70,7 @@ _sig("wg_device_sync", _st, c_dev_p)
 _sig("wg_device_check", _st, c_dev_p)
 _sig("wg_device_sgemm_stats", _st, c_dev_p, ct.POINTER(SgemmStats))
 _sig("wg_device_set_sgemm_path", _st, c_dev_p, ct.c_int)
+_sig("wg_device_set_dgemm_path", _st, c_dev_p, ct.c_int)
 class KernelProfile(ct.Structure):
     _fields_ = [("name", ct.c_char * 48), ("launches", ct.c_uint64), ("total_ms", ct.c_double)]
 

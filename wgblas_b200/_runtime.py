@@ -81,6 +81,11 @@ class Device:
         code = {"auto": nat.WG_SGEMM_AUTO, "simt": nat.WG_SGEMM_SIMT, "tf32x3": nat.WG_SGEMM_TF32X3}[path]
         nat.check(nat.lib.wg_device_set_sgemm_path(self.handle, code))
 
+    def set_dgemm_path(self, path: str) -> None:
+        """'auto' (default), 'simt' (DFMA kernel) or 'dmma' (FP64 tensor-core kernel)."""
+        code = {"auto": nat.WG_DGEMM_AUTO, "simt": nat.WG_DGEMM_SIMT, "dmma": nat.WG_DGEMM_DMMA}[path]
+        nat.check(nat.lib.wg_device_set_dgemm_path(self.handle, code))
+
     def set_profiling(self, on: bool) -> None:
         nat.check(nat.lib.wg_device_set_profiling(self.handle, int(bool(on))))
 

@@ -38,6 +38,7 @@ struct wg_device {
   unsigned *dwords;  // WG_DW_COUNT device words
   uint32_t epoch;    // sgemm call counter, tags WG_DW_FALLBACK
   int sgemm_path;
+  int dgemm_path;
   wg_sgemm_stats stats;
   uint64_t launches;  // kernels launched on this handle
   // profiling: event pairs waiting to be summed, and per-family totals
@@ -103,6 +104,11 @@ cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t 
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
                                 uint32_t only_if_epoch);
+
+// dgemm on the FP64 tensor-core (DMMA) path, mma.sync.m16n8k8.f64 (dgemm_dmma.cu).
+cudaError_t wg_launch_dgemm_dmma(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                 double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
+                                 double beta, double *C, int64_t ldc);
 
 // C = (alpha == 0 ? 0 : alpha*0) + beta*C elementwise — the k == 0 / alpha == 0 cases.
 template <typename T>

@@ -84,6 +84,7 @@ extern "C" wg_status wg_device_open(int ordinal, unsigned flags, wg_device **out
   }
   d->stream = d->own_stream;
   d->sgemm_path = WG_SGEMM_AUTO;
+  d->dgemm_path = WG_DGEMM_AUTO;
   *out = d;
   return WG_OK;
 }
@@ -244,6 +245,14 @@ extern "C" wg_status wg_device_profile_read(wg_device *d, wg_kernel_profile *out
 extern "C" wg_status wg_device_kernel_launches(const wg_device *d, uint64_t *launches) {
   if (!d || !launches) return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
   *launches = d->launches;
+  return WG_OK;
+}
+
+extern "C" wg_status wg_device_set_dgemm_path(wg_device *d, int path) {
+  if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  if (path != WG_DGEMM_AUTO && path != WG_DGEMM_SIMT && path != WG_DGEMM_DMMA)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown dgemm path %d", path);
+  d->dgemm_path = path;
   return WG_OK;
 }
 
