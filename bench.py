@@ -363,9 +363,12 @@ def main():
     fp32_peak = fp64_peak = hbm = None
     if not args.no_extra and rank == 0:
         fp32_peak = dev.probe_peak("fp32")
-        fp64_peak = dev.probe_peak("fp64")
+        fp64_dfma = dev.probe_peak("fp64")
+        fp64_dmma = dev.probe_peak("fp64_dmma")
+        fp64_peak = max(fp64_dfma, fp64_dmma)  # the FP64 peak: the faster of the two FP64 pipes
         hbm = dev.probe_peak("hbm")
-        extra["probes"] = {"fp32_ffma_tflops": fp32_peak, "fp64_dfma_tflops": fp64_peak, "hbm_copy_gbs": hbm,
+        extra["probes"] = {"fp32_ffma_tflops": fp32_peak, "fp64_dfma_tflops": fp64_dfma,
+                           "fp64_dmma_tflops": fp64_dmma, "hbm_copy_gbs": hbm,
                            "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
         extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
         for name in ("dgemm4096", "sgemm512", "ragged"):
@@ -388,6 +391,11 @@ def main():
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": None,
                 "peak_basis": f"{peak_src} bf16 dense x 0.5 (tf32 rate) / 3 products = 3xTF32 ceiling in fp32 FLOPs"}
+    elif dom[0] == "dgemm_dmma":
+        peak = fp64_peak
+        roof = {"bound": "fp64-tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak if peak else None, "traffic": None,
+                "peak_basis": "max of the DMMA-chain and DFMA-chain probes measured in this run"}
     else:
         peak = (fp64_peak if w["routine"] == "dgemm" else fp32_peak) or None
         roof = {"bound": "fp64-simt" if w["routine"] == "dgemm" else "fp32-simt", "achieved": achieved,

@@ -135,6 +135,7 @@ wg_status wg_device_kernel_launches(const wg_device *dev, uint64_t *launches);
 #define WG_PROBE_FP32_FMA 0 /* value: TFLOP/s of FFMA chains on every SM */
 #define WG_PROBE_FP64_FMA 1 /* value: TFLOP/s of DFMA chains on every SM */
 #define WG_PROBE_HBM_COPY 2 /* value: GB/s (read + write) of a 2 GiB device copy */
+#define WG_PROBE_FP64_DMMA 3 /* value: TFLOP/s of FP64 tensor-core (mma.sync f64) chains */
 wg_status wg_probe_peak(wg_device *dev, int kind, double *value);
 
 /* ---- device buffers: replace the storage of GpuMatrix / GpuVector ------- */
@@ -216,6 +217,46 @@ wg_status wg_dgemm_host(wg_device *dev, int transA, int transB, int64_t m, int64
                         double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
                         double beta, const double *C_in, double *C_out, int64_t ldc,
                         float *gpu_ms);
+
+/* ---- multi-GPU: C sharded by row blocks, B broadcast over NVLink (NCCL) ---- */
+/* The reference drives several GPUs only as independent devices with no data
+ * exchange (src/init.mjs:14-29, examples/init-two-gpus/init-two-gpus.js); this
+ * adds the sharded GEMM of its multi-GPU target. One communicator per device
+ * handle (one process per GPU, or one handle per GPU in a process). NCCL is
+ * loaded at run time (libnccl.so.2). */
+typedef struct wg_comm wg_comm;
+#define WG_COMM_ID_BYTES 128
+/* A fresh communicator id; rank 0 makes it and shares it out of band. */
+wg_status wg_comm_unique_id(unsigned char *id, size_t len);
+/* Joins communicator `id` as `rank` of `nranks`. Non-blocking init: gives up
+ * after timeout_ms (<= 0: 60 s), aborting, with WG_ERR_NCCL. */
+wg_status wg_comm_init_rank(wg_device *dev, int nranks, int rank, const unsigned char *id, size_t len,
+                            int timeout_ms, wg_comm **out);
+wg_status wg_comm_destroy(wg_comm *comm);
+wg_status wg_comm_abort(wg_comm *comm);
+wg_status wg_comm_rank(const wg_comm *comm, int *rank, int *nranks);
+/* Waits (bounded by the communicator's timeout) for the last sharded call's
+ * work; on timeout or an asynchronous NCCL error aborts and returns WG_ERR_NCCL. */
+wg_status wg_comm_wait(wg_comm *comm);
+/* This rank's block of C (m_local x n, device pointer, ldc) := alpha * op(A_local)
+ * (m_local x k) * op(B) + beta * C_local. B (column-major k x n, or n x k when
+ * transB) holds the operand on `root` and is overwritten with it on the other
+ * ranks: it is broadcast in panels of panel_cols columns (<= 0: one panel), and
+ * the GEMM of each panel starts as soon as that panel has arrived. n, k, ldb,
+ * transB, root and panel_cols must agree on every rank. Queued on the device
+ * stream; wg_comm_wait or wg_device_sync waits for it. */
+wg_status wg_sgemm_sharded(wg_comm *comm, int transA, int transB, int64_t m_local, int64_t n, int64_t k,
+                           float alpha, const float *A_local, int64_t lda, float *B, int64_t ldb, int root,
+                           float beta, float *C_local, int64_t ldc, int64_t panel_cols);
+wg_status wg_dgemm_sharded(wg_comm *comm, int transA, int transB, int64_t m_local, int64_t n, int64_t k,
+                           double alpha, const double *A_local, int64_t lda, double *B, int64_t ldb, int root,
+                           double beta, double *C_local, int64_t ldc, int64_t panel_cols);
+/* Gathers every rank's C rows into C_full (ldc_full) on `root`; row_offsets has
+ * nranks+1 entries (rank r owns rows [row_offsets[r], row_offsets[r+1])). */
+wg_status wg_sgemm_gather_rows(wg_comm *comm, const float *C_local, int64_t m_local, int64_t n, int64_t ldc,
+                               int root, float *C_full, int64_t ldc_full, const int64_t *row_offsets);
+wg_status wg_dgemm_gather_rows(wg_comm *comm, const double *C_local, int64_t m_local, int64_t n, int64_t ldc,
+                               int root, double *C_full, int64_t ldc_full, const int64_t *row_offsets);
 
 /* ---- seeded inputs: src/random/random.mjs:4-26 ------------------------------ */
 /* randomFloat32Array(n, low, high, seed) / randomFloat64Array: mulberry32 draws

@@ -75,7 +75,7 @@ class KernelProfile(ct.Structure):
     _fields_ = [("name", ct.c_char * 48), ("launches", ct.c_uint64), ("total_ms", ct.c_double)]
 
 
-WG_PROBE_FP32_FMA, WG_PROBE_FP64_FMA, WG_PROBE_HBM_COPY = 0, 1, 2
+WG_PROBE_FP32_FMA, WG_PROBE_FP64_FMA, WG_PROBE_HBM_COPY, WG_PROBE_FP64_DMMA = 0, 1, 2, 3
 _sig("wg_device_set_profiling", _st, c_dev_p, ct.c_int)
 _sig("wg_device_profile_read", _st, c_dev_p, ct.POINTER(KernelProfile), ct.c_int, ct.POINTER(ct.c_int))
 _sig("wg_device_kernel_launches", _st, c_dev_p, ct.POINTER(ct.c_uint64))
@@ -107,6 +107,21 @@ _sig("wg_sgemm_host", _st, *_gemm_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void
      ct.c_void_p, ct.c_void_p, _i64, _f32p)
 _sig("wg_dgemm_host", _st, *_gemm_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double,
      ct.c_void_p, ct.c_void_p, _i64, _f32p)
+c_comm_p = ct.c_void_p
+_sig("wg_comm_unique_id", _st, ct.c_char_p, ct.c_size_t)
+_sig("wg_comm_init_rank", _st, c_dev_p, ct.c_int, ct.c_int, ct.c_char_p, ct.c_size_t, ct.c_int, ct.POINTER(c_comm_p))
+_sig("wg_comm_destroy", _st, c_comm_p)
+_sig("wg_comm_abort", _st, c_comm_p)
+_sig("wg_comm_rank", _st, c_comm_p, ct.POINTER(ct.c_int), ct.POINTER(ct.c_int))
+_sig("wg_comm_wait", _st, c_comm_p)
+_shard = [c_comm_p, ct.c_int, ct.c_int, _i64, _i64, _i64]
+_sig("wg_sgemm_sharded", _st, *_shard, ct.c_float, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_int, ct.c_float,
+     ct.c_void_p, _i64, _i64)
+_sig("wg_dgemm_sharded", _st, *_shard, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_int, ct.c_double,
+     ct.c_void_p, _i64, _i64)
+_gather = [c_comm_p, ct.c_void_p, _i64, _i64, _i64, ct.c_int, ct.c_void_p, _i64, ct.POINTER(_i64)]
+_sig("wg_sgemm_gather_rows", _st, *_gather)
+_sig("wg_dgemm_gather_rows", _st, *_gather)
 _sig("wg_random_f32", None, _f32p, _i64, ct.c_double, ct.c_double, ct.c_uint32)
 _sig("wg_random_f64", None, _f64p, _i64, ct.c_double, ct.c_double, ct.c_uint32)
 _sig("wg_random_normal_f32", None, _f32p, _i64, ct.c_uint32)

@@ -102,8 +102,10 @@ class Device:
         return int(v.value)
 
     def probe_peak(self, kind: str) -> float:
-        """Roofline probe: 'fp32' / 'fp64' FMA TFLOP/s or 'hbm' copy GB/s."""
-        code = {"fp32": nat.WG_PROBE_FP32_FMA, "fp64": nat.WG_PROBE_FP64_FMA, "hbm": nat.WG_PROBE_HBM_COPY}[kind]
+        """Roofline probe: 'fp32' / 'fp64' FMA-chain TFLOP/s, 'fp64_dmma' FP64 tensor-core
+        TFLOP/s, or 'hbm' copy GB/s."""
+        code = {"fp32": nat.WG_PROBE_FP32_FMA, "fp64": nat.WG_PROBE_FP64_FMA, "hbm": nat.WG_PROBE_HBM_COPY,
+                "fp64_dmma": nat.WG_PROBE_FP64_DMMA}[kind]
         v = ct.c_double(0)
         nat.check(nat.lib.wg_probe_peak(self.handle, code, ct.byref(v)))
         return float(v.value)

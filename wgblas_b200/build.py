@@ -14,7 +14,7 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libwgblas_b200.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 
-SOURCES = ["runtime.cu", "gemm.cu", "gemm_simt.cu", "sgemm_tf32x3.cu", "probe.cu", "sgemm_noalloc.cu", "dgemm_dmma.cu"]
+SOURCES = ["runtime.cu", "gemm.cu", "gemm_simt.cu", "sgemm_tf32x3.cu", "probe.cu", "sgemm_noalloc.cu", "dgemm_dmma.cu", "shard.cu"]
 HEADERS = ["internal.h", "tcgen05.cuh"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -44,7 +44,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
                 cmd.insert(1, "-Xptxas=-v")
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
-        subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB, *objs], check=True)
+        subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-ldl"], check=True)
     return LIB
 
 

@@ -58,6 +58,16 @@ wg_status check_arch(const wg_device *d) {
 template <typename T>
 wg_status gemm_launch(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                       const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+}  // namespace
+
+template <typename T>
+wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                          const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc) {
+  if (m == 0 || n == 0) return WG_OK;
+  return gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+namespace {
 
 // sgemm kernel choice. The 3xTF32 tensor-core kernel needs enough k to amortise
 // its split pass and gives no benefit on tiny grids; everything else, and any
@@ -261,6 +271,12 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
 }
 
 }  // namespace
+
+template wg_status wg_gemm_enqueue<float>(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *,
+                                          int64_t, const float *, int64_t, float, float *, int64_t);
+template wg_status wg_gemm_enqueue<double>(wg_device *, int, int, int64_t, int64_t, int64_t, double,
+                                           const double *, int64_t, const double *, int64_t, double, double *,
+                                           int64_t);
 
 extern "C" wg_status wg_sgemm(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                               float alpha, const wg_buffer *A, int64_t offA, int64_t lda,

@@ -91,6 +91,12 @@ struct wg_device_guard {
   }
 };
 
+// Queues C = alpha*op(A)op(B) + beta*C on d->stream through the kernel
+// dispatcher (no argument checks, no dgemm quick return: callers check).
+template <typename T>
+wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
+                          const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+
 // Returns at least `bytes` of device scratch owned by the handle (stream-ordered reuse).
 wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);
 

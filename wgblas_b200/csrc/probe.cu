@@ -29,6 +29,63 @@ __global__ void __launch_bounds__(256) fma_probe_kernel(T x, T y, int iters, T *
   if (s == T(-12345.678)) sink[threadIdx.x] = s;  // never true; keeps the chains live
 }
 
+// Independent chains of FP64 tensor-core MMAs (mma.sync m16n8k8 f64) per warp.
+__global__ void __launch_bounds__(256) dmma_probe_kernel(double x, int iters, double *sink) {
+  constexpr int CH = 4;
+  double acc[CH][4];
+  double a[4], b[2];
+#pragma unroll
+  for (int v = 0; v < 4; v++) a[v] = x * (threadIdx.x + v);
+  b[0] = x;
+  b[1] = 1.0 - x;
+#pragma unroll
+  for (int c = 0; c < CH; c++)
+#pragma unroll
+    for (int v = 0; v < 4; v++) acc[c][v] = 0.0;
+  for (int i = 0; i < iters; i++) {
+#pragma unroll
+    for (int c = 0; c < CH; c++)
+      asm volatile(
+          "mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 "
+          "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+          : "+d"(acc[c][0]), "+d"(acc[c][1]), "+d"(acc[c][2]), "+d"(acc[c][3])
+          : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
+  }
+  double s = 0.0;
+#pragma unroll
+  for (int c = 0; c < CH; c++)
+#pragma unroll
+    for (int v = 0; v < 4; v++) s += acc[c][v];
+  if (s == -12345.678) sink[threadIdx.x] = s;
+}
+
+wg_status dmma_probe(wg_device *d, double *tflops) {
+  const int blocks = d->sm_count * 4, threads = 256, iters = 1 << 12;
+  double *sink = nullptr;
+  WG_CUDA(cudaMallocAsync((void **)&sink, threads * sizeof(double), d->stream));
+  cudaEvent_t e0, e1;
+  WG_CUDA(cudaEventCreate(&e0));
+  WG_CUDA(cudaEventCreate(&e1));
+  float best = 1e30f;
+  for (int rep = 0; rep < 4; rep++) {
+    cudaEventRecord(e0, d->stream);
+    dmma_probe_kernel<<<blocks, threads, 0, d->stream>>>(1e-3, iters, sink);
+    cudaEventRecord(e1, d->stream);
+    WG_CUDA(cudaEventSynchronize(e1));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (rep > 0 && ms < best) best = ms;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFreeAsync(sink, d->stream);
+  WG_CUDA(cudaStreamSynchronize(d->stream));
+  // 4 chains x 16x8x8 MACs per warp per iteration
+  const double flops = 2.0 * 16 * 8 * 8 * 4.0 * (double)iters * blocks * (threads / 32);
+  *tflops = flops / (best * 1e-3) / 1e12;
+  return WG_OK;
+}
+
 __global__ void copy_probe_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, size_t n) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = src[i];
@@ -103,6 +160,7 @@ extern "C" wg_status wg_probe_peak(wg_device *d, int kind, double *value) {
     case WG_PROBE_FP32_FMA: return fma_probe<float>(d, value);
     case WG_PROBE_FP64_FMA: return fma_probe<double>(d, value);
     case WG_PROBE_HBM_COPY: return copy_probe(d, value);
+    case WG_PROBE_FP64_DMMA: return dmma_probe(d, value);
     default: return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown probe %d", kind);
   }
 }

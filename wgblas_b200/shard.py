@@ -1,0 +1,140 @@
+"""Multi-GPU sgemm / dgemm: C sharded by row blocks, B broadcast over NVLink.
+
+The reference drives several GPUs only as independent devices
+(examples/init-two-gpus/init-two-gpus.js); this module adds the sharded GEMM
+of its multi-GPU target on top of the C ABI's communicator (wg_comm_*,
+wgblas_b200/csrc/shard.cu). One process per GPU: every rank holds its row
+block of op(A) and of C resident on its GPU (scattered once), and B lives on
+the root; each call broadcasts B in column panels, the GEMM of each panel
+starting as soon as the panel has arrived.
+
+The host-side planning here (``plan_rows``, ``row_block``, ``place_rows``) is
+pure Python/numpy and is what the CPU multi-process tests check.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+
+import numpy as np
+
+from . import _native as nat
+from ._runtime import Device
+from .classes import GpuMatrix
+
+
+def plan_rows(m: int, nranks: int, align: int = 128) -> list[int]:
+    """Row offsets (nranks + 1 entries) splitting m rows into contiguous blocks.
+
+    Blocks are multiples of `align` rows (the tensor-core kernels' tile height)
+    except the last non-empty one, and differ by at most `align` rows."""
+    if nranks < 1:
+        raise ValueError("nranks must be >= 1")
+    units = -(-m // align) if m > 0 else 0
+    base, extra = divmod(units, nranks)
+    offs = [0]
+    for r in range(nranks):
+        u = base + (1 if r < extra else 0)
+        offs.append(min(m, offs[-1] + u * align))
+    offs[-1] = m
+    return offs
+
+
+def row_block(X: np.ndarray, rows: int, cols: int, ld: int, r0: int, r1: int, trans: bool) -> tuple[np.ndarray, int]:
+    """Rows [r0, r1) of op(X) for a column-major X (rows x cols of op(X)), as a
+    dense column-major block of op(X)'s orientation: returns (block, ld_block).
+
+    Without trans, op(X) = X and the block is X[r0:r1, :] (ld = r1 - r0); with
+    trans, op(X) = X^T and the block is X[:, r0:r1] stored as its own column-major
+    (cols x (r1-r0)) matrix, so the caller keeps trans set (ld = cols)."""
+    mr = r1 - r0
+    if not trans:
+        out = np.empty(max(mr * cols, 1), X.dtype)[: mr * cols]
+        for j in range(cols):
+            out[j * mr:(j + 1) * mr] = X[r0 + j * ld: r1 + j * ld]
+        return out, max(mr, 1)
+    out = np.empty(max(cols * mr, 1), X.dtype)[: cols * mr]
+    for i in range(mr):
+        out[i * cols:(i + 1) * cols] = X[(r0 + i) * ld: (r0 + i) * ld + cols]
+    return out, max(cols, 1)
+
+
+def place_rows(C_full: np.ndarray, ldc: int, block: np.ndarray, ld_block: int, r0: int, r1: int, n: int) -> None:
+    """Writes a dense column-major row block back into rows [r0, r1) of C_full."""
+    mr = r1 - r0
+    for j in range(n):
+        C_full[r0 + j * ldc: r1 + j * ldc] = block[j * ld_block: j * ld_block + mr]
+
+
+class Comm:
+    """A communicator joining one device handle to the other ranks' (wg_comm)."""
+
+    def __init__(self, device: Device, nranks: int, rank: int, unique_id: bytes, timeout_ms: int = 60000):
+        self.device = device
+        self.nranks = nranks
+        self.rank = rank
+        h = nat.c_comm_p()
+        nat.check(nat.lib.wg_comm_init_rank(device.handle, nranks, rank, unique_id, len(unique_id), timeout_ms,
+                                            ct.byref(h)))
+        self._h = h
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ct.create_string_buffer(128)
+        nat.check(nat.lib.wg_comm_unique_id(buf, 128))
+        return buf.raw
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise RuntimeError("communicator destroyed")
+        return self._h
+
+    def wait(self) -> None:
+        nat.check(nat.lib.wg_comm_wait(self.handle))
+
+    def abort(self) -> None:
+        if self._h is not None:
+            nat.lib.wg_comm_abort(self._h)
+
+    def destroy(self) -> None:
+        if self._h is not None:
+            nat.lib.wg_comm_destroy(self._h)
+            self._h = None
+
+
+def comm_from_torch(device: Device, timeout_ms: int = 60000) -> Comm:
+    """Creates the communicator of a torch.distributed job (any backend; the
+    128-byte id travels through it)."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    box = [Comm.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return Comm(device, world, rank, box[0], timeout_ms)
+
+
+def _ptr(g: GpuMatrix) -> ct.c_void_p:
+    return ct.c_void_p(g.device_ptr())
+
+
+def gemm_sharded(comm: Comm, transA: bool, transB: bool, m_local: int, n: int, k: int, alpha, A_local: GpuMatrix,
+                 B: GpuMatrix, beta, C_local: GpuMatrix, root: int = 0, panel_cols: int = 0) -> None:
+    """Queues this rank's C_local := alpha*op(A_local)*op(B) + beta*C_local with B
+    broadcast from `root` (column-major GpuMatrix operands; B is overwritten with
+    root's B on the other ranks). dtype follows the operands (float32 -> sgemm)."""
+    f64 = np.dtype(C_local.dtype) == np.float64
+    fn = nat.lib.wg_dgemm_sharded if f64 else nat.lib.wg_sgemm_sharded
+    al, be = (float(alpha), float(beta)) if f64 else (np.float32(alpha), np.float32(beta))
+    nat.check(fn(comm.handle, int(bool(transA)), int(bool(transB)), m_local, n, k, al,
+                 _ptr(A_local) if m_local else None, A_local.lda, _ptr(B), B.lda, root, be,
+                 _ptr(C_local) if m_local else None, C_local.lda, panel_cols))
+
+
+def gather_rows(comm: Comm, C_local: GpuMatrix, m_local: int, n: int, row_offsets: list[int], root: int = 0,
+                C_full: GpuMatrix | None = None) -> None:
+    """Queues the gather of every rank's C rows into C_full on `root`."""
+    f64 = np.dtype(C_local.dtype) == np.float64
+    fn = nat.lib.wg_dgemm_gather_rows if f64 else nat.lib.wg_sgemm_gather_rows
+    offs = (ct.c_int64 * len(row_offsets))(*row_offsets)
+    nat.check(fn(comm.handle, _ptr(C_local) if m_local else None, m_local, n, C_local.lda, root,
+                 _ptr(C_full) if C_full is not None else None, C_full.lda if C_full is not None else 0, offs))
