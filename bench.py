@@ -13,10 +13,15 @@ Workloads:
   dgemm4096   configs[2]: dgemm 4096^3 column-major NT, alpha=-0.75, beta=1.25, U[-1,1]
   sgemm512    configs[0]: sgemm 512^3 NN, alpha=1.5, beta=0.5, U[-1,1]
   ragged      configs[3]: sgemm 1000x1023x777, lda=1024 ldb=800 ldc=1040, NN
+  shard16384  configs[4]: sgemm 16384^3 NN, alpha=1, beta=1, U[-1,1], C row-block sharded
+              over the ranks with B broadcast from rank 0 over NVLink (the default at N>1)
+  shard16384d the same for dgemm
 A step is one sgemm/dgemm call on operands resident in HBM; L2 is flushed
 (a 512 MB device write) between steps, outside the per-step CUDA events.
-With --gpus N>1 (torchrun), every rank runs the same workload on its own GPU
-(independent replicas; value = sum over ranks of their work / max rank time).
+With --gpus N>1 (torchrun) the default workload is shard16384: each rank keeps
+its row block of A and C resident, and every step broadcasts B from rank 0 in
+2048-column panels, each panel's GEMM overlapping the next panel's transfer;
+value = total FLOPs / max over ranks of the step time (strong scaling).
 
 --impl reference times the reference's arithmetic on the host cores instead:
 the CPU oracle's restatement of the reference's fp32 shader arithmetic
@@ -49,7 +54,12 @@ WORKLOADS = {
                      lda=512, ldb=512, ldc=512, alpha=1.5, beta=0.5, data="uniform"),
     "ragged": dict(routine="sgemm", config_index=3, transA=0, transB=0, m=1000, n=1023, k=777,
                    lda=1024, ldb=800, ldc=1040, alpha=0.3, beta=-2.0, data="uniform"),
+    "shard16384": dict(routine="sgemm", config_index=4, transA=0, transB=0, m=16384, n=16384, k=16384,
+                       lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
+    "shard16384d": dict(routine="dgemm", config_index=4, transA=0, transB=0, m=16384, n=16384, k=16384,
+                        lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
 }
+PANEL_COLS = 2048  # B broadcast panel width of the sharded workloads
 
 
 def flops(w):
@@ -163,6 +173,17 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def sum_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -221,6 +242,62 @@ def time_resident(wg, dev, w, steps, warmup, world, flush):
     return ms, prof, launches, wall
 
 
+def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
+    """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs)."""
+    import torch
+
+    from wgblas_b200.shard import gemm_sharded, plan_rows
+
+    m, n, k = w["m"], w["n"], w["k"]
+    offs = plan_rows(m, world)
+    mr = offs[rank + 1] - offs[rank]
+    dt = np.float64 if w["routine"] == "dgemm" else np.float32
+    rnd = wg.randomFloat64Array if dt == np.float64 else wg.randomFloat32Array
+    GA = wg.GpuMatrix.from_(dev, rnd(mr * k, -1, 1, 10 + rank), mr, k, mr, "column-major")
+    GC = wg.GpuMatrix.from_(dev, rnd(mr * n, -1, 1, 30 + rank), mr, n, mr, "column-major")
+    GB = (wg.GpuMatrix.from_(dev, rnd(k * n, -1, 1, 2), k, n, k, "column-major") if rank == 0
+          else wg.GpuMatrix.empty(dev, k, n, k, "column-major", dt))
+    stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+
+    def step():
+        gemm_sharded(comm, w["transA"], w["transB"], mr, n, k, w["alpha"], GA, GB, w["beta"], GC, root=0,
+                     panel_cols=PANEL_COLS)
+
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                flush.add_(1.0)
+                step()
+            dev.synchronize()
+            comm.wait()
+            dev.check()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            barrier(world)
+            dev.synchronize()
+            dev.profile_read()
+            dev.set_profiling(True)
+            launches0 = dev.kernel_launches()
+            t0 = time.perf_counter()
+            for i in range(steps):
+                flush.add_(1.0)
+                starts[i].record(stream)
+                step()
+                ends[i].record(stream)
+            dev.synchronize()
+            comm.wait()
+            wall = time.perf_counter() - t0
+            launches = dev.kernel_launches() - launches0
+            dev.set_profiling(False)
+            prof = dev.profile_read()
+            dev.check()
+            ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    finally:
+        for g in (GA, GB, GC):
+            g.destroy()
+    return ms, prof, launches, wall
+
+
 def time_e2e(wg, dev, w, steps, warmup):
     """The same metric through the public API on page-locked host arrays: every step
     uploads op(A), op(B) (and C when beta != 0), computes, and reads C back."""
@@ -259,10 +336,10 @@ def cpu_baseline(w, target_s=12.0):
     m, k = w["m"], w["k"]
     dt = np.float64 if w["routine"] == "dgemm" else np.float32
     rng = np.random.default_rng(0)
-    A = rng.uniform(-1, 1, w["lda"] * ac).astype(dt)
+    A = rng.random(w["lda"] * ac, dtype=dt) * 2 - 1
 
     def run(ns):
-        B = rng.uniform(-1, 1, (w["ldb"] * (ns if not w["transB"] else bc))).astype(dt)
+        B = rng.random(w["ldb"] * (ns if not w["transB"] else bc), dtype=dt) * 2 - 1
         ldb = w["ldb"]
         C = np.zeros(w["ldc"] * ns, dt)
         t0 = time.perf_counter()
@@ -313,18 +390,27 @@ def run_reference(args, world, rank):
 
 
 def pick_workload(args, world):
-    return "sgemm4096" if args.workload == "auto" else args.workload
+    if args.workload == "auto":
+        return "shard16384" if world > 1 else "sgemm4096"
+    return args.workload
 
 
-def config_of(w, name):
+def config_of(w, name, world=1):
+    shard = ""
+    if w.get("sharded"):
+        shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 in {PANEL_COLS}-column "
+                 "panels (NCCL over NVLink)")
     return {"workload": f"configs[{w['config_index']}] {w['routine']} {w['m']}x{w['n']}x{w['k']} "
-                        f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major",
+                        f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major{shard}",
+            "parallelism": f"row-sharded x{world}" if w.get("sharded") else "single GPU",
             "m": w["m"], "n": w["n"], "k": w["k"], "lda": w["lda"], "ldb": w["ldb"], "ldc": w["ldc"],
             "alpha": w["alpha"], "beta": w["beta"], "inputs": "N(0,1) seeded" if w["data"] == "normal" else "U[-1,1] seeded",
             "l2": "flushed between steps (512 MB device write outside the step events)"}
 
 
 def main():
+    # NCCL's own banner and debug output go to stderr: stdout carries the one JSON line.
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
@@ -351,12 +437,22 @@ def main():
 
     phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     smi_index = phys[local] if len(phys) > local and phys[local].strip() else str(local)
+    comm = None
+    if w.get("sharded"):
+        from wgblas_b200.shard import Comm, comm_from_torch
+
+        comm = comm_from_torch(dev) if world > 1 else Comm(dev, 1, 0, Comm.unique_id())
     with Clocks(smi_index) as clk:
-        ms, prof, launches, wall = time_resident(wg, dev, w, args.steps, args.warmup, world, flush)
+        if w.get("sharded"):
+            ms, prof, launches, wall = time_sharded(wg, dev, comm, w, args.steps, args.warmup, world, rank, flush)
+        else:
+            ms, prof, launches, wall = time_resident(wg, dev, w, args.steps, args.warmup, world, flush)
     clocks = clk.summary()
     step_ms = statistics.mean(ms)
     step_ms_max = max_over_ranks(step_ms, world)
-    value = flops(w) * world / (step_ms_max * 1e-3) / 1e12
+    # sharded: the ranks together do one product; replicas: each rank does one
+    value = flops(w) * (1 if w.get("sharded") else world) / (step_ms_max * 1e-3) / 1e12
+    launches_total = int(sum_over_ranks(launches, world))
 
     peaks, peak_src = measured_peaks()
     extra = {}
@@ -371,7 +467,7 @@ def main():
                            "fp64_dmma_tflops": fp64_dmma, "hbm_copy_gbs": hbm,
                            "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
         extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
-        for name in ("dgemm4096", "sgemm512", "ragged"):
+        for name in ("dgemm4096", "sgemm512", "ragged") if world == 1 else ():
             if name == pick_workload(args, world):
                 continue
             wx = WORKLOADS[name]
@@ -381,6 +477,28 @@ def main():
             extra[name] = {"tflops": tf, "ms_per_step": statistics.mean(msx),
                            f"pct_of_{'fp64' if wx['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf / pk,
                            "kernels": {k: v[1] / max(v[0], 1) for k, v in profx.items()}}
+
+    if not args.no_extra and world == 1 and not w.get("sharded"):
+        # configs[4] on one GPU through the same sharded path (one rank): the N=1
+        # reference point for the multi-GPU scaling of the sharded workload.
+        from wgblas_b200.shard import Comm
+
+        c1 = Comm(dev, 1, 0, Comm.unique_id())
+        try:
+            ws = WORKLOADS["shard16384"]
+            ms1, prof1, _, _ = time_sharded(wg, dev, c1, ws, 3, 3, 1, 0, flush)
+            tf1 = flops(ws) / (statistics.mean(ms1) * 1e-3) / 1e12
+            extra["shard16384_1gpu"] = {"tflops": tf1, "ms_per_step": statistics.mean(ms1),
+                                        "pct_of_fp32_peak": 100.0 * tf1 / fp32_peak if fp32_peak else None,
+                                        "kernels": {k: v[1] / max(v[0], 1) for k, v in prof1.items()}}
+        finally:
+            c1.destroy()
+    if world > 1 and not args.no_extra and w["routine"] == "sgemm":
+        # configs[4] for dgemm on the same ranks
+        wd = WORKLOADS["shard16384d"]
+        msd, _, _, _ = time_sharded(wg, dev, comm, wd, 3, 2, world, rank, flush)
+        md = max_over_ranks(statistics.mean(msd), world)
+        extra["shard16384d"] = {"tflops": flops(wd) / (md * 1e-3) / 1e12, "ms_per_step": md}
 
     # Roofline of the dominant kernel, from the per-kernel events of the timed region.
     dom = max(prof.items(), key=lambda kv: kv[1][1]) if prof else ("?", (1, step_ms))
@@ -405,18 +523,21 @@ def main():
     roof["kernel_ms"] = dom_ms
     roof["kernels"] = {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in prof.items()}
 
-    e2e = time_e2e(wg, dev, w, max(3, args.steps // 2), args.warmup) if rank == 0 else None
+    e2e = time_e2e(wg, dev, w, max(3, args.steps // 2), args.warmup) if (rank == 0 and not w.get("sharded")) else None
     cb = None if (args.no_cpu_baseline or rank != 0 or world > 1) else cpu_baseline(w)
     barrier(world)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True,
+                "scaling": "strong" if w.get("sharded") else "weak",
                 "vs_baseline": None, "dtype": "f64" if w["routine"] == "dgemm" else "f32",
-                "data": "synthetic (seeded mulberry32)", "config": config_of(w, args.workload),
+                "data": "synthetic (seeded mulberry32)", "config": config_of(w, args.workload, world),
                 "roofline": roof, "cpu_baseline": cb, "e2e": e2e,
-                "gpu_launches": int(max_over_ranks(launches, world) * world) if world > 1 else int(launches),
+                "gpu_launches": launches_total,
                 "clocks": clocks, "wall_s_timed_region": wall, "extra": extra}
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.destroy()
     if world > 1:
         import torch.distributed as dist
 

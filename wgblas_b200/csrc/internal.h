@@ -131,3 +131,11 @@ bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 wg_status wg_sgemm_tf32x3(wg_device *dev, int transA, int transB, int64_t m, int64_t n,
                           int64_t k, float alpha, const float *A, int64_t lda, const float *B,
                           int64_t ldb, float beta, float *C, int64_t ldc, void *ws);
+// The same, for one column panel of a larger product: pack_a = false reuses the
+// op(A) split left in `ws` by an earlier panel of the same m x k operand, and all
+// panels of one product share `epoch` (wg_next_epoch) so a flagged operand sends
+// that panel and every later one to the FFMA kernel.
+wg_status wg_sgemm_tf32x3_panel(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                                float *C, int64_t ldc, void *ws, bool pack_a, uint32_t epoch);
+uint32_t wg_next_epoch(wg_device *dev);

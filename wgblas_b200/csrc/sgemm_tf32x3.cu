@@ -330,20 +330,18 @@ bool wg_tf32x3_supported(const wg_device *d, int64_t m, int64_t n, int64_t k) {
          L.np / Sh::BN <= 65535;
 }
 
-wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
-                          const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C,
-                          int64_t ldc, void *ws) {
+wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                                float *C, int64_t ldc, void *ws, bool pack_a, uint32_t epoch) {
   const Layout L = layout_of(m, n, k);
   float *ahi = static_cast<float *>(ws);
   float *alo = ahi + L.a_bytes / sizeof(float);
   float *bhi = alo + L.a_bytes / sizeof(float);
   float *blo = bhi + L.b_bytes / sizeof(float);
-  if (++d->epoch == 0) d->epoch = 1;
-  const uint32_t epoch = d->epoch;
 
   // op(A)(i, p): K-contiguous when transA (A[p + i*lda]); op(B)(p, j) as row j of
   // the N x K operand: K-contiguous when !transB (B[p + j*ldb]).
-  PackArgs pa{A, lda, transA ? 1 : 0, m, L.mp, ahi, alo, (L.mp / 32) * (L.kp / 32)};
+  PackArgs pa{A, lda, transA ? 1 : 0, m, L.mp, ahi, alo, pack_a ? (L.mp / 32) * (L.kp / 32) : 0};
   PackArgs pb{B, ldb, transB ? 0 : 1, n, L.np, bhi, blo, (L.np / 32) * (L.kp / 32)};
   const int64_t blocks = pa.tiles_r + pb.tiles_r;
   {
@@ -366,10 +364,22 @@ wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64
     WG_CUDA(cudaGetLastError());
   }
   {
-    // Device-side fallback: exits at once unless the pack pass flagged this epoch.
+    // Device-side fallback: exits at once unless a pack pass flagged this epoch.
     wg_launch_scope scope(d, "sgemm_simt_fallback");
     WG_CUDA(wg_launch_gemm_simt<float>(d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
                                        d->dwords, epoch));
   }
   return WG_OK;
+}
+
+uint32_t wg_next_epoch(wg_device *d) {
+  if (++d->epoch == 0) d->epoch = 1;
+  return d->epoch;
+}
+
+wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
+                          const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C,
+                          int64_t ldc, void *ws) {
+  return wg_sgemm_tf32x3_panel(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, true,
+                               wg_next_epoch(d));
 }
