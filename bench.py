@@ -385,7 +385,7 @@ def run_reference(args, world, rank):
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
                              "sample": cb["sample"]},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -408,9 +408,23 @@ def config_of(w, name, world=1):
             "l2": "flushed between steps (512 MB device write outside the step events)"}
 
 
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the one JSON line to the process's original stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
-    # NCCL's own banner and debug output go to stderr: stdout carries the one JSON line.
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    # Native libraries (NCCL's banner, for one) may print to file descriptor 1;
+    # move it to stderr for the whole run so stdout carries only the JSON line.
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
@@ -535,7 +549,7 @@ def main():
                 "roofline": roof, "cpu_baseline": cb, "e2e": e2e,
                 "gpu_launches": launches_total,
                 "clocks": clocks, "wall_s_timed_region": wall, "extra": extra}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if comm is not None:
         comm.destroy()
     if world > 1:
