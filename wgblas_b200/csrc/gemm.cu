@@ -95,9 +95,10 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
   }
   if (tc) {
     void *ws = nullptr;
-    wg_status st = wg_workspace(d, wg_tf32x3_workspace_bytes(m, n, k), &ws);
+    const size_t bytes = wg_tf32x3_workspace_bytes_sk(d, m, n, k);
+    wg_status st = wg_workspace(d, bytes, &ws);
     if (st != WG_OK) return st;
-    st = wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws);
+    st = wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes);
     if (st != WG_OK) return st;
     d->stats.tf32x3_launches++;
     return WG_OK;

@@ -121,21 +121,25 @@ template <typename T>
 cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T beta, T *C,
                             int64_t ldc);
 
-// Bytes of scratch the 3xTF32 path needs for this shape.
+// Bytes of scratch the 3xTF32 path needs for this shape: the split operands
+// alone (whole-tile scheduling), or with the stream-K partial sums and counters.
 size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
+size_t wg_tf32x3_workspace_bytes_sk(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 // True when the 3xTF32 path supports this shape on this device.
 bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 // Splits op(A), op(B) into tf32 hi/lo operands in `ws`, then runs the tcgen05 kernel.
 // Operands outside the split's exact range make the kernel exit and the FFMA
 // kernel (launched right after, gated on the same epoch) compute C instead.
+// `ws` holds ws_bytes: stream-K scheduling is used when it also fits the
+// partial sums (wg_tf32x3_workspace_bytes_sk), whole tiles otherwise.
 wg_status wg_sgemm_tf32x3(wg_device *dev, int transA, int transB, int64_t m, int64_t n,
                           int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                          int64_t ldb, float beta, float *C, int64_t ldc, void *ws);
+                          int64_t ldb, float beta, float *C, int64_t ldc, void *ws, size_t ws_bytes);
 // The same, for one column panel of a larger product: pack_a = false reuses the
 // op(A) split left in `ws` by an earlier panel of the same m x k operand, and all
 // panels of one product share `epoch` (wg_next_epoch) so a flagged operand sends
 // that panel and every later one to the FFMA kernel.
 wg_status wg_sgemm_tf32x3_panel(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
                                 float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
-                                float *C, int64_t ldc, void *ws, bool pack_a, uint32_t epoch);
+                                float *C, int64_t ldc, void *ws, size_t ws_bytes, bool pack_a, uint32_t epoch);
 uint32_t wg_next_epoch(wg_device *dev);

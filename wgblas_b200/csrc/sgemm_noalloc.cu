@@ -87,5 +87,6 @@ extern "C" wg_status wg_sgemm_noalloc(wg_device *d, int transA, int transB, int6
   void *ws = nullptr;
   wg_status st = scratch_address(d->ordinal, &ws);
   if (st != WG_OK) return st;
-  return wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws);
+  // Whole-tile scheduling: the fixed array holds the split operands only.
+  return wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, need);
 }

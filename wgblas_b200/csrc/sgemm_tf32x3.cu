@@ -15,11 +15,23 @@
 //     and flags (dwords[WG_DW_FALLBACK] = epoch) any element that is not finite
 //     or whose magnitude lies outside [2^-50, 2^50] — there the split loses its
 //     accuracy (subnormal lo parts) or IEEE semantics (Inf*0 in a cross term).
-//  2. tf32x3_mma: one 128 x BN tile of C per CTA; warp 0 streams the four
-//     operand tiles of each k-block into a STAGES-deep shared-memory ring with
-//     TMA (no multicast), warp 1 issues three tcgen05.mma.kind::tf32 per 8-wide
-//     k step into a TMEM accumulator, warps 2-5 read TMEM with tcgen05.ld and
-//     store C column by column (32 rows = 128 contiguous bytes per warp store).
+//  2. tf32x3_mma: a persistent grid, one CTA per SM, over 128 x BN tiles of C.
+//     Warp 0 streams the four operand tiles of each k-block into a
+//     STAGES-deep shared-memory ring with TMA (no multicast); warp 1 issues
+//     three tcgen05.mma.kind::tf32 per 8-wide k step into one of two TMEM
+//     accumulators; warps 2-5 read the other accumulator with tcgen05.ld and
+//     store C column by column (32 rows = 128 contiguous bytes per warp store),
+//     so a tile's epilogue overlaps the next tile's main loop. Tiles are
+//     visited in groups of GROUP_M tile rows for L2 reuse.
+//     Work split: whole tiles round-robin (c, c+G, ...) for every full wave,
+//     which keeps the SMs on neighbouring tiles for L2 reuse; the leftover
+//     tiles of a partial last wave are cut into s equal k-segments when that
+//     shortens the wave (plan_of), and the segments are dealt out so CTAs
+//     running together share a k range. A split tile is finished by whichever
+//     segment arrives last (a per-tile atomic counter): the others leave their
+//     fp32 partial sums in the workspace, and the last adds all segments in k
+//     order — no CTA ever waits for another, and the result does not depend
+//     on arrival order. Without room for the partial sums all tiles go whole.
 //     If the flag carries this call's epoch the kernel exits at once, and the
 //     FFMA kernel launched after it (gated on the same epoch) computes C.
 #include <cuda.h>
@@ -82,8 +94,12 @@ struct PackArgs {
 // whichever dimension the source stores contiguously (through shared memory
 // when that is the row dimension).
 __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64_t k, int64_t kp,
-                                                   int64_t tiles_a, unsigned *dwords, uint32_t epoch) {
+                                                   int64_t tiles_a, unsigned *dwords, uint32_t epoch,
+                                                   unsigned *counters, int64_t n_counters) {
   __shared__ float tile[32][33];
+  // The stream-K tile counters of the MMA launch that follows start at zero.
+  if (blockIdx.x == 0)
+    for (int64_t i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
   const bool is_a = blockIdx.x < tiles_a;
   const PackArgs &P = is_a ? a : b;
   const int64_t t = is_a ? blockIdx.x : blockIdx.x - tiles_a;
@@ -121,6 +137,10 @@ __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64
   if (__any_sync(0xffffffffu, bad) && tx == 0) *(volatile unsigned *)(dwords + WG_DW_FALLBACK) = epoch;
 }
 
+
+constexpr int GROUP_M = 16;  // tile rows per rasterization group
+constexpr int MAX_SEG = 16;  // most k-segments one tile is split into
+
 struct MmaArgs {
   int64_t m, n, k;
   float alpha, beta;
@@ -128,7 +148,77 @@ struct MmaArgs {
   int64_t ldc;
   unsigned *dwords;
   uint32_t epoch;
+  int tiles_m, tiles_n, kt;  // tile grid and k-blocks per tile
+  int dp_tiles;              // tiles [0, dp_tiles) are taken whole, round-robin over the grid
+  int sk_tiles;              // the remaining tiles, each split into sk_split k-segments
+  int sk_split;
+  float *partials;           // split tiles: [sk_tiles * sk_split][BN][BM] partial sums
+  unsigned *counters;        // split tiles: one arrival counter each
 };
+
+// Tile t -> (tile row, tile column), GROUP_M tile rows at a time.
+__device__ __forceinline__ void raster(const MmaArgs &a, int t, int &tm, int &tn) {
+  const int per_group = GROUP_M * a.tiles_n;
+  const int g = t / per_group, first = g * GROUP_M;
+  const int rows = a.tiles_m - first < GROUP_M ? a.tiles_m - first : GROUP_M;
+  const int r = t % per_group;
+  tm = first + r % rows;
+  tn = r / rows;
+}
+
+// One unit of work: k-blocks [kb0, kb1) of tile t; for a split tile, its
+// segment `seg` of sk_split (tile index within the split region: t - dp_tiles).
+struct Unit {
+  int t, kb0, kb1, seg;
+};
+
+// Walks this CTA's units in order — whole tiles c, c+G, ... then split units
+// c, c+G, ... — and every role calls it with the same state. Split unit u is
+// segment u / sk_tiles of split tile u % sk_tiles, so CTAs running at the same
+// time work on neighbouring tiles over the same k range.
+struct Units {
+  int t;  // whole-tile cursor
+  int u;  // split-unit cursor
+  __device__ __forceinline__ Units(const MmaArgs &) : t(blockIdx.x), u(blockIdx.x) {}
+  __device__ __forceinline__ bool next(const MmaArgs &a, Unit &x) {
+    if (t < a.dp_tiles) {
+      x.t = t;
+      x.kb0 = 0;
+      x.kb1 = a.kt;
+      x.seg = -1;
+      t += gridDim.x;
+      return true;
+    }
+    if (u >= a.sk_tiles * a.sk_split) return false;
+    const int local = u % a.sk_tiles;
+    x.seg = u / a.sk_tiles;
+    x.t = a.dp_tiles + local;
+    x.kb0 = (int)((int64_t)a.kt * x.seg / a.sk_split);
+    x.kb1 = (int)((int64_t)a.kt * (x.seg + 1) / a.sk_split);
+    u += gridDim.x;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// True on every epilogue thread iff `v` is true on all of them, so a decision to
+// stop is the same for all four warps and no warp is left waiting at epi_bar.
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(wgtc::smem_addr(bar)) : "memory");
+}
 
 template <class S>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -143,20 +233,23 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   uint8_t *smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned ring
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S::STAGES * S::STAGE);
   uint64_t *empty = full + S::STAGES;
-  uint64_t *accum = empty + S::STAGES;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  uint64_t *acc_full = empty + S::STAGES;  // [2]: accumulator b holds a finished unit
+  uint64_t *acc_empty = acc_full + 2;      // [2]: the epilogue has drained accumulator b
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile unsigned *last_flag = reinterpret_cast<volatile unsigned *>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * S::BN;
-  const int nk = (int)((args.k + S::BK - 1) / S::BK);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; s++) {
       wgtc::mbar_init(&full[s], 1);
       wgtc::mbar_init(&empty[s], 1);
     }
-    wgtc::mbar_init(accum, 1);
+    for (int b = 0; b < 2; b++) {
+      wgtc::mbar_init(&acc_full[b], 1);
+      wgtc::mbar_init(&acc_empty[b], 32 * EPI_WARPS);
+    }
     *abort_flag = 0;
     wgtc::fence_barrier_init();
   }
@@ -167,7 +260,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
     wgtc::prefetch_tensormap(&map_blo);
   }
   if (warp == 1) {
-    wgtc::tmem_alloc(tmem_slot, S::TMEM_COLS);
+    wgtc::tmem_alloc(tmem_slot, 2 * S::TMEM_COLS);  // two accumulators
     wgtc::tmem_relinquish();
   }
   wgtc::tc_fence_before();
@@ -176,89 +269,183 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer ----
-    int issued = 0;
-    for (int kb = 0; kb < nk; kb++) {
-      const int s = kb % S::STAGES;
-      const uint32_t ph = (uint32_t)(kb / S::STAGES) & 1u;
-      if (!wgtc::mbar_wait_bounded(&empty[s], ph ^ 1u, WAIT_BUDGET) || *abort_flag) {
-        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
-        *abort_flag = 1;
-        break;
+    // ---- TMA producer: one continuous ring across this CTA's units ----
+    Units it(args);
+    Unit u;
+    int64_t g = 0;
+    bool ok = true;
+    while (ok && it.next(args, u)) {
+      int tm, tn;
+      raster(args, u.t, tm, tn);
+      for (int kb = u.kb0; kb < u.kb1; kb++, g++) {
+        const int s = (int)(g % S::STAGES);
+        const uint32_t ph = (uint32_t)(g / S::STAGES) & 1u;
+        if (!wgtc::mbar_wait_bounded(&empty[s], ph ^ 1u, WAIT_BUDGET) || *abort_flag) {
+          atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        uint8_t *st = smem + (size_t)s * S::STAGE;
+        wgtc::mbar_arrive_expect_tx(&full[s], S::STAGE);
+        const int kc = kb * S::BK;
+        wgtc::tma_load_2d(st, &map_ahi, &full[s], kc, tm * BM);
+        wgtc::tma_load_2d(st + S::A_TILE, &map_alo, &full[s], kc, tm * BM);
+        wgtc::tma_load_2d(st + 2 * S::A_TILE, &map_bhi, &full[s], kc, tn * S::BN);
+        wgtc::tma_load_2d(st + 2 * S::A_TILE + S::B_TILE, &map_blo, &full[s], kc, tn * S::BN);
       }
-      uint8_t *st = smem + (size_t)s * S::STAGE;
-      wgtc::mbar_arrive_expect_tx(&full[s], S::STAGE);
-      const int kc = kb * S::BK;
-      wgtc::tma_load_2d(st, &map_ahi, &full[s], kc, (int)m0);
-      wgtc::tma_load_2d(st + S::A_TILE, &map_alo, &full[s], kc, (int)m0);
-      wgtc::tma_load_2d(st + 2 * S::A_TILE, &map_bhi, &full[s], kc, (int)n0);
-      wgtc::tma_load_2d(st + 2 * S::A_TILE + S::B_TILE, &map_blo, &full[s], kc, (int)n0);
-      issued = kb + 1;
     }
     // Let every copy this thread issued land before the CTA can exit.
-    for (int kb = issued - S::STAGES > 0 ? issued - S::STAGES : 0; kb < issued; kb++)
-      wgtc::mbar_wait_bounded(&full[kb % S::STAGES], (uint32_t)(kb / S::STAGES) & 1u, WAIT_BUDGET);
+    for (int64_t q = g - S::STAGES > 0 ? g - S::STAGES : 0; q < g; q++)
+      wgtc::mbar_wait_bounded(&full[q % S::STAGES], (uint32_t)(q / S::STAGES) & 1u, WAIT_BUDGET);
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     constexpr uint32_t idesc = wgtc::idesc_tf32(BM, S::BN);
+    Units it(args);
+    Unit u;
+    int64_t g = 0;
+    int n_units = 0;
     bool ok = true;
-    for (int kb = 0; kb < nk && ok; kb++) {
-      const int s = kb % S::STAGES;
-      const uint32_t ph = (uint32_t)(kb / S::STAGES) & 1u;
-      if (!wgtc::mbar_wait_bounded(&full[s], ph, WAIT_BUDGET) || *abort_flag) {
-        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+    while (ok && it.next(args, u)) {
+      const int b = n_units & 1;
+      const uint32_t use = (uint32_t)(n_units >> 1);
+      if (!wgtc::mbar_wait_bounded(&acc_empty[b], (use & 1u) ^ 1u, WAIT_BUDGET) || *abort_flag) {
+        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
         *abort_flag = 1;
-        ok = false;
         break;
       }
       wgtc::tc_fence_after();
-      const uint32_t st = wgtc::smem_addr(smem + (size_t)s * S::STAGE);
-      const uint32_t a_hi = st, a_lo = st + S::A_TILE, b_hi = st + 2 * S::A_TILE,
-                     b_lo = st + 2 * S::A_TILE + S::B_TILE;
+      const uint32_t d_tmem = tmem + (uint32_t)(b * S::TMEM_COLS);
+      for (int kb = u.kb0; kb < u.kb1; kb++, g++) {
+        const int s = (int)(g % S::STAGES);
+        const uint32_t ph = (uint32_t)(g / S::STAGES) & 1u;
+        if (!wgtc::mbar_wait_bounded(&full[s], ph, WAIT_BUDGET) || *abort_flag) {
+          atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        wgtc::tc_fence_after();
+        const uint32_t st = wgtc::smem_addr(smem + (size_t)s * S::STAGE);
+        const uint32_t a_hi = st, a_lo = st + S::A_TILE, b_hi = st + 2 * S::A_TILE,
+                       b_lo = st + 2 * S::A_TILE + S::B_TILE;
 #pragma unroll
-      for (int kk = 0; kk < S::BK / 8; kk++) {
-        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle span
-        const uint64_t dah = wgtc::smem_desc_kmajor(a_hi + off, S::ROW_BYTES);
-        const uint64_t dal = wgtc::smem_desc_kmajor(a_lo + off, S::ROW_BYTES);
-        const uint64_t dbh = wgtc::smem_desc_kmajor(b_hi + off, S::ROW_BYTES);
-        const uint64_t dbl = wgtc::smem_desc_kmajor(b_lo + off, S::ROW_BYTES);
-        const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
-        wgtc::mma_tf32(tmem, dal, dbh, idesc, acc0);  // small terms first
-        wgtc::mma_tf32(tmem, dah, dbl, idesc, 1u);
-        wgtc::mma_tf32(tmem, dah, dbh, idesc, 1u);
+        for (int kk = 0; kk < S::BK / 8; kk++) {
+          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle span
+          const uint64_t dah = wgtc::smem_desc_kmajor(a_hi + off, S::ROW_BYTES);
+          const uint64_t dal = wgtc::smem_desc_kmajor(a_lo + off, S::ROW_BYTES);
+          const uint64_t dbh = wgtc::smem_desc_kmajor(b_hi + off, S::ROW_BYTES);
+          const uint64_t dbl = wgtc::smem_desc_kmajor(b_lo + off, S::ROW_BYTES);
+          const uint32_t acc0 = (kb > u.kb0 || kk > 0) ? 1u : 0u;
+          wgtc::mma_tf32(d_tmem, dal, dbh, idesc, acc0);  // small terms first
+          wgtc::mma_tf32(d_tmem, dah, dbl, idesc, 1u);
+          wgtc::mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+        }
+        wgtc::mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
-      wgtc::mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      wgtc::mma_commit(&acc_full[b]);  // accumulator b complete once all its MMAs finish
+      n_units++;
     }
-    wgtc::mma_commit(accum);  // accumulator complete (or abandoned) once all MMAs finish
   } else if (warp >= 2) {
-    // ---- epilogue: TMEM -> registers -> C ----
-    // tcgen05.ld is warp-collective: decide per warp, not per thread.
-    const bool ready = __all_sync(0xffffffffu, wgtc::mbar_wait_bounded(accum, 0, WAIT_BUDGET));
-    if (!ready && lane == 0) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
-    wgtc::tc_fence_after();
-    const bool aborted = __any_sync(0xffffffffu, *abort_flag != 0);
-    if (ready && !aborted) {
-      const int q = warp & 3;  // TMEM lane quarter this warp may access
-      const int64_t row = m0 + q * 32 + lane;
-      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
-      const float alpha = args.alpha, beta = args.beta;
-      for (int c = 0; c < S::BN; c += 32) {
-        uint32_t r[32];
-        wgtc::tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
-        wgtc::tmem_ld_wait();
-        if (row < args.m) {
+    // ---- epilogue: TMEM -> registers -> C (or a partial-sum slot) ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    const float alpha = args.alpha, beta = args.beta;
+    Units it(args);
+    Unit u;
+    int n_units = 0;
+    while (it.next(args, u)) {
+      const int b = n_units & 1;
+      const uint32_t use = (uint32_t)(n_units >> 1);
+      // One decision for all 128 epilogue threads (tcgen05.ld is warp-collective and
+      // the partial-sum path below meets at a named barrier).
+      const bool ready = wgtc::mbar_wait_bounded(&acc_full[b], use & 1u, WAIT_BUDGET);
+      if (!epi_all(ready && *abort_flag == 0)) {
+        if (!ready) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      wgtc::tc_fence_after();
+      int tm, tn;
+      raster(args, u.t, tm, tn);
+      const int64_t row = (int64_t)tm * BM + row_in_tile;
+      const int64_t n0 = (int64_t)tn * S::BN;
+      const uint32_t trow = tmem + (uint32_t)(b * S::TMEM_COLS) + ((uint32_t)(q * 32) << 16);
+      const bool whole = u.seg < 0;
+      bool finish = whole;
+      const int local = u.t - args.dp_tiles;
+      if (!whole) {
+        // Leave this segment's partial sums, then count arrivals on the tile.
+        float *part = args.partials + ((int64_t)local * args.sk_split + u.seg) * S::BN * BM + row_in_tile;
+        for (int c = 0; c < S::BN; c += 32) {
+          uint32_t r[32];
+          wgtc::tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
+          wgtc::tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int64_t col = n0 + c + j;
-            if (col < args.n) {
-              float *cp = args.C + row + col * args.ldc;
-              const float acc = __uint_as_float(r[j]);
-              const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc);
-              *cp = (beta != 0.0f) ? __fmaf_rn(beta, *cp, s) : s;
+          for (int j = 0; j < 32; j++) part[(int64_t)(c + j) * BM] = __uint_as_float(r[j]);
+        }
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const unsigned prev = atomicAdd(args.counters + local, 1u);
+          const bool last = prev == (unsigned)(args.sk_split - 1);
+          if (last) args.counters[local] = 0;  // ready for the next call on this workspace
+          *last_flag = last ? 1u : 0u;
+          __threadfence();
+        }
+        epi_bar();
+        finish = *last_flag != 0;
+        if (finish) __threadfence();  // order the reads of the other segments' partial sums
+      }
+      if (finish) {
+        // Segments of this tile in k order; this CTA's own comes from TMEM. Each
+        // segment's 32 columns of a chunk are loaded together (independent loads),
+        // so the sum pays one L2 round trip per segment per chunk.
+        const int nseg = whole ? 1 : args.sk_split;
+        const int own = whole ? 0 : u.seg;
+        const float *part0 = whole ? nullptr
+                                   : args.partials + (int64_t)local * args.sk_split * S::BN * BM + row_in_tile;
+        for (int c = 0; c < S::BN; c += 32) {
+          uint32_t r[32];
+          wgtc::tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
+          wgtc::tmem_ld_wait();
+          float acc[32];
+#pragma unroll
+          for (int j = 0; j < 32; j++) acc[j] = __uint_as_float(r[j]);
+          if (nseg > 1) {
+            float sum[32];
+            for (int sgi = 0; sgi < nseg; sgi++) {
+              float v[32];
+              if (sgi == own) {
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = acc[j];
+              } else {
+                const float *p = part0 + ((int64_t)sgi * S::BN + c) * BM;
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = __ldcg(p + (int64_t)j * BM);
+              }
+#pragma unroll
+              for (int j = 0; j < 32; j++) sum[j] = sgi == 0 ? v[j] : sum[j] + v[j];
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j++) acc[j] = sum[j];
+          }
+          if (row < args.m) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const int64_t col = n0 + c + j;
+              if (col < args.n) {
+                float *cp = args.C + row + col * args.ldc;
+                const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc[j]);
+                *cp = (beta != 0.0f) ? __fmaf_rn(beta, *cp, s) : s;
+              }
             }
           }
         }
       }
+      wgtc::tc_fence_before();
+      mbar_arrive(&acc_empty[b]);  // accumulator b may be refilled
+      n_units++;
     }
   }
 
@@ -267,10 +454,11 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   if (warp == 1) {
     __syncwarp();
     wgtc::tc_fence_after();
-    wgtc::tmem_dealloc(tmem, S::TMEM_COLS);
+    wgtc::tmem_dealloc(tmem, 2 * S::TMEM_COLS);
   }
 }
 
+// ---- host side ------------------------------------------------------------
 // ---- host side ------------------------------------------------------------
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -304,7 +492,8 @@ bool make_map(CUtensorMap *map, float *ptr, int64_t rows, int64_t kp, int box_ro
 
 struct Layout {
   int64_t mp, np, kp;
-  size_t a_bytes, b_bytes, total;
+  size_t a_bytes, b_bytes, operands;  // split operands
+  int tiles_m, tiles_n, kt;
 };
 
 Layout layout_of(int64_t m, int64_t n, int64_t k) {
@@ -314,30 +503,93 @@ Layout layout_of(int64_t m, int64_t n, int64_t k) {
   L.kp = (k + 31) / 32 * 32;  // the pack kernel's tile; a multiple of BK
   L.a_bytes = (size_t)L.mp * L.kp * sizeof(float);
   L.b_bytes = (size_t)L.np * L.kp * sizeof(float);
-  L.total = 2 * L.a_bytes + 2 * L.b_bytes;
+  L.operands = 2 * L.a_bytes + 2 * L.b_bytes;
+  L.tiles_m = (int)(L.mp / BM);
+  L.tiles_n = (int)(L.np / Sh::BN);
+  L.kt = (int)(L.kp / Sh::BK);
   return L;
+}
+
+// How a call's tiles are spread over the persistent grid.
+struct Plan {
+  int grid;      // CTAs (at most one per SM)
+  int dp_tiles;  // tiles taken whole, round-robin
+  int sk_tiles;  // tiles split into sk_split k-segments
+  int sk_split;
+};
+
+// Whole tiles for every full wave; the rem = T mod G leftover tiles are split
+// into s k-segments when that shortens the last wave. The last wave costs
+// ceil(s*rem/G) units of kt/s k-blocks each, plus about 4 k-blocks' time per
+// split unit for writing and re-reading its partial sums; s (at most kt/4 and
+// MAX_SEG) minimises that, and s = 1 keeps the tiles whole.
+Plan plan_of(const wg_device *d, const Layout &L, bool allow_split) {
+  const int T = L.tiles_m * L.tiles_n, G = d->sm_count;
+  Plan p;
+  p.grid = T < G ? T : G;
+  p.dp_tiles = T;
+  p.sk_tiles = 0;
+  p.sk_split = 1;
+  const int rem = T % G;
+  if (!allow_split || rem == 0) return p;
+  const int smax = L.kt / 4 < MAX_SEG ? L.kt / 4 : MAX_SEG;
+  int best_s = 1;
+  double best = (double)L.kt;
+  for (int s = 2; s <= smax; s++) {
+    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s + 4.0);
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  if (best_s == 1) return p;
+  p.dp_tiles = T - rem;
+  p.sk_tiles = rem;
+  p.sk_split = best_s;
+  const int units = rem * best_s;
+  p.grid = T - rem >= G ? G : (units < G ? units : G);
+  return p;
+}
+
+// Scratch after the split operands: the partial sums and counters of the split tiles.
+size_t sk_bytes(const Plan &p) {
+  return (size_t)p.sk_tiles * p.sk_split * BM * Sh::BN * sizeof(float) + (size_t)p.sk_tiles * sizeof(unsigned) +
+         256;
 }
 
 }  // namespace
 
-size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) { return layout_of(m, n, k).total; }
+size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) { return layout_of(m, n, k).operands; }
+
+size_t wg_tf32x3_workspace_bytes_sk(const wg_device *d, int64_t m, int64_t n, int64_t k) {
+  const Layout L = layout_of(m, n, k);
+  return L.operands + sk_bytes(plan_of(d, L, true));
+}
 
 bool wg_tf32x3_supported(const wg_device *d, int64_t m, int64_t n, int64_t k) {
   if (d->cc_major != 10 || k < 8 || !encode_fn()) return false;
   const Layout L = layout_of(m, n, k);
-  // TMA coordinates are 32-bit and the K extent's byte stride must fit the map.
+  // TMA coordinates are 32-bit; tile and iteration counts stay in int range.
   return L.mp < ((int64_t)1 << 31) && L.np < ((int64_t)1 << 31) && L.kp < ((int64_t)1 << 31) &&
-         L.np / Sh::BN <= 65535;
+         (int64_t)L.tiles_m * L.tiles_n < ((int64_t)1 << 30);
 }
 
 wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                                 float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
-                                float *C, int64_t ldc, void *ws, bool pack_a, uint32_t epoch) {
+                                float *C, int64_t ldc, void *ws, size_t ws_bytes, bool pack_a, uint32_t epoch) {
   const Layout L = layout_of(m, n, k);
   float *ahi = static_cast<float *>(ws);
   float *alo = ahi + L.a_bytes / sizeof(float);
   float *bhi = alo + L.a_bytes / sizeof(float);
   float *blo = bhi + L.b_bytes / sizeof(float);
+  // Split the last wave's tiles when the workspace has room for their partial sums.
+  Plan plan = plan_of(d, L, true);
+  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(d, L, false);
+  const bool split = plan.sk_tiles > 0;
+  const int grid = plan.grid;
+  float *partials = split ? reinterpret_cast<float *>(static_cast<char *>(ws) + L.operands) : nullptr;
+  unsigned *counters =
+      split ? reinterpret_cast<unsigned *>(partials + (size_t)plan.sk_tiles * plan.sk_split * BM * Sh::BN) : nullptr;
 
   // op(A)(i, p): K-contiguous when transA (A[p + i*lda]); op(B)(p, j) as row j of
   // the N x K operand: K-contiguous when !transB (B[p + j*ldb]).
@@ -346,7 +598,8 @@ wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m,
   const int64_t blocks = pa.tiles_r + pb.tiles_r;
   {
     wg_launch_scope scope(d, "sgemm_tf32x3_pack");
-    tf32x3_pack<<<(unsigned)blocks, 256, 0, d->stream>>>(pa, pb, k, L.kp, pa.tiles_r, d->dwords, epoch);
+    tf32x3_pack<<<(unsigned)blocks, 256, 0, d->stream>>>(pa, pb, k, L.kp, pa.tiles_r, d->dwords, epoch, counters,
+                                                         split ? (int64_t)plan.sk_tiles : 0);
     WG_CUDA(cudaGetLastError());
   }
 
@@ -354,10 +607,10 @@ wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m,
   if (!make_map(&maps[0], ahi, L.mp, L.kp, BM) || !make_map(&maps[1], alo, L.mp, L.kp, BM) ||
       !make_map(&maps[2], bhi, L.np, L.kp, Sh::BN) || !make_map(&maps[3], blo, L.np, L.kp, Sh::BN))
     return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
-  MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, epoch};
+  MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, epoch, L.tiles_m, L.tiles_n, L.kt, plan.dp_tiles,
+               plan.sk_tiles, plan.sk_split, partials, counters};
   auto kern = tf32x3_mma<Sh>;
   WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
-  dim3 grid((unsigned)(L.mp / BM), (unsigned)(L.np / Sh::BN));
   {
     wg_launch_scope scope(d, "sgemm_tf32x3_mma");
     kern<<<grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
@@ -379,7 +632,7 @@ uint32_t wg_next_epoch(wg_device *d) {
 
 wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
                           const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C,
-                          int64_t ldc, void *ws) {
-  return wg_sgemm_tf32x3_panel(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, true,
+                          int64_t ldc, void *ws, size_t ws_bytes) {
+  return wg_sgemm_tf32x3_panel(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, ws_bytes, true,
                                wg_next_epoch(d));
 }

@@ -148,11 +148,13 @@ wg_status panel_gemm<float>(wg_device *d, bool first, uint32_t epoch, int transA
   if (!tc) return wg_gemm_enqueue<float>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
   void *ws = nullptr;
   // Sized for the widest panel so every panel of the product fits the same layout.
-  wg_status st = wg_workspace(d, wg_tf32x3_workspace_bytes(m, panel < n_total ? panel : n_total, k), &ws);
+  const size_t bytes = wg_tf32x3_workspace_bytes_sk(d, m, panel < n_total ? panel : n_total, k);
+  wg_status st = wg_workspace(d, bytes, &ws);
   if (st != WG_OK) return st;
   d->stats.calls++;
   d->stats.tf32x3_launches++;
-  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, first, epoch);
+  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes, first,
+                               epoch);
 }
 
 template <typename T>
