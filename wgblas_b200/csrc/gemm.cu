@@ -8,6 +8,7 @@
 // column-major frame so that a C caller gets WG_ERR_INVALID_ARGUMENT instead of
 // an out-of-bounds access.
 #include <cstring>
+#include <vector>
 
 #include "internal.h"
 
@@ -207,7 +208,7 @@ wg_status gemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, i
 }
 
 // Copies the rows x cols block of a column-major host matrix (leading dimension
-// ld) into a dense device matrix, or back.
+// ld) into a dense device matrix.
 template <typename T>
 cudaError_t h2d_block(T *dst, const T *src, int64_t ld, Stored s, cudaStream_t st) {
   if (s.rows == 0 || s.cols == 0) return cudaSuccess;
@@ -215,6 +216,32 @@ cudaError_t h2d_block(T *dst, const T *src, int64_t ld, Stored s, cudaStream_t s
                            cudaMemcpyHostToDevice, st);
 }
 
+// Panel width of the host-array path: wide enough that each panel's GEMM is
+// efficient, narrow enough that the upload, the GEMM and the read-back of
+// consecutive panels overlap.
+int64_t host_panel_cols(int64_t m, int64_t n, int64_t k) {
+  const double flops = 2.0 * (double)m * (double)n * (double)k;
+  if (flops < 2e9 || n < 512) return n;  // too small to be worth splitting
+  int64_t p = (n + 3) / 4;
+  p = (p + 255) / 256 * 256;
+  return p < n ? p : n;
+}
+
+struct HostPipe {
+  cudaEvent_t ev_a = nullptr;  // op(A) on the device
+  std::vector<cudaEvent_t> ev_b, ev_c;
+  ~HostPipe() {
+    if (ev_a) cudaEventDestroy(ev_a);
+    for (cudaEvent_t e : ev_b) cudaEventDestroy(e);
+    for (cudaEvent_t e : ev_c) cudaEventDestroy(e);
+  }
+};
+
+// The typed-array path: op(A) is uploaded once; op(B) (and C when beta != 0)
+// is uploaded in column panels on a copy stream, each panel's GEMM starts when
+// its panel has arrived, and each finished panel of C is read back on a second
+// copy stream while the next one uploads and computes. Page-locked host arrays
+// make all three overlap.
 template <typename T>
 wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                     const T *A, int64_t lda, const T *B, int64_t ldb, T beta, const T *C_in, T *C_out,
@@ -238,33 +265,79 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   st = check_arch(d);
   if (st != WG_OK) return st;
   wg_device_guard guard(d->ordinal);
+  if (!d->h2d) WG_CUDA(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
+  if (!d->d2h) WG_CUDA(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
   cudaStream_t s = d->stream;
   const Stored sa = stored_a(transA, m, k), sb = stored_b(transB, n, k);
   const size_t na = reads_ab ? (size_t)(sa.rows * sa.cols) : 0;
   const size_t nb = reads_ab ? (size_t)(sb.rows * sb.cols) : 0;
   const size_t nc = (size_t)(m * n);
+  const int64_t lda_d = sa.rows > 0 ? sa.rows : 1, ldb_d = sb.rows > 0 ? sb.rows : 1;
+  const int64_t panel = reads_ab ? host_panel_cols(m, n, k) : n;
+  const int64_t panels = (n + panel - 1) / panel;
+  HostPipe pipe;
   T *dA = nullptr, *dB = nullptr, *dC = nullptr;
+  cudaError_t e = cudaSuccess;
   // Stream-ordered temporaries from the device's memory pool, released in
   // stream order like the reference's `finally` (src/sgemm/sgemm.mjs:263-268).
-  cudaError_t e = cudaMallocAsync((void **)&dC, nc * sizeof(T), s);
+  e = cudaMallocAsync((void **)&dC, nc * sizeof(T), s);
   if (e == cudaSuccess && na) e = cudaMallocAsync((void **)&dA, na * sizeof(T), s);
   if (e == cudaSuccess && nb) e = cudaMallocAsync((void **)&dB, nb * sizeof(T), s);
-  if (e == cudaSuccess && na) e = h2d_block(dA, A, lda, sa, s);
-  if (e == cudaSuccess && nb) e = h2d_block(dB, B, ldb, sb, s);
-  if (e == cudaSuccess && reads_c) e = h2d_block(dC, C_in, ldc, Stored{m, n}, s);
-  if (e == cudaSuccess) {
-    st = gemm_timed<T>(d, transA, transB, m, n, k, alpha, dA, sa.rows > 0 ? sa.rows : 1, dB,
-                       sb.rows > 0 ? sb.rows : 1, beta, dC, m, gpu_ms);
-    if (st == WG_OK)
-      e = cudaMemcpy2DAsync(C_out, ldc * sizeof(T), dC, m * sizeof(T), m * sizeof(T), n,
-                            cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&pipe.ev_a, cudaEventDisableTiming);
+  for (int64_t j = 0; e == cudaSuccess && j < panels; j++) {
+    cudaEvent_t eb = nullptr, ec = nullptr;
+    e = cudaEventCreateWithFlags(&eb, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ec, cudaEventDisableTiming);
+    pipe.ev_b.push_back(eb);
+    pipe.ev_c.push_back(ec);
   }
+  // The copy streams start after the allocations (made on the compute stream).
+  if (e == cudaSuccess) e = cudaEventRecord(pipe.ev_a, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(d->h2d, pipe.ev_a, 0);
+  if (e == cudaSuccess && na) e = h2d_block(dA, A, lda, sa, d->h2d);
+  if (e == cudaSuccess) e = cudaEventRecord(pipe.ev_a, d->h2d);
+  for (int64_t j = 0; e == cudaSuccess && j < panels; j++) {
+    const int64_t j0 = j * panel, cols = n - j0 < panel ? n - j0 : panel;
+    if (nb) {
+      if (transB)  // rows j0.. of the n x k stored B
+        e = cudaMemcpy2DAsync(dB + j0, ldb_d * sizeof(T), B + j0, ldb * sizeof(T), cols * sizeof(T), k,
+                              cudaMemcpyHostToDevice, d->h2d);
+      else         // columns j0.. of the k x n stored B
+        e = h2d_block(dB + j0 * ldb_d, B + j0 * ldb, ldb, Stored{k, cols}, d->h2d);
+    }
+    if (e == cudaSuccess && reads_c) e = h2d_block(dC + j0 * m, C_in + j0 * ldc, ldc, Stored{m, cols}, d->h2d);
+    if (e == cudaSuccess) e = cudaEventRecord(pipe.ev_b[j], d->h2d);
+  }
+  const bool timing = gpu_ms && (d->flags & WG_DEVICE_TIMING);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, pipe.ev_a, 0);
+  if (e == cudaSuccess && timing) e = cudaEventRecord(d->ev_start, s);
+  const uint32_t epoch = wg_next_epoch(d);
+  for (int64_t j = 0; e == cudaSuccess && j < panels; j++) {
+    const int64_t j0 = j * panel, cols = n - j0 < panel ? n - j0 : panel;
+    e = cudaStreamWaitEvent(s, pipe.ev_b[j], 0);
+    if (e != cudaSuccess) break;
+    const T *bp = dB ? (transB ? dB + j0 : dB + j0 * ldb_d) : nullptr;
+    st = panels == 1 ? gemm_launch<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta, dC, m)
+                     : wg_gemm_panel<T>(d, j == 0, epoch, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d,
+                                        beta, dC + j0 * m, m, n, panel);
+    if (st != WG_OK) break;
+    e = cudaEventRecord(pipe.ev_c[j], s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->d2h, pipe.ev_c[j], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(C_out + j0 * ldc, ldc * sizeof(T), dC + j0 * m, m * sizeof(T), m * sizeof(T), cols,
+                            cudaMemcpyDeviceToHost, d->d2h);
+  }
+  if (e == cudaSuccess && st == WG_OK && timing) e = cudaEventRecord(d->ev_stop, s);
+  // The temporaries are released once the last read-back has finished.
+  cudaEvent_t done = panels ? pipe.ev_c[panels - 1] : pipe.ev_a;
+  if (cudaEventRecord(done, d->d2h) == cudaSuccess) cudaStreamWaitEvent(s, done, 0);
   if (dA) cudaFreeAsync(dA, s);
   if (dB) cudaFreeAsync(dB, s);
   if (dC) cudaFreeAsync(dC, s);
   cudaError_t e2 = cudaStreamSynchronize(s);
   if (st != WG_OK) return st;
   if (e == cudaSuccess) e = e2;
+  if (e == cudaSuccess && timing) e = cudaEventElapsedTime(gpu_ms, d->ev_start, d->ev_stop);
   if (e != cudaSuccess)
     return wg_fail(e == cudaErrorMemoryAllocation ? WG_ERR_OUT_OF_MEMORY : WG_ERR_CUDA,
                    "host-array GEMM failed: %s", cudaGetErrorString(e));
@@ -272,6 +345,38 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
 }
 
 }  // namespace
+
+// One panel's GEMM. sgemm panels on the 3xTF32 path split op(A) once (first
+// panel) and only the B panel afterwards; everything else goes through the
+// dispatcher.
+template <typename T>
+wg_status wg_gemm_panel(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
+                     int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
+                     int64_t n_total, int64_t panel) {
+  return wg_gemm_enqueue<T>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+template <>
+wg_status wg_gemm_panel<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
+                            int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
+                            int64_t ldb, float beta, float *C, int64_t ldc, int64_t n_total, int64_t panel) {
+  const bool tc = d->sgemm_path != WG_SGEMM_SIMT && alpha != 0.0f && k >= 64 &&
+                  wg_tf32x3_supported(d, m, panel < n_total ? panel : n_total, k);
+  if (!tc) return wg_gemm_enqueue<float>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
+  void *ws = nullptr;
+  // Sized for the widest panel so every panel of the product fits the same layout.
+  const size_t bytes = wg_tf32x3_workspace_bytes_sk(d, m, panel < n_total ? panel : n_total, k);
+  wg_status st = wg_workspace(d, bytes, &ws);
+  if (st != WG_OK) return st;
+  d->stats.calls++;
+  d->stats.tf32x3_launches++;
+  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes, first,
+                               epoch);
+}
+
+template wg_status wg_gemm_panel<double>(wg_device *, bool, uint32_t, int, int, int64_t, int64_t, int64_t, double,
+                                         const double *, int64_t, const double *, int64_t, double, double *, int64_t,
+                                         int64_t, int64_t);
 
 template wg_status wg_gemm_enqueue<float>(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *,
                                           int64_t, const float *, int64_t, float, float *, int64_t);

@@ -39,6 +39,7 @@ struct wg_device {
   uint32_t epoch;    // sgemm call counter, tags WG_DW_FALLBACK
   int sgemm_path;
   int dgemm_path;
+  cudaStream_t h2d, d2h;  // copy streams of the host-array path (created on first use)
   wg_sgemm_stats stats;
   uint64_t launches;  // kernels launched on this handle
   // profiling: event pairs waiting to be summed, and per-family totals
@@ -96,6 +97,19 @@ struct wg_device_guard {
 template <typename T>
 wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                           const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+
+// One column panel (cols of n_total columns, panels `panel` wide) of a product
+// queued panel by panel on d->stream. sgemm panels on the 3xTF32 path split
+// op(A) only for the first panel (first = true) and share `epoch`
+// (wg_next_epoch) across the product; other calls go through the dispatcher.
+template <typename T>
+wg_status wg_gemm_panel(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
+                        int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
+                        int64_t n_total, int64_t panel);
+template <>
+wg_status wg_gemm_panel<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
+                               int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
+                               int64_t ldb, float beta, float *C, int64_t ldc, int64_t n_total, int64_t panel);
 
 // Returns at least `bytes` of device scratch owned by the handle (stream-ordered reuse).
 wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);

@@ -102,6 +102,8 @@ extern "C" wg_status wg_device_close(wg_device *d) {
     cudaEventDestroy(p.e1);
   }
   for (cudaEvent_t e : d->event_pool) cudaEventDestroy(e);
+  if (d->h2d) cudaStreamDestroy(d->h2d);
+  if (d->d2h) cudaStreamDestroy(d->d2h);
   cudaStreamDestroy(d->own_stream);
   delete d;
   return WG_OK;

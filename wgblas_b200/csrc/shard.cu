@@ -129,34 +129,6 @@ cudaEvent_t panel_event(wg_comm *c, size_t i) {
   return c->ev[i];
 }
 
-// One panel's GEMM. sgemm panels on the 3xTF32 path split op(A) once (first
-// panel) and only the B panel afterwards; everything else goes through the
-// dispatcher.
-template <typename T>
-wg_status panel_gemm(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
-                     int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                     int64_t n_total, int64_t panel) {
-  return wg_gemm_enqueue<T>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
-}
-
-template <>
-wg_status panel_gemm<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
-                            int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                            int64_t ldb, float beta, float *C, int64_t ldc, int64_t n_total, int64_t panel) {
-  const bool tc = d->sgemm_path != WG_SGEMM_SIMT && alpha != 0.0f && k >= 64 &&
-                  wg_tf32x3_supported(d, m, panel < n_total ? panel : n_total, k);
-  if (!tc) return wg_gemm_enqueue<float>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
-  void *ws = nullptr;
-  // Sized for the widest panel so every panel of the product fits the same layout.
-  const size_t bytes = wg_tf32x3_workspace_bytes_sk(d, m, panel < n_total ? panel : n_total, k);
-  wg_status st = wg_workspace(d, bytes, &ws);
-  if (st != WG_OK) return st;
-  d->stats.calls++;
-  d->stats.tf32x3_launches++;
-  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes, first,
-                               epoch);
-}
-
 template <typename T>
 wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n, int64_t k, T alpha, const T *A,
                   int64_t lda, T *B, int64_t ldb, int root, T beta, T *C, int64_t ldc, int64_t panel) {
@@ -193,8 +165,8 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
     WG_CUDA(cudaEventRecord(ev, c->stream));
     WG_CUDA(cudaStreamWaitEvent(d->stream, ev, 0));
     if (m_local > 0) {
-      st = panel_gemm<T>(d, j == 0, epoch, transA, transB, m_local, cols, k, alpha, A, lda, bp, ldb, beta,
-                         C + (transB ? 0 : j0 * ldc), ldc, n, panel);
+      st = wg_gemm_panel<T>(d, j == 0, epoch, transA, transB, m_local, cols, k, alpha, A, lda, bp, ldb, beta,
+                            C + (transB ? 0 : j0 * ldc), ldc, n, panel);
       if (st != WG_OK) return st;
     }
   }
