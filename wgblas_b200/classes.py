@@ -47,10 +47,13 @@ class _Pinned:
         p = ct.c_void_p()
         nat.check(nat.lib.wg_host_alloc(max(nbytes, 1), ct.byref(p)))
         self.ptr = p.value
+        # Held here so the array can still be freed while the interpreter shuts
+        # down and module globals are already cleared.
+        self._free = nat.lib.wg_host_free
 
     def __del__(self):
         if getattr(self, "ptr", None):
-            nat.lib.wg_host_free(ct.c_void_p(self.ptr))
+            self._free(ct.c_void_p(self.ptr))
             self.ptr = None
 
 

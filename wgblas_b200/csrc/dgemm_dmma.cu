@@ -135,8 +135,19 @@ dgemm_dmma_kernel(int64_t m, int64_t n, int64_t k, double alpha, const double *_
     __syncthreads();
   }
 
+  // The 16 old C values of one 16-row slice are loaded before any is written,
+  // so the slice costs one memory round trip rather than one per element.
 #pragma unroll
-  for (int mt = 0; mt < 4; mt++)
+  for (int mt = 0; mt < 4; mt++) {
+    double old[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+      for (int v = 0; v < 4; v++) {
+        const int64_t row = m0 + wm + mt * 16 + g + 8 * (v >> 1);
+        const int64_t col = n0 + wn + nt * 8 + 2 * t + (v & 1);
+        old[nt][v] = (beta != 0.0 && row < m && col < n) ? C[row + col * ldc] : 0.0;
+      }
 #pragma unroll
     for (int nt = 0; nt < 4; nt++)
 #pragma unroll
@@ -144,11 +155,11 @@ dgemm_dmma_kernel(int64_t m, int64_t n, int64_t k, double alpha, const double *_
         const int64_t row = m0 + wm + mt * 16 + g + 8 * (v >> 1);
         const int64_t col = n0 + wn + nt * 8 + 2 * t + (v & 1);
         if (row < m && col < n) {
-          double *cp = C + row + col * ldc;
           const double s = (alpha == 0.0) ? 0.0 : __dmul_rn(alpha, acc[mt][nt][v]);
-          *cp = (beta != 0.0) ? __fma_rn(beta, *cp, s) : s;
+          C[row + col * ldc] = (beta != 0.0) ? __fma_rn(beta, old[nt][v], s) : s;
         }
       }
+  }
 }
 
 template <int TA, int TB>

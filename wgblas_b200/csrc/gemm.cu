@@ -216,6 +216,26 @@ cudaError_t h2d_block(T *dst, const T *src, int64_t ld, Stored s, cudaStream_t s
                            cudaMemcpyHostToDevice, st);
 }
 
+// A memory pool on the device that keeps what it has mapped when its
+// allocations are freed (release threshold = unlimited), so repeated host-array
+// calls reuse device memory instead of mapping and unmapping it every call. It
+// is destroyed, and its memory returned, with the device handle.
+cudaError_t staging_pool(int ordinal, cudaMemPool_t *out) {
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = ordinal;
+  cudaError_t e = cudaMemPoolCreate(out, &props);
+  if (e != cudaSuccess) return e;
+  uint64_t keep = UINT64_MAX;
+  e = cudaMemPoolSetAttribute(*out, cudaMemPoolAttrReleaseThreshold, &keep);
+  if (e != cudaSuccess) {
+    cudaMemPoolDestroy(*out);
+    *out = nullptr;
+  }
+  return e;
+}
+
 // Panel width of the host-array path: wide enough that each panel's GEMM is
 // efficient, narrow enough that the upload, the GEMM and the read-back of
 // consecutive panels overlap.
@@ -267,6 +287,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   wg_device_guard guard(d->ordinal);
   if (!d->h2d) WG_CUDA(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
   if (!d->d2h) WG_CUDA(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+  if (!d->staging) WG_CUDA(staging_pool(d->ordinal, &d->staging));
   cudaStream_t s = d->stream;
   const Stored sa = stored_a(transA, m, k), sb = stored_b(transB, n, k);
   const size_t na = reads_ab ? (size_t)(sa.rows * sa.cols) : 0;
@@ -278,11 +299,12 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   HostPipe pipe;
   T *dA = nullptr, *dB = nullptr, *dC = nullptr;
   cudaError_t e = cudaSuccess;
-  // Stream-ordered temporaries from the device's memory pool, released in
-  // stream order like the reference's `finally` (src/sgemm/sgemm.mjs:263-268).
-  e = cudaMallocAsync((void **)&dC, nc * sizeof(T), s);
-  if (e == cudaSuccess && na) e = cudaMallocAsync((void **)&dA, na * sizeof(T), s);
-  if (e == cudaSuccess && nb) e = cudaMallocAsync((void **)&dB, nb * sizeof(T), s);
+  // Stream-ordered temporaries, released in stream order like the reference's
+  // `finally` (src/sgemm/sgemm.mjs:263-268); the pool keeps the memory mapped
+  // for the next call.
+  e = cudaMallocFromPoolAsync((void **)&dC, nc * sizeof(T), d->staging, s);
+  if (e == cudaSuccess && na) e = cudaMallocFromPoolAsync((void **)&dA, na * sizeof(T), d->staging, s);
+  if (e == cudaSuccess && nb) e = cudaMallocFromPoolAsync((void **)&dB, nb * sizeof(T), d->staging, s);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&pipe.ev_a, cudaEventDisableTiming);
   for (int64_t j = 0; e == cudaSuccess && j < panels; j++) {
     cudaEvent_t eb = nullptr, ec = nullptr;

@@ -40,6 +40,7 @@ struct wg_device {
   int sgemm_path;
   int dgemm_path;
   cudaStream_t h2d, d2h;  // copy streams of the host-array path (created on first use)
+  cudaMemPool_t staging;  // device copies of host-array operands; keeps its memory between calls
   wg_sgemm_stats stats;
   uint64_t launches;  // kernels launched on this handle
   // profiling: event pairs waiting to be summed, and per-family totals

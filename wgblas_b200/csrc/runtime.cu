@@ -104,6 +104,7 @@ extern "C" wg_status wg_device_close(wg_device *d) {
   for (cudaEvent_t e : d->event_pool) cudaEventDestroy(e);
   if (d->h2d) cudaStreamDestroy(d->h2d);
   if (d->d2h) cudaStreamDestroy(d->d2h);
+  if (d->staging) cudaMemPoolDestroy(d->staging);
   cudaStreamDestroy(d->own_stream);
   delete d;
   return WG_OK;

@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64
 
 constexpr int GROUP_M = 16;  // tile rows per rasterization group
 constexpr int MAX_SEG = 16;  // most k-segments one tile is split into
+constexpr int SEG_GROUP = 2; // partial-sum segments the fixup loads at once
 
 struct MmaArgs {
   int64_t m, n, k;
@@ -398,13 +399,16 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
         if (finish) __threadfence();  // order the reads of the other segments' partial sums
       }
       if (finish) {
-        // Segments of this tile in k order; this CTA's own comes from TMEM. Each
-        // segment's 32 columns of a chunk are loaded together (independent loads),
-        // so the sum pays one L2 round trip per segment per chunk.
+        // Segments of this tile in k order; this CTA's own comes from TMEM. The
+        // partial sums of SEG_GROUP segments (32 columns each) are loaded together,
+        // and the 32 old C values of a chunk are loaded before any is written, so a
+        // chunk costs one memory round trip per SEG_GROUP segments (plus one for C)
+        // instead of one per value.
         const int nseg = whole ? 1 : args.sk_split;
         const int own = whole ? 0 : u.seg;
         const float *part0 = whole ? nullptr
                                    : args.partials + (int64_t)local * args.sk_split * S::BN * BM + row_in_tile;
+        const bool in_rows = row < args.m;
         for (int c = 0; c < S::BN; c += 32) {
           uint32_t r[32];
           wgtc::tmem_ld_32x32b_x32(trow + (uint32_t)c, r);
@@ -414,30 +418,47 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
           for (int j = 0; j < 32; j++) acc[j] = __uint_as_float(r[j]);
           if (nseg > 1) {
             float sum[32];
-            for (int sgi = 0; sgi < nseg; sgi++) {
-              float v[32];
-              if (sgi == own) {
+            for (int g0 = 0; g0 < nseg; g0 += SEG_GROUP) {
+              float v[SEG_GROUP][32];
 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = acc[j];
-              } else {
-                const float *p = part0 + ((int64_t)sgi * S::BN + c) * BM;
+              for (int q = 0; q < SEG_GROUP; q++) {
+                const int sgi = g0 + q;
+                if (sgi < nseg && sgi != own) {
+                  const float *p = part0 + ((int64_t)sgi * S::BN + c) * BM;
 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = __ldcg(p + (int64_t)j * BM);
+                  for (int j = 0; j < 32; j++) v[q][j] = __ldcg(p + (int64_t)j * BM);
+                }
               }
 #pragma unroll
-              for (int j = 0; j < 32; j++) sum[j] = sgi == 0 ? v[j] : sum[j] + v[j];
+              for (int q = 0; q < SEG_GROUP; q++) {
+                const int sgi = g0 + q;
+                if (sgi < nseg) {
+#pragma unroll
+                  for (int j = 0; j < 32; j++) {
+                    const float x = sgi == own ? acc[j] : v[q][j];
+                    sum[j] = sgi == 0 ? x : sum[j] + x;
+                  }
+                }
+              }
             }
 #pragma unroll
             for (int j = 0; j < 32; j++) acc[j] = sum[j];
           }
-          if (row < args.m) {
+          if (in_rows) {
+            float old[32];
+            if (beta != 0.0f) {
+#pragma unroll
+              for (int j = 0; j < 32; j++) {
+                const int64_t col = n0 + c + j;
+                old[j] = col < args.n ? args.C[row + col * args.ldc] : 0.0f;
+              }
+            }
 #pragma unroll
             for (int j = 0; j < 32; j++) {
               const int64_t col = n0 + c + j;
               if (col < args.n) {
-                float *cp = args.C + row + col * args.ldc;
                 const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc[j]);
-                *cp = (beta != 0.0f) ? __fmaf_rn(beta, *cp, s) : s;
+                args.C[row + col * args.ldc] = (beta != 0.0f) ? __fmaf_rn(beta, old[j], s) : s;
               }
             }
           }
@@ -519,10 +540,12 @@ struct Plan {
 };
 
 // Whole tiles for every full wave; the rem = T mod G leftover tiles are split
-// into s k-segments when that shortens the last wave. The last wave costs
-// ceil(s*rem/G) units of kt/s k-blocks each, plus about 4 k-blocks' time per
-// split unit for writing and re-reading its partial sums; s (at most kt/4 and
-// MAX_SEG) minimises that, and s = 1 keeps the tiles whole.
+// into s k-segments when that shortens the last wave. In units of one k-block's
+// MMA time, the last wave costs ceil(s*rem/G) rounds of kt/s k-blocks, plus the
+// fixup: each segment writes a 128 KB partial tile and the last one reads the
+// other s-1 back, about 2 k-blocks' time per 128 KB at one SM's share of L2
+// bandwidth, so 2s + 2 in all. s (at most kt/4 and MAX_SEG) minimises that, and
+// s = 1 keeps the tiles whole.
 Plan plan_of(const wg_device *d, const Layout &L, bool allow_split) {
   const int T = L.tiles_m * L.tiles_n, G = d->sm_count;
   Plan p;
@@ -536,7 +559,7 @@ Plan plan_of(const wg_device *d, const Layout &L, bool allow_split) {
   int best_s = 1;
   double best = (double)L.kt;
   for (int s = 2; s <= smax; s++) {
-    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s + 4.0);
+    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s) + 2.0 * s + 2.0;
     if (cost < best - 1e-9) {
       best = cost;
       best_s = s;
