@@ -20,7 +20,8 @@ A step is one sgemm/dgemm call on operands resident in HBM; L2 is flushed
 (a 512 MB device write) between steps, outside the per-step CUDA events.
 With --gpus N>1 (torchrun) the default workload is shard16384: each rank keeps
 its row block of A and C resident, and every step broadcasts B from rank 0 in
-2048-column panels, each panel's GEMM overlapping the next panel's transfer;
+column panels (the library's planned widths for sgemm, one panel for dgemm),
+each panel's GEMM overlapping the next panel's transfer;
 value = total FLOPs / max over ranks of the step time (strong scaling).
 
 --impl reference times the reference's arithmetic on the host cores instead:
@@ -59,7 +60,7 @@ WORKLOADS = {
     "shard16384d": dict(routine="dgemm", config_index=4, transA=0, transB=0, m=16384, n=16384, k=16384,
                         lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
 }
-PANEL_COLS = 2048  # B broadcast panel width of the sharded workloads
+PANEL_COLS = 0  # B broadcast panels of the sharded workloads: 0 = the library's plan
 
 
 def flops(w):
@@ -395,11 +396,31 @@ def pick_workload(args, world):
     return args.workload
 
 
+def panel_plan(w, world):
+    """The broadcast panel widths a sharded call uses (its planned widths on the
+    3xTF32 path; a dgemm product is one panel)."""
+    if w["routine"] == "dgemm" or PANEL_COLS:
+        return [w["n"]] if not PANEL_COLS else f"{PANEL_COLS} wide"
+    import ctypes as ct
+
+    sys.path.insert(0, ROOT)
+    from wgblas_b200 import _native as nat
+
+    import torch
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    m_local = -(-w["m"] // world)
+    widths = (ct.c_int64 * 4096)()
+    count = ct.c_size_t()
+    nat.check(nat.lib.wg_sharded_panel_plan(sms, world, m_local, w["n"], w["k"], widths, 4096, ct.byref(count)))
+    return [int(widths[i]) for i in range(count.value)]
+
+
 def config_of(w, name, world=1):
     shard = ""
     if w.get("sharded"):
-        shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 in {PANEL_COLS}-column "
-                 "panels (NCCL over NVLink)")
+        shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 in column panels "
+                 f"{panel_plan(w, world)} (NCCL over NVLink)")
     return {"workload": f"configs[{w['config_index']}] {w['routine']} {w['m']}x{w['n']}x{w['k']} "
                         f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major{shard}",
             "parallelism": f"row-sharded x{world}" if w.get("sharded") else "single GPU",
@@ -515,9 +536,17 @@ def main():
         extra["shard16384d"] = {"tflops": flops(wd) / (md * 1e-3) / 1e12, "ms_per_step": md}
 
     # Roofline of the dominant kernel, from the per-kernel events of the timed region.
+    # Sharded: this rank's share of the product runs as several panel launches per
+    # step, so achieved = the rank's FLOPs per step / the kernel's time per step.
     dom = max(prof.items(), key=lambda kv: kv[1][1]) if prof else ("?", (1, step_ms))
     dom_ms = dom[1][1] / max(dom[1][0], 1)
-    achieved = flops(w) / (dom_ms * 1e-3) / 1e12
+    rank_share = 1.0
+    if w.get("sharded"):
+        from wgblas_b200.shard import plan_rows
+
+        offs = plan_rows(w["m"], world)
+        rank_share = (offs[rank + 1] - offs[rank]) / w["m"]
+    achieved = flops(w) * rank_share / (dom[1][1] / args.steps * 1e-3) / 1e12
     if dom[0].startswith("sgemm_tf32x3"):
         peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) * 0.5 / 3.0
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -535,6 +564,7 @@ def main():
                 "peak_basis": "FMA-chain probe measured in this run (no FP32/FP64 SIMT figure in MEASURED_PEAKS.json)"}
     roof["kernel"] = dom[0]
     roof["kernel_ms"] = dom_ms
+    roof["launches_per_step"] = dom[1][0] / args.steps
     roof["kernels"] = {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in prof.items()}
 
     e2e = time_e2e(wg, dev, w, max(3, args.steps // 2), args.warmup) if (rank == 0 and not w.get("sharded")) else None

@@ -103,6 +103,20 @@ typedef struct wg_sgemm_stats {
 } wg_sgemm_stats;
 wg_status wg_device_sgemm_stats(wg_device *dev, wg_sgemm_stats *stats);
 
+/* How the 3xTF32 tensor-core kernel would divide an m x n x k product among
+ * sm_count SMs: 128 x 256 output tiles, each k_blocks 16-wide k steps; a
+ * persistent grid of `grid` CTAs takes whole_tiles tiles whole and cuts the
+ * remaining split_tiles into split_segments k-segments each (1 = none). Host
+ * arithmetic only: no device is touched. workspace_bytes is the scratch that
+ * plan needs (split operands and partial sums). No counterpart in the
+ * reference; it documents the scheduling for tests and tuning. */
+typedef struct wg_tc_plan {
+  int64_t tiles_m, tiles_n, k_blocks;
+  int grid, whole_tiles, split_tiles, split_segments;
+  size_t workspace_bytes;
+} wg_tc_plan;
+wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_t k, wg_tc_plan *out);
+
 /* sgemm kernel choice: AUTO picks by shape and alignment; the others force one
  * kernel (tests and benchmarks). */
 #define WG_SGEMM_AUTO 0
@@ -217,6 +231,15 @@ wg_status wg_dgemm_host(wg_device *dev, int transA, int transB, int64_t m, int64
                         double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
                         double beta, const double *C_in, double *C_out, int64_t ldc,
                         float *gpu_ms);
+
+/* Column-panel widths wg_sgemm_sharded uses when panel_cols is 0 and the
+ * product runs on the 3xTF32 kernel (alpha != 0, k >= 64, transB = 0): panels
+ * sized so each GEMM fills whole waves of the SMs and the first panel's
+ * broadcast is short. Host arithmetic only; sm_count is the SMs of one GPU.
+ * `count` receives the number of panels even when `capacity` is too small. */
+wg_status wg_sharded_panel_plan(int sm_count, int nranks, int64_t m_local, int64_t n, int64_t k, int64_t *widths,
+                                size_t capacity, size_t *count);
+
 
 /* ---- multi-GPU: C sharded by row blocks, B broadcast over NVLink (NCCL) ---- */
 /* The reference drives several GPUs only as independent devices with no data

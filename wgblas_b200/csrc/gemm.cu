@@ -8,6 +8,7 @@
 // column-major frame so that a C caller gets WG_ERR_INVALID_ARGUMENT instead of
 // an out-of-bounds access.
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include "internal.h"
@@ -296,6 +297,11 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   const int64_t lda_d = sa.rows > 0 ? sa.rows : 1, ldb_d = sb.rows > 0 ? sb.rows : 1;
   const int64_t panel = reads_ab ? host_panel_cols(m, n, k) : n;
   const int64_t panels = (n + panel - 1) / panel;
+  size_t panel_ws = 0;  // > 0: the panels run on the 3xTF32 kernel with this much scratch
+  if (panels > 1 && std::is_same<T, float>::value && wg_sgemm_panel_on_tc(d, (float)alpha, m, panel, k)) {
+    const int64_t widths[2] = {panel, n - (panels - 1) * panel};
+    panel_ws = wg_tf32x3_panels_workspace(d, m, k, widths, 2);
+  }
   HostPipe pipe;
   T *dA = nullptr, *dB = nullptr, *dC = nullptr;
   cudaError_t e = cudaSuccess;
@@ -341,7 +347,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
     const T *bp = dB ? (transB ? dB + j0 : dB + j0 * ldb_d) : nullptr;
     st = panels == 1 ? gemm_launch<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta, dC, m)
                      : wg_gemm_panel<T>(d, j == 0, epoch, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d,
-                                        beta, dC + j0 * m, m, n, panel);
+                                        beta, dC + j0 * m, m, panel_ws);
     if (st != WG_OK) break;
     e = cudaEventRecord(pipe.ev_c[j], s);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->d2h, pipe.ev_c[j], 0);
@@ -368,37 +374,47 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
 
 }  // namespace
 
-// One panel's GEMM. sgemm panels on the 3xTF32 path split op(A) once (first
-// panel) and only the B panel afterwards; everything else goes through the
-// dispatcher.
+// One panel's GEMM. sgemm panels on the 3xTF32 path (ws_bytes > 0) split op(A)
+// once (first panel) and only the B panel afterwards; everything else goes
+// through the dispatcher.
 template <typename T>
 wg_status wg_gemm_panel(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
-                     int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                     int64_t n_total, int64_t panel) {
+                        int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
+                        size_t ws_bytes) {
   return wg_gemm_enqueue<T>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
+}
+
+bool wg_sgemm_panel_on_tc(const wg_device *d, float alpha, int64_t m, int64_t cols, int64_t k) {
+  return d->sgemm_path != WG_SGEMM_SIMT && alpha != 0.0f && k >= 64 && m > 0 && cols > 0 &&
+         wg_tf32x3_supported(d, m, cols, k);
+}
+
+size_t wg_tf32x3_panels_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count) {
+  size_t bytes = 0;
+  for (size_t i = 0; i < count; i++) {
+    const size_t b = wg_tf32x3_workspace_bytes_sk(d, m, widths[i], k);
+    bytes = b > bytes ? b : bytes;
+  }
+  return bytes;
 }
 
 template <>
 wg_status wg_gemm_panel<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
-                            int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                            int64_t ldb, float beta, float *C, int64_t ldc, int64_t n_total, int64_t panel) {
-  const bool tc = d->sgemm_path != WG_SGEMM_SIMT && alpha != 0.0f && k >= 64 &&
-                  wg_tf32x3_supported(d, m, panel < n_total ? panel : n_total, k);
-  if (!tc) return wg_gemm_enqueue<float>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
+                               int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
+                               int64_t ldb, float beta, float *C, int64_t ldc, size_t ws_bytes) {
+  if (ws_bytes == 0) return wg_gemm_enqueue<float>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
   void *ws = nullptr;
-  // Sized for the widest panel so every panel of the product fits the same layout.
-  const size_t bytes = wg_tf32x3_workspace_bytes_sk(d, m, panel < n_total ? panel : n_total, k);
-  wg_status st = wg_workspace(d, bytes, &ws);
+  wg_status st = wg_workspace(d, ws_bytes, &ws);
   if (st != WG_OK) return st;
   d->stats.calls++;
   d->stats.tf32x3_launches++;
-  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes, first,
-                               epoch);
+  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, ws_bytes,
+                               first, epoch);
 }
 
 template wg_status wg_gemm_panel<double>(wg_device *, bool, uint32_t, int, int, int64_t, int64_t, int64_t, double,
                                          const double *, int64_t, const double *, int64_t, double, double *, int64_t,
-                                         int64_t, int64_t);
+                                         size_t);
 
 template wg_status wg_gemm_enqueue<float>(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *,
                                           int64_t, const float *, int64_t, float, float *, int64_t);

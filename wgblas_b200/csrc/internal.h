@@ -30,6 +30,7 @@ struct wg_device {
   cudaStream_t stream;  // the stream work is ordered on (own_stream or the caller's)
   cudaEvent_t ev_start, ev_stop;
   int sm_count;
+  int tc_grid_cap;  // > 0: at most this many CTAs in the 3xTF32 persistent grid
   int cc_major, cc_minor;
   size_t total_mem;
   char name[256];
@@ -99,18 +100,24 @@ template <typename T>
 wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                           const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
 
-// One column panel (cols of n_total columns, panels `panel` wide) of a product
-// queued panel by panel on d->stream. sgemm panels on the 3xTF32 path split
-// op(A) only for the first panel (first = true) and share `epoch`
-// (wg_next_epoch) across the product; other calls go through the dispatcher.
+// One column panel (cols columns) of a product queued panel by panel on
+// d->stream. sgemm panels on the 3xTF32 path split op(A) only for the first
+// panel (first = true), share `epoch` (wg_next_epoch) across the product, and
+// keep their split operands in one workspace of ws_bytes
+// (wg_tf32x3_panels_workspace over all the product's panel widths) so op(A)'s
+// split stays in place; other calls go through the dispatcher.
 template <typename T>
 wg_status wg_gemm_panel(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
                         int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                        int64_t n_total, int64_t panel);
+                        size_t ws_bytes);
 template <>
 wg_status wg_gemm_panel<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
                                int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                               int64_t ldb, float beta, float *C, int64_t ldc, int64_t n_total, int64_t panel);
+                               int64_t ldb, float beta, float *C, int64_t ldc, size_t ws_bytes);
+// True when wg_gemm_panel<float> runs this panel shape on the 3xTF32 kernel.
+bool wg_sgemm_panel_on_tc(const wg_device *d, float alpha, int64_t m, int64_t cols, int64_t k);
+// Scratch for every panel of an m x (sum of widths) x k sgemm on the 3xTF32 path.
+size_t wg_tf32x3_panels_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count);
 
 // Returns at least `bytes` of device scratch owned by the handle (stream-ordered reuse).
 wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);
@@ -140,6 +147,12 @@ cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T bet
 // alone (whole-tile scheduling), or with the stream-K partial sums and counters.
 size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
 size_t wg_tf32x3_workspace_bytes_sk(const wg_device *dev, int64_t m, int64_t n, int64_t k);
+// SMs the 3xTF32 kernel's persistent grid may use on this handle (all of them
+// unless tc_grid_cap holds some back, e.g. for NCCL kernels running alongside).
+int wg_tf32x3_sms(const wg_device *dev);
+// Modelled run time of the 3xTF32 kernel for one m x n x k product on G SMs, in
+// units of one 16-deep k-block of one tile's MMAs (about 0.5 us on B200).
+double wg_tf32x3_cost(int G, int64_t m, int64_t n, int64_t k);
 // True when the 3xTF32 path supports this shape on this device.
 bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 // Splits op(A), op(B) into tf32 hi/lo operands in `ws`, then runs the tcgen05 kernel.

@@ -541,13 +541,14 @@ struct Plan {
 
 // Whole tiles for every full wave; the rem = T mod G leftover tiles are split
 // into s k-segments when that shortens the last wave. In units of one k-block's
-// MMA time, the last wave costs ceil(s*rem/G) rounds of kt/s k-blocks, plus the
-// fixup: each segment writes a 128 KB partial tile and the last one reads the
-// other s-1 back, about 2 k-blocks' time per 128 KB at one SM's share of L2
-// bandwidth, so 2s + 2 in all. s (at most kt/4 and MAX_SEG) minimises that, and
-// s = 1 keeps the tiles whole.
-Plan plan_of(const wg_device *d, const Layout &L, bool allow_split) {
-  const int T = L.tiles_m * L.tiles_n, G = d->sm_count;
+// MMA time (about 0.5 us on B200), the last wave costs ceil(s*rem/G) rounds of
+// kt/s k-blocks, plus the split's overhead: partial-tile writes, the finishing
+// segment's reads of the other s-1 partial tiles at the end of the wave, and the
+// round imbalance. Measured on B200 over s = 2..16 and kt = 64..1024, that
+// overhead is about 28(s-1) + 8 k-blocks. s (at most kt/4 and MAX_SEG) minimises
+// the total, and s = 1 keeps the tiles whole.
+Plan plan_of(int G, const Layout &L, bool allow_split) {
+  const int T = L.tiles_m * L.tiles_n;
   Plan p;
   p.grid = T < G ? T : G;
   p.dp_tiles = T;
@@ -559,7 +560,7 @@ Plan plan_of(const wg_device *d, const Layout &L, bool allow_split) {
   int best_s = 1;
   double best = (double)L.kt;
   for (int s = 2; s <= smax; s++) {
-    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s) + 2.0 * s + 2.0;
+    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s) + 28.0 * (s - 1) + 8.0;
     if (cost < best - 1e-9) {
       best = cost;
       best_s = s;
@@ -584,9 +585,22 @@ size_t sk_bytes(const Plan &p) {
 
 size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) { return layout_of(m, n, k).operands; }
 
+int wg_tf32x3_sms(const wg_device *d) {
+  return d->tc_grid_cap > 0 && d->tc_grid_cap < d->sm_count ? d->tc_grid_cap : d->sm_count;
+}
+
 size_t wg_tf32x3_workspace_bytes_sk(const wg_device *d, int64_t m, int64_t n, int64_t k) {
   const Layout L = layout_of(m, n, k);
-  return L.operands + sk_bytes(plan_of(d, L, true));
+  return L.operands + sk_bytes(plan_of(wg_tf32x3_sms(d), L, true));
+}
+
+double wg_tf32x3_cost(int G, int64_t m, int64_t n, int64_t k) {
+  const Layout L = layout_of(m, n, k);
+  const Plan p = plan_of(G, L, true);
+  if (p.sk_tiles == 0) return (double)((p.dp_tiles + G - 1) / G) * L.kt;  // whole tiles only
+  const int s = p.sk_split;
+  const int64_t rounds = ((int64_t)s * p.sk_tiles + G - 1) / G;
+  return (double)(p.dp_tiles / G) * L.kt + (double)rounds * ((double)L.kt / s) + 28.0 * (s - 1) + 8.0;
 }
 
 bool wg_tf32x3_supported(const wg_device *d, int64_t m, int64_t n, int64_t k) {
@@ -595,6 +609,25 @@ bool wg_tf32x3_supported(const wg_device *d, int64_t m, int64_t n, int64_t k) {
   // TMA coordinates are 32-bit; tile and iteration counts stay in int range.
   return L.mp < ((int64_t)1 << 31) && L.np < ((int64_t)1 << 31) && L.kp < ((int64_t)1 << 31) &&
          (int64_t)L.tiles_m * L.tiles_n < ((int64_t)1 << 30);
+}
+
+extern "C" wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_t k, wg_tc_plan *out) {
+  if (!out) return wg_fail(WG_ERR_INVALID_ARGUMENT, "out is NULL");
+  if (sm_count <= 0 || m <= 0 || n <= 0 || k < 8)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "sm_count, m and n must be positive and k >= 8");
+  const Layout L = layout_of(m, n, k);
+  if ((int64_t)L.tiles_m * L.tiles_n >= ((int64_t)1 << 30))
+    return wg_fail(WG_ERR_NOT_SUPPORTED, "too many tiles");
+  const Plan p = plan_of(sm_count, L, true);
+  out->tiles_m = L.tiles_m;
+  out->tiles_n = L.tiles_n;
+  out->k_blocks = L.kt;
+  out->grid = p.grid;
+  out->whole_tiles = p.dp_tiles;
+  out->split_tiles = p.sk_tiles;
+  out->split_segments = p.sk_split;
+  out->workspace_bytes = L.operands + sk_bytes(p);
+  return WG_OK;
 }
 
 wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
@@ -606,8 +639,8 @@ wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m,
   float *bhi = alo + L.a_bytes / sizeof(float);
   float *blo = bhi + L.b_bytes / sizeof(float);
   // Split the last wave's tiles when the workspace has room for their partial sums.
-  Plan plan = plan_of(d, L, true);
-  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(d, L, false);
+  Plan plan = plan_of(wg_tf32x3_sms(d), L, true);
+  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(wg_tf32x3_sms(d), L, false);
   const bool split = plan.sk_tiles > 0;
   const int grid = plan.grid;
   float *partials = split ? reinterpret_cast<float *>(static_cast<char *>(ws) + L.operands) : nullptr;

@@ -25,6 +25,7 @@
 #include <new>
 #include <mutex>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "internal.h"
@@ -39,6 +40,7 @@ struct NcclApi {
   ncclResult_t (*CommAbort)(ncclComm_t);
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *);
   ncclResult_t (*Broadcast)(const void *, void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
   ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
   ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
   ncclResult_t (*GroupStart)();
@@ -60,6 +62,7 @@ NcclApi *nccl() {
     LOAD(CommAbort, "ncclCommAbort");
     LOAD(CommGetAsyncError, "ncclCommGetAsyncError");
     LOAD(Broadcast, "ncclBroadcast");
+    LOAD(AllReduce, "ncclAllReduce");
     LOAD(Send, "ncclSend");
     LOAD(Recv, "ncclRecv");
     LOAD(GroupStart, "ncclGroupStart");
@@ -67,7 +70,7 @@ NcclApi *nccl() {
     LOAD(GetErrorString, "ncclGetErrorString");
 #undef LOAD
     api.ok = api.GetUniqueId && api.CommInitRankConfig && api.CommDestroy && api.CommAbort &&
-             api.CommGetAsyncError && api.Broadcast && api.Send && api.Recv && api.GroupStart && api.GroupEnd &&
+             api.CommGetAsyncError && api.Broadcast && api.AllReduce && api.Send && api.Recv && api.GroupStart && api.GroupEnd &&
              api.GetErrorString;
   });
   return api.ok ? &api : nullptr;
@@ -85,6 +88,13 @@ struct wg_comm {
   cudaEvent_t done;             // all of the call's work, for bounded waits
   int timeout_ms;
   bool aborted;
+  // Last automatic panel plan, keyed by (n, k): planning a very wide product
+  // is not free, and the ranks must agree on the widths (see agreed_panels).
+  int64_t plan_key[2];
+  std::vector<int64_t> plan_widths;
+  int64_t *agree;       // two device words for the planning all-reduce
+  int64_t *agree_host;  // and their page-locked host copy
+  cudaEvent_t agreed;
 };
 
 namespace {
@@ -113,12 +123,49 @@ wg_status settle(wg_comm *c, ncclResult_t r, const char *what) {
   return WG_OK;
 }
 
+// Waits for `ev` (recorded on the communicator's stream), bounded by the
+// communicator's timeout; aborts the communicator on timeout or an
+// asynchronous NCCL error.
+wg_status wait_event(wg_comm *c, cudaEvent_t ev, const char *what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return WG_OK;
+    if (e != cudaErrorNotReady) return wg_fail(WG_ERR_CUDA, "%s failed: %s", what, cudaGetErrorString(e));
+    ncclResult_t r = ncclSuccess;
+    nccl()->CommGetAsyncError(c->comm, &r);
+    if ((r != ncclSuccess && r != ncclInProgress) ||
+        std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(c->timeout_ms)) {
+      nccl()->CommAbort(c->comm);
+      c->aborted = true;
+      return r != ncclSuccess && r != ncclInProgress
+                 ? nccl_fail(c, r, what)
+                 : wg_fail(WG_ERR_NCCL, "%s did not finish within %d ms on rank %d; communicator aborted", what,
+                           c->timeout_ms, c->rank);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
 template <typename T>
 ncclDataType_t nccl_type();
 template <>
 ncclDataType_t nccl_type<float>() { return ncclFloat; }
 template <>
 ncclDataType_t nccl_type<double>() { return ncclDouble; }
+
+// Frees the communicator's CUDA resources (whichever were created) and the
+// object itself; the NCCL communicator is destroyed or aborted by the caller.
+void release(wg_comm *c) {
+  for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
+  if (c->entry) cudaEventDestroy(c->entry);
+  if (c->done) cudaEventDestroy(c->done);
+  if (c->agreed) cudaEventDestroy(c->agreed);
+  if (c->agree) cudaFree(c->agree);
+  if (c->agree_host) cudaFreeHost(c->agree_host);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
 
 cudaEvent_t panel_event(wg_comm *c, size_t i) {
   while (c->ev.size() <= i) {
@@ -128,6 +175,109 @@ cudaEvent_t panel_event(wg_comm *c, size_t i) {
   }
   return c->ev[i];
 }
+
+// SMs left out of the 3xTF32 persistent grid while a sharded product runs on
+// more than one rank and the broadcast is a large share of the work, so the
+// broadcast of the next panel (an NCCL kernel) finds SMs to run on instead of
+// waiting for the current panel's GEMM to end. Measured on 8 x B200 at
+// 16384^3: 8 reserved SMs gave 5.94 ms per product against 6.23 ms with none
+// (2048 rows per rank); with 4096 or 8192 rows per rank, reserving cost 2-4 %.
+constexpr int kNcclSms = 8;
+
+// True when broadcasting one tile column of B (256 x k at about 400 GB/s) takes
+// more than half as long as this rank's GEMM on it (m_local rows at about
+// 0.5 us per 16-deep k-block of a tile, on G SMs).
+bool reserve_for_nccl(int nranks, int G, int64_t m_local, int64_t k) {
+  if (nranks <= 1 || G <= 2 * kNcclSms) return false;
+  const double bcast = 256.0 * (double)k * 4.0 / 400e9;
+  const double tiles = (double)((m_local + 127) / 128);
+  const double gemm = tiles / G * (double)((k + 31) / 32 * 2) * 0.5e-6;
+  return bcast > 0.5 * gemm;
+}
+
+// Column panels of a sharded sgemm on the 3xTF32 kernel. Panel j's GEMM starts
+// when both the previous panel's GEMM and panel j's broadcast are done; with
+// the broadcast of consecutive panels back to back on the communicator's
+// stream, the end time of the product is a shortest path over the panel
+// boundaries, found here by dynamic programming over 256-column tile columns.
+// Costs are in units of one 16-deep k-block of one tile's MMAs (about 0.5 us):
+// the GEMM from the kernel's own schedule model (wg_tf32x3_cost), the B split
+// at about 5 TB/s (4 bytes read, 8 written per element), about 30 us per panel
+// for its three launches and the pipeline fill and drain, and the broadcast at
+// about 400 GB/s when there is more than one rank. Wave quantisation makes
+// the panel widths matter: 16 tile rows x 9 tile columns fill 144 of 148 SMs,
+// 16 x 8 only 128.
+std::vector<int64_t> plan_panels(int G, int nranks, int64_t m, int64_t n, int64_t k) {
+  constexpr double kb_s = 0.5e-6;
+  constexpr double kPanelFixed = 60.0;
+  const int64_t tc = (n + 255) / 256;
+  const int64_t cmax = tc < 256 ? tc : 256;
+  const double kp = (double)((k + 31) / 32 * 32);
+  const double bcast = nranks > 1 ? 256.0 * (double)k * 4.0 / 400e9 / kb_s : 0.0;  // per tile column
+  const double pack = 256.0 * kp * 12.0 / 5e12 / kb_s;
+  std::vector<double> full(cmax + 1, 0.0);  // GEMM cost of a panel of c whole tile columns
+  for (int64_t c = 1; c <= cmax; c++) full[c] = wg_tf32x3_cost(G, m, c * 256, k);
+  std::vector<double> best(tc + 1, 1e300);
+  std::vector<int64_t> from(tc + 1, 0);
+  best[0] = 0.0;
+  for (int64_t y = 1; y <= tc; y++) {
+    for (int64_t c = 1; c <= cmax && c <= y; c++) {
+      const int64_t x = y - c;
+      const int64_t cols = (y * 256 < n ? y * 256 : n) - x * 256;
+      const double gemm = cols == c * 256 ? full[c] : wg_tf32x3_cost(G, m, cols, k);
+      const double arrive = (double)y * bcast;  // panel [x, y) fully broadcast
+      const double t = (best[x] > arrive ? best[x] : arrive) + (double)c * pack + gemm + kPanelFixed;
+      if (t < best[y]) {
+        best[y] = t;
+        from[y] = x;
+      }
+    }
+  }
+  std::vector<int64_t> widths;
+  for (int64_t y = tc; y > 0; y = from[y]) widths.push_back((y * 256 < n ? y * 256 : n) - from[y] * 256);
+  return std::vector<int64_t>(widths.rbegin(), widths.rend());
+}
+
+// The automatic panel widths of a sharded sgemm. Every rank must broadcast the
+// same panels, so the plan is made only from values all ranks share: n, k and
+// the rank count, plus the largest m_local and the fewest SMs of any rank,
+// agreed by one all-reduce. The plan is cached per (n, k); the ranks make their
+// calls with the same (n, k) sequence, so they take the all-reduce together.
+wg_status agreed_panels(wg_comm *c, int64_t m_local, int64_t n, int64_t k, std::vector<int64_t> &out) {
+  if (!c->plan_widths.empty() && c->plan_key[0] == n && c->plan_key[1] == k) {
+    out = c->plan_widths;
+    return WG_OK;
+  }
+  int64_t m_max = m_local, g_min = wg_tf32x3_sms(c->dev);
+  if (c->nranks > 1) {
+    c->agree_host[0] = m_local;
+    c->agree_host[1] = -g_min;
+    WG_CUDA(cudaMemcpyAsync(c->agree, c->agree_host, 2 * sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
+    wg_status st = settle(c, nccl()->AllReduce(c->agree, c->agree, 2, ncclInt64, ncclMax, c->comm, c->stream),
+                          "ncclAllReduce");
+    if (st != WG_OK) return st;
+    WG_CUDA(cudaMemcpyAsync(c->agree_host, c->agree, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, c->stream));
+    WG_CUDA(cudaEventRecord(c->agreed, c->stream));
+    st = wait_event(c, c->agreed, "panel planning all-reduce");
+    if (st != WG_OK) return st;
+    m_max = c->agree_host[0];
+    g_min = -c->agree_host[1];
+  }
+  c->plan_widths = m_max > 0 && g_min > 0 ? plan_panels((int)g_min, c->nranks, m_max, n, k)
+                                          : std::vector<int64_t>{n};
+  c->plan_key[0] = n;
+  c->plan_key[1] = k;
+  out = c->plan_widths;
+  return WG_OK;
+}
+
+// Restores the device's 3xTF32 grid cap when a sharded call returns.
+struct GridCap {
+  wg_device *d;
+  int saved;
+  GridCap(wg_device *dev, int cap) : d(dev), saved(dev->tc_grid_cap) { d->tc_grid_cap = cap; }
+  ~GridCap() { d->tc_grid_cap = saved; }
+};
 
 template <typename T>
 wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n, int64_t k, T alpha, const T *A,
@@ -147,28 +297,47 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
   NcclApi *N = nccl();
   wg_device *d = c->dev;
   wg_device_guard guard(d->ordinal);
-  if (panel <= 0) panel = n;
+  GridCap cap(d, reserve_for_nccl(c->nranks, d->sm_count, m_local, k) ? d->sm_count - kNcclSms : 0);
+  // Panel widths, the same on every rank: one panel for a transposed B (its
+  // columns are not contiguous), the caller's width when given, planned widths
+  // for an sgemm the 3xTF32 kernel can take, else one panel.
+  std::vector<int64_t> widths;
+  const bool auto_plan = std::is_same<T, float>::value && !transB && panel <= 0 && alpha != T(0) && k >= 64;
+  if (transB || (panel <= 0 && !auto_plan)) {
+    widths.push_back(n);
+  } else if (panel > 0) {
+    for (int64_t j0 = 0; j0 < n; j0 += panel) widths.push_back(n - j0 < panel ? n - j0 : panel);
+  } else {
+    wg_status st = agreed_panels(c, m_local, n, k, widths);
+    if (st != WG_OK) return st;
+  }
+  int64_t widest = 0;
+  for (int64_t w : widths) widest = w > widest ? w : widest;
+  // This rank's panels run on the 3xTF32 kernel when its own block allows it.
+  const bool tc = std::is_same<T, float>::value && m_local > 0 && !transB &&
+                  wg_sgemm_panel_on_tc(d, (float)alpha, m_local, widest, k);
+  const size_t ws = tc ? wg_tf32x3_panels_workspace(d, m_local, k, widths.data(), widths.size()) : 0;
   const uint32_t epoch = wg_next_epoch(d);
   // B must be ready on root, and earlier readers of B done on every rank, before it is overwritten.
   WG_CUDA(cudaEventRecord(c->entry, d->stream));
   WG_CUDA(cudaStreamWaitEvent(c->stream, c->entry, 0));
-  const int64_t panels = transB ? 1 : (n + panel - 1) / panel;
-  for (int64_t j = 0; j < panels; j++) {
-    const int64_t j0 = transB ? 0 : j * panel;
-    const int64_t cols = transB ? n : (n - j0 < panel ? n - j0 : panel);
+  int64_t j0 = 0;
+  for (size_t j = 0; j < widths.size(); j++) {
+    const int64_t cols = widths[j];
     // Column panel of a column-major k x n B (transB = 0), or all of the n x k B.
     const size_t count = transB ? (size_t)((k - 1) * ldb + n) : (size_t)((cols - 1) * ldb + k);
     T *bp = B + (transB ? 0 : j0 * ldb);
     wg_status st = settle(c, N->Broadcast(bp, bp, count, nccl_type<T>(), root, c->comm, c->stream), "ncclBroadcast");
     if (st != WG_OK) return st;
-    cudaEvent_t ev = panel_event(c, (size_t)j);
+    cudaEvent_t ev = panel_event(c, j);
     WG_CUDA(cudaEventRecord(ev, c->stream));
     WG_CUDA(cudaStreamWaitEvent(d->stream, ev, 0));
     if (m_local > 0) {
       st = wg_gemm_panel<T>(d, j == 0, epoch, transA, transB, m_local, cols, k, alpha, A, lda, bp, ldb, beta,
-                            C + (transB ? 0 : j0 * ldc), ldc, n, panel);
+                            C + (transB ? 0 : j0 * ldc), ldc, ws);
       if (st != WG_OK) return st;
     }
+    j0 += cols;
   }
   WG_CUDA(cudaEventRecord(c->done, d->stream));
   return WG_OK;
@@ -225,6 +394,19 @@ wg_status gather(wg_comm *c, const T *C_local, int64_t m_local, int64_t n, int64
 
 }  // namespace
 
+extern "C" wg_status wg_sharded_panel_plan(int sm_count, int nranks, int64_t m_local, int64_t n, int64_t k,
+                                           int64_t *widths, size_t capacity, size_t *count) {
+  if (!count || sm_count <= 0 || nranks < 1 || m_local <= 0 || n <= 0 || k < 64 || (capacity && !widths))
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
+  const int G = reserve_for_nccl(nranks, sm_count, m_local, k) ? sm_count - kNcclSms : sm_count;
+  const std::vector<int64_t> w = plan_panels(G, nranks, m_local, n, k);
+  *count = w.size();
+  if (capacity < w.size()) return wg_fail(WG_ERR_INVALID_ARGUMENT, "widths holds %zu, the plan has %zu panels",
+                                          capacity, w.size());
+  for (size_t i = 0; i < w.size(); i++) widths[i] = w[i];
+  return WG_OK;
+}
+
 extern "C" wg_status wg_comm_unique_id(unsigned char *id, size_t len) {
   if (!id || len < NCCL_UNIQUE_ID_BYTES) return wg_fail(WG_ERR_INVALID_ARGUMENT, "need a 128-byte id buffer");
   NcclApi *N = nccl();
@@ -253,8 +435,11 @@ extern "C" wg_status wg_comm_init_rank(wg_device *d, int nranks, int rank, const
   cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->entry, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->agreed, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaMalloc((void **)&c->agree, 2 * sizeof(int64_t));
+  if (e == cudaSuccess) e = cudaHostAlloc((void **)&c->agree_host, 2 * sizeof(int64_t), cudaHostAllocDefault);
   if (e != cudaSuccess) {
-    delete c;
+    release(c);
     return wg_fail(WG_ERR_CUDA, "communicator stream/event creation failed: %s", cudaGetErrorString(e));
   }
   ncclUniqueId u;
@@ -267,10 +452,7 @@ extern "C" wg_status wg_comm_init_rank(wg_device *d, int nranks, int rank, const
                                                            : nccl_fail(c, r, "ncclCommInitRankConfig");
   if (st != WG_OK) {
     if (c->comm && !c->aborted) N->CommAbort(c->comm);
-    cudaStreamDestroy(c->stream);
-    cudaEventDestroy(c->entry);
-    cudaEventDestroy(c->done);
-    delete c;
+    release(c);
     return st;
   }
   *out = c;
@@ -285,11 +467,7 @@ extern "C" wg_status wg_comm_destroy(wg_comm *c) {
     cudaStreamSynchronize(c->stream);
     N->CommDestroy(c->comm);
   }
-  for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
-  cudaEventDestroy(c->entry);
-  cudaEventDestroy(c->done);
-  cudaStreamDestroy(c->stream);
-  delete c;
+  release(c);
   return WG_OK;
 }
 
@@ -312,25 +490,7 @@ extern "C" wg_status wg_comm_rank(const wg_comm *c, int *rank, int *nranks) {
 extern "C" wg_status wg_comm_wait(wg_comm *c) {
   if (!c || c->aborted) return wg_fail(WG_ERR_INVALID_ARGUMENT, "communicator is NULL or aborted");
   wg_device_guard guard(c->dev->ordinal);
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    cudaError_t e = cudaEventQuery(c->done);
-    if (e == cudaSuccess) break;
-    if (e != cudaErrorNotReady) return wg_fail(WG_ERR_CUDA, "sharded GEMM failed: %s", cudaGetErrorString(e));
-    ncclResult_t r = ncclSuccess;
-    nccl()->CommGetAsyncError(c->comm, &r);
-    if ((r != ncclSuccess && r != ncclInProgress) ||
-        std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(c->timeout_ms)) {
-      nccl()->CommAbort(c->comm);
-      c->aborted = true;
-      return r != ncclSuccess && r != ncclInProgress
-                 ? nccl_fail(c, r, "collective")
-                 : wg_fail(WG_ERR_NCCL, "sharded GEMM did not finish within %d ms on rank %d; communicator aborted",
-                           c->timeout_ms, c->rank);
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
-  }
-  return WG_OK;
+  return wait_event(c, c->done, "sharded GEMM");
 }
 
 extern "C" wg_status wg_sgemm_sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n, int64_t k,
