@@ -60,6 +60,7 @@ def run(dev, comm, rank, world, routine, m, n, k, ta, tb, alpha, beta, panel):
 
 
 CASES = [("sgemm", 1000, 777, 300, 0, 0, 1.5, 0.5, 256), ("sgemm", 640, 512, 256, 1, 1, 1.0, 0.0, 0),
+         ("sgemm", 1000, 2900, 640, 0, 0, 0.5, -1.0, 0),  # planned panels; uneven row blocks at world 2
          ("dgemm", 700, 333, 129, 0, 0, -0.75, 1.25, 100), ("dgemm", 384, 256, 64, 1, 0, 2.0, -1.0, 0)]
 
 

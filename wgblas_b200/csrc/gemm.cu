@@ -108,7 +108,7 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
   d->stats.simt_launches++;
   wg_launch_scope scope(d, "sgemm_simt");
   WG_CUDA(wg_launch_gemm_simt<float>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
-                                     d->dwords, 0u));
+                                     d->dwords, nullptr));
   return WG_OK;
 }
 
@@ -133,7 +133,7 @@ wg_status gemm_launch<double>(wg_device *d, int transA, int transB, int64_t m, i
   }
   wg_launch_scope scope(d, "dgemm_simt");
   WG_CUDA(wg_launch_gemm_simt<double>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C,
-                                      ldc, d->dwords, 0u));
+                                      ldc, d->dwords, nullptr));
   return WG_OK;
 }
 
@@ -297,11 +297,11 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   const int64_t lda_d = sa.rows > 0 ? sa.rows : 1, ldb_d = sb.rows > 0 ? sb.rows : 1;
   const int64_t panel = reads_ab ? host_panel_cols(m, n, k) : n;
   const int64_t panels = (n + panel - 1) / panel;
-  size_t panel_ws = 0;  // > 0: the panels run on the 3xTF32 kernel with this much scratch
-  if (panels > 1 && std::is_same<T, float>::value && wg_sgemm_panel_on_tc(d, (float)alpha, m, panel, k)) {
-    const int64_t widths[2] = {panel, n - (panels - 1) * panel};
-    panel_ws = wg_tf32x3_panels_workspace(d, m, k, widths, 2);
-  }
+  // sgemm panels on the tensor cores run as one wg_tc_product, whose op(B)
+  // splits overlap the previous panel's MMA.
+  const bool tc = panels > 1 && std::is_same<T, float>::value && wg_sgemm_panel_on_tc(d, (float)alpha, m, panel, k);
+  const int64_t widths[2] = {panel, n - (panels - 1) * panel};
+  wg_tc_product prod{};
   HostPipe pipe;
   T *dA = nullptr, *dB = nullptr, *dC = nullptr;
   cudaError_t e = cudaSuccess;
@@ -339,15 +339,21 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   const bool timing = gpu_ms && (d->flags & WG_DEVICE_TIMING);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s, pipe.ev_a, 0);
   if (e == cudaSuccess && timing) e = cudaEventRecord(d->ev_start, s);
-  const uint32_t epoch = wg_next_epoch(d);
-  for (int64_t j = 0; e == cudaSuccess && j < panels; j++) {
+  if (e == cudaSuccess && tc)
+    st = wg_tc_product_begin(&prod, d, transA, transB, m, k, (float)alpha, (const float *)dA, lda_d, (float)beta,
+                             widths, 2, pipe.ev_a);
+  for (int64_t j = 0; e == cudaSuccess && st == WG_OK && j < panels; j++) {
     const int64_t j0 = j * panel, cols = n - j0 < panel ? n - j0 : panel;
-    e = cudaStreamWaitEvent(s, pipe.ev_b[j], 0);
-    if (e != cudaSuccess) break;
     const T *bp = dB ? (transB ? dB + j0 : dB + j0 * ldb_d) : nullptr;
-    st = panels == 1 ? gemm_launch<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta, dC, m)
-                     : wg_gemm_panel<T>(d, j == 0, epoch, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d,
-                                        beta, dC + j0 * m, m, panel_ws);
+    if (tc) {
+      st = wg_tc_product_panel(&prod, cols, (const float *)bp, ldb_d, (float *)(dC + j0 * m), m, pipe.ev_b[j]);
+    } else {
+      e = cudaStreamWaitEvent(s, pipe.ev_b[j], 0);
+      if (e != cudaSuccess) break;
+      st = panels == 1 ? gemm_launch<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta, dC, m)
+                       : wg_gemm_panel<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta,
+                                          dC + j0 * m, m);
+    }
     if (st != WG_OK) break;
     e = cudaEventRecord(pipe.ev_c[j], s);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->d2h, pipe.ev_c[j], 0);
@@ -356,6 +362,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
                             cudaMemcpyDeviceToHost, d->d2h);
   }
   if (e == cudaSuccess && st == WG_OK && timing) e = cudaEventRecord(d->ev_stop, s);
+  if (tc) wg_tc_product_join(&prod);
   // The temporaries are released once the last read-back has finished.
   cudaEvent_t done = panels ? pipe.ev_c[panels - 1] : pipe.ev_a;
   if (cudaEventRecord(done, d->d2h) == cudaSuccess) cudaStreamWaitEvent(s, done, 0);
@@ -374,13 +381,9 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
 
 }  // namespace
 
-// One panel's GEMM. sgemm panels on the 3xTF32 path (ws_bytes > 0) split op(A)
-// once (first panel) and only the B panel afterwards; everything else goes
-// through the dispatcher.
 template <typename T>
-wg_status wg_gemm_panel(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
-                        int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                        size_t ws_bytes) {
+wg_status wg_gemm_panel(wg_device *d, int transA, int transB, int64_t m, int64_t cols, int64_t k, T alpha,
+                        const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc) {
   return wg_gemm_enqueue<T>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
 }
 
@@ -389,32 +392,10 @@ bool wg_sgemm_panel_on_tc(const wg_device *d, float alpha, int64_t m, int64_t co
          wg_tf32x3_supported(d, m, cols, k);
 }
 
-size_t wg_tf32x3_panels_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count) {
-  size_t bytes = 0;
-  for (size_t i = 0; i < count; i++) {
-    const size_t b = wg_tf32x3_workspace_bytes_sk(d, m, widths[i], k);
-    bytes = b > bytes ? b : bytes;
-  }
-  return bytes;
-}
-
-template <>
-wg_status wg_gemm_panel<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
-                               int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                               int64_t ldb, float beta, float *C, int64_t ldc, size_t ws_bytes) {
-  if (ws_bytes == 0) return wg_gemm_enqueue<float>(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc);
-  void *ws = nullptr;
-  wg_status st = wg_workspace(d, ws_bytes, &ws);
-  if (st != WG_OK) return st;
-  d->stats.calls++;
-  d->stats.tf32x3_launches++;
-  return wg_sgemm_tf32x3_panel(d, transA, transB, m, cols, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, ws_bytes,
-                               first, epoch);
-}
-
-template wg_status wg_gemm_panel<double>(wg_device *, bool, uint32_t, int, int, int64_t, int64_t, int64_t, double,
-                                         const double *, int64_t, const double *, int64_t, double, double *, int64_t,
-                                         size_t);
+template wg_status wg_gemm_panel<float>(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *,
+                                        int64_t, const float *, int64_t, float, float *, int64_t);
+template wg_status wg_gemm_panel<double>(wg_device *, int, int, int64_t, int64_t, int64_t, double, const double *,
+                                         int64_t, const double *, int64_t, double, double *, int64_t);
 
 template wg_status wg_gemm_enqueue<float>(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *,
                                           int64_t, const float *, int64_t, float, float *, int64_t);

@@ -82,10 +82,10 @@ template <typename T, int TA, int TB>
 __global__ void __launch_bounds__(NT, 1)
 gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__ A, int64_t lda,
                  const T *__restrict__ B, int64_t ldb, T beta, T *__restrict__ C, int64_t ldc,
-                 unsigned *dwords, uint32_t only_if_epoch) {
-  if (only_if_epoch) {
+                 unsigned *dwords, wg_gate gate, int gated) {
+  if (gated) {
     // Device-side fallback of the 3xTF32 path: run only if its operand check failed.
-    if (*(volatile unsigned *)(dwords + WG_DW_FALLBACK) != only_if_epoch) return;
+    if (!wg_gate_open(gate)) return;
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicAdd(dwords + WG_DW_FALLBACKS, 1u);
   }
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -216,15 +216,16 @@ __global__ void scale_kernel(int64_t m, int64_t n, T alpha, T beta, T *__restric
 template <typename T, int TA, int TB>
 cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, T alpha, const T *A,
                       int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                      unsigned *dwords, uint32_t only_if_epoch) {
+                      unsigned *dwords, const wg_gate *gate) {
   auto kern = gemm_simt_kernel<T, TA, TB>;
   // Per-device attribute: set on every launch so each device that runs the kernel has it.
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem_bytes<T>());
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
-  kern<<<grid, NT, smem_bytes<T>(), s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords,
-                                          only_if_epoch);
+  const wg_gate g = gate ? *gate : wg_gate{nullptr, nullptr, 0u, 0u};
+  kern<<<grid, NT, smem_bytes<T>(), s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, g,
+                                          gate ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -234,14 +235,14 @@ template <typename T>
 cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t m, int64_t n,
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
-                                uint32_t only_if_epoch) {
+                                const wg_gate *gate) {
   if ((n + BN - 1) / BN > 65535) return cudaErrorInvalidConfiguration;
   if (transA) {
-    return transB ? launch_tt<T, 1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, only_if_epoch)
-                  : launch_tt<T, 1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, only_if_epoch);
+    return transB ? launch_tt<T, 1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate)
+                  : launch_tt<T, 1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate);
   }
-  return transB ? launch_tt<T, 0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, only_if_epoch)
-                : launch_tt<T, 0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, only_if_epoch);
+  return transB ? launch_tt<T, 0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate)
+                : launch_tt<T, 0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate);
 }
 
 template <typename T>
@@ -256,9 +257,9 @@ cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T bet
 
 template cudaError_t wg_launch_gemm_simt<float>(cudaStream_t, int, int, int64_t, int64_t, int64_t, float,
                                                 const float *, int64_t, const float *, int64_t, float,
-                                                float *, int64_t, unsigned *, uint32_t);
+                                                float *, int64_t, unsigned *, const wg_gate *);
 template cudaError_t wg_launch_gemm_simt<double>(cudaStream_t, int, int, int64_t, int64_t, int64_t, double,
                                                  const double *, int64_t, const double *, int64_t, double,
-                                                 double *, int64_t, unsigned *, uint32_t);
+                                                 double *, int64_t, unsigned *, const wg_gate *);
 template cudaError_t wg_launch_scale<float>(cudaStream_t, int64_t, int64_t, float, float, float *, int64_t);
 template cudaError_t wg_launch_scale<double>(cudaStream_t, int64_t, int64_t, double, double, double *, int64_t);

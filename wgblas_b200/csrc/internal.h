@@ -12,10 +12,27 @@
 // Device-side status words, one small array per device handle.
 enum {
   WG_DW_ERROR = 0,     // bitmask of WG_DERR_* set by kernels whose bounded waits gave up
-  WG_DW_FALLBACK = 1,  // epoch of the latest sgemm call whose operands ruled out 3xTF32
-  WG_DW_FALLBACKS = 2, // number of FFMA fallbacks run because of WG_DW_FALLBACK
+  WG_DW_FALLBACK = 1,     // epoch of the latest sgemm call whose operands ruled out 3xTF32
+  WG_DW_FALLBACKS = 2,    // number of FFMA fallbacks run because a gate was open
+  WG_DW_FALLBACK_A = 3,   // panelled products: epoch of the latest op(A) that ruled out 3xTF32
+  WG_DW_FALLBACK_B0 = 4,  // panelled products: the same for the op(B) panels of split buffer 0
+  WG_DW_FALLBACK_B1 = 5,  // ... and of split buffer 1
   WG_DW_COUNT = 8
 };
+
+// Device-side switch between the 3xTF32 kernel and its FFMA fallback: open
+// (fall back) when *a == ea or *b == eb. The operand split sets the words; a
+// tensor-core launch exits at once when its gate is open, and the FFMA launch
+// queued after it runs only then.
+struct wg_gate {
+  const unsigned *a, *b;
+  uint32_t ea, eb;
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ bool wg_gate_open(const wg_gate &g) {
+  return *(volatile const unsigned *)g.a == g.ea || *(volatile const unsigned *)g.b == g.eb;
+}
+#endif
 // Bits of WG_DW_ERROR.
 enum {
   WG_DERR_TMA_WAIT = 1u,  // producer or consumer gave up waiting on a pipeline stage
@@ -42,6 +59,10 @@ struct wg_device {
   int dgemm_path;
   cudaStream_t h2d, d2h;  // copy streams of the host-array path (created on first use)
   cudaMemPool_t staging;  // device copies of host-array operands; keeps its memory between calls
+  // panelled 3xTF32 products: the stream their operand splits run on, and events
+  // (entry, op(A) split ready, a panel's op(B) split ready, split buffer 0/1 free)
+  cudaStream_t side;
+  cudaEvent_t tc_ev[5];
   wg_sgemm_stats stats;
   uint64_t launches;  // kernels launched on this handle
   // profiling: event pairs waiting to be summed, and per-family totals
@@ -55,10 +76,14 @@ struct wg_device {
 };
 
 // Brackets one kernel launch for per-kernel profiling and counts it.
+// Counts one kernel launch and, while profiling is on, brackets it with events
+// on the stream it is launched on (the device stream unless given).
 struct wg_launch_scope {
   wg_device *d;
+  cudaStream_t s;
   int slot;
-  wg_launch_scope(wg_device *dev, const char *family);
+  wg_launch_scope(wg_device *dev, const char *family) : wg_launch_scope(dev, family, nullptr) {}
+  wg_launch_scope(wg_device *dev, const char *family, cudaStream_t stream);
   ~wg_launch_scope();
 };
 
@@ -101,23 +126,49 @@ wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64
                           const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
 
 // One column panel (cols columns) of a product queued panel by panel on
-// d->stream. sgemm panels on the 3xTF32 path split op(A) only for the first
-// panel (first = true), share `epoch` (wg_next_epoch) across the product, and
-// keep their split operands in one workspace of ws_bytes
-// (wg_tf32x3_panels_workspace over all the product's panel widths) so op(A)'s
-// split stays in place; other calls go through the dispatcher.
+// d->stream, through the dispatcher (sgemm products on the tensor cores use
+// wg_tc_product instead).
 template <typename T>
-wg_status wg_gemm_panel(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m, int64_t cols,
-                        int64_t k, T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                        size_t ws_bytes);
-template <>
-wg_status wg_gemm_panel<float>(wg_device *d, bool first, uint32_t epoch, int transA, int transB, int64_t m,
-                               int64_t cols, int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                               int64_t ldb, float beta, float *C, int64_t ldc, size_t ws_bytes);
-// True when wg_gemm_panel<float> runs this panel shape on the 3xTF32 kernel.
+wg_status wg_gemm_panel(wg_device *d, int transA, int transB, int64_t m, int64_t cols, int64_t k, T alpha,
+                        const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+// True when an sgemm panel of this shape can run on the 3xTF32 kernel.
 bool wg_sgemm_panel_on_tc(const wg_device *d, float alpha, int64_t m, int64_t cols, int64_t k);
-// Scratch for every panel of an m x (sum of widths) x k sgemm on the 3xTF32 path.
-size_t wg_tf32x3_panels_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count);
+
+// A 3xTF32 sgemm computed in column panels whose op(B) arrives panel by panel
+// (uploaded from the host, or broadcast from another GPU). op(A) is split once;
+// each panel's op(B) is split on the device's side stream into one of two
+// alternating buffers, so the split of panel j+1 runs while the MMA of panel j
+// runs on d->stream. Each split flags its own operand (WG_DW_FALLBACK_A, _B0/_B1
+// with a fresh epoch), and a panel whose op(A) or op(B) is ruled out runs on
+// the FFMA kernel instead, so one bad panel does not send the others there.
+struct wg_tc_product {
+  wg_device *d;
+  int transA, transB;
+  int64_t m, k;
+  float alpha, beta;
+  const float *A;
+  int64_t lda;
+  char *ws;
+  size_t a_region, slot_bytes, partial_room;
+  int64_t counter_room;
+  int64_t panels;
+  uint32_t epoch_a;
+};
+// Scratch of a product with these panel widths (queried before begin).
+size_t wg_tc_product_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count);
+// Splits op(A) (on the side stream, after a_ready when given); every later panel
+// of the product must be one of `widths`.
+wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int transB, int64_t m, int64_t k,
+                              float alpha, const float *A, int64_t lda, float beta, const int64_t *widths,
+                              size_t count, cudaEvent_t a_ready);
+// C (m x cols) = alpha*op(A)*op(B panel) + beta*C once b_ready (when given) has
+// fired: the split on the side stream, the MMA and its gated FFMA fallback on
+// d->stream. B is the panel's first column of op(B) in the caller's layout.
+wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, int64_t ldb, float *C, int64_t ldc,
+                              cudaEvent_t b_ready);
+// Orders d->stream after everything the product queued on the side stream (call
+// it before releasing operands the splits read, also after an error).
+void wg_tc_product_join(wg_tc_product *p);
 
 // Returns at least `bytes` of device scratch owned by the handle (stream-ordered reuse).
 wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);
@@ -125,13 +176,13 @@ wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);
 // ---- kernel launchers (gemm_simt.cu, sgemm_tf32x3.cu) ----
 
 // C = alpha*op(A)op(B) + beta*C on the FFMA / DFMA pipes, sequential k per element.
-// When only_if_epoch != 0 every CTA first reads dwords[WG_DW_FALLBACK] and exits
-// unless it equals only_if_epoch (the device-side fallback of the 3xTF32 path).
+// With a gate, every CTA first checks it and exits unless it is open (the
+// device-side fallback of the 3xTF32 path), counting runs in dwords[WG_DW_FALLBACKS].
 template <typename T>
 cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t m, int64_t n,
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
-                                uint32_t only_if_epoch);
+                                const wg_gate *gate);
 
 // dgemm on the FP64 tensor-core (DMMA) path, mma.sync.m16n8k8.f64 (dgemm_dmma.cu).
 cudaError_t wg_launch_dgemm_dmma(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
@@ -163,11 +214,4 @@ bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 wg_status wg_sgemm_tf32x3(wg_device *dev, int transA, int transB, int64_t m, int64_t n,
                           int64_t k, float alpha, const float *A, int64_t lda, const float *B,
                           int64_t ldb, float beta, float *C, int64_t ldc, void *ws, size_t ws_bytes);
-// The same, for one column panel of a larger product: pack_a = false reuses the
-// op(A) split left in `ws` by an earlier panel of the same m x k operand, and all
-// panels of one product share `epoch` (wg_next_epoch) so a flagged operand sends
-// that panel and every later one to the FFMA kernel.
-wg_status wg_sgemm_tf32x3_panel(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
-                                float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
-                                float *C, int64_t ldc, void *ws, size_t ws_bytes, bool pack_a, uint32_t epoch);
 uint32_t wg_next_epoch(wg_device *dev);

@@ -105,6 +105,12 @@ extern "C" wg_status wg_device_close(wg_device *d) {
   if (d->h2d) cudaStreamDestroy(d->h2d);
   if (d->d2h) cudaStreamDestroy(d->d2h);
   if (d->staging) cudaMemPoolDestroy(d->staging);
+  if (d->side) {
+    cudaStreamSynchronize(d->side);
+    cudaStreamDestroy(d->side);
+  }
+  for (cudaEvent_t e : d->tc_ev)
+    if (e) cudaEventDestroy(e);
   cudaStreamDestroy(d->own_stream);
   delete d;
   return WG_OK;
@@ -186,7 +192,8 @@ static cudaEvent_t pool_event(wg_device *d) {
   return e;
 }
 
-wg_launch_scope::wg_launch_scope(wg_device *dev, const char *family) : d(dev), slot(-1) {
+wg_launch_scope::wg_launch_scope(wg_device *dev, const char *family, cudaStream_t stream)
+    : d(dev), s(stream ? stream : dev->stream), slot(-1) {
   d->launches++;
   if (!d->profiling) return;
   int f = -1;
@@ -200,13 +207,13 @@ wg_launch_scope::wg_launch_scope(wg_device *dev, const char *family) : d(dev), s
   }
   wg_device::pending_t p{f, pool_event(d), pool_event(d)};
   if (!p.e0 || !p.e1) return;
-  cudaEventRecord(p.e0, d->stream);
+  cudaEventRecord(p.e0, s);
   d->pending.push_back(p);
   slot = (int)d->pending.size() - 1;
 }
 
 wg_launch_scope::~wg_launch_scope() {
-  if (slot >= 0) cudaEventRecord(d->pending[slot].e1, d->stream);
+  if (slot >= 0) cudaEventRecord(d->pending[slot].e1, s);
 }
 
 extern "C" wg_status wg_device_set_profiling(wg_device *d, int on) {
@@ -219,6 +226,7 @@ extern "C" wg_status wg_device_profile_read(wg_device *d, wg_kernel_profile *out
   if (!d || !count || (max > 0 && !out)) return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
   wg_device_guard guard(d->ordinal);
   WG_CUDA(cudaStreamSynchronize(d->stream));
+  if (d->side) WG_CUDA(cudaStreamSynchronize(d->side));
   for (auto &p : d->pending) {
     float ms = 0.0f;
     if (cudaEventElapsedTime(&ms, p.e0, p.e1) == cudaSuccess) {

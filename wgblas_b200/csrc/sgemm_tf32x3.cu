@@ -87,6 +87,8 @@ struct PackArgs {
   int64_t rows_p; // padded rows
   float *hi, *lo; // rows_p x kp, row-major (K contiguous)
   int64_t tiles_r;
+  unsigned *flag; // set to `epoch` when an element rules the split out
+  uint32_t epoch;
 };
 
 // One 32 x 32 (rows x k) tile per 256-thread block; blocks [0, tilesA) pack A,
@@ -94,8 +96,7 @@ struct PackArgs {
 // whichever dimension the source stores contiguously (through shared memory
 // when that is the row dimension).
 __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64_t k, int64_t kp,
-                                                   int64_t tiles_a, unsigned *dwords, uint32_t epoch,
-                                                   unsigned *counters, int64_t n_counters) {
+                                                   int64_t tiles_a, unsigned *counters, int64_t n_counters) {
   __shared__ float tile[32][33];
   // The stream-K tile counters of the MMA launch that follows start at zero.
   if (blockIdx.x == 0)
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64
     P.hi[r * kp + p] = h;
     P.lo[r * kp + p] = l;
   }
-  if (__any_sync(0xffffffffu, bad) && tx == 0) *(volatile unsigned *)(dwords + WG_DW_FALLBACK) = epoch;
+  if (__any_sync(0xffffffffu, bad) && tx == 0) *(volatile unsigned *)P.flag = P.epoch;
 }
 
 
@@ -147,8 +148,8 @@ struct MmaArgs {
   float alpha, beta;
   float *C;
   int64_t ldc;
-  unsigned *dwords;
-  uint32_t epoch;
+  unsigned *dwords;          // WG_DW_ERROR receives the wait-timeout bits
+  wg_gate gate;              // open: the operands ruled the split out, the FFMA kernel computes C
   int tiles_m, tiles_n, kt;  // tile grid and k-blocks per tile
   int dp_tiles;              // tiles [0, dp_tiles) are taken whole, round-robin over the grid
   int sk_tiles;              // the remaining tiles, each split into sk_split k-segments
@@ -227,7 +228,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
            const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
            const MmaArgs args) {
   // Operands ruled out by the pack pass: the FFMA kernel queued next computes C.
-  if (*(volatile unsigned *)(args.dwords + WG_DW_FALLBACK) == args.epoch) return;
+  if (wg_gate_open(args.gate)) return;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = wgtc::smem_addr(smem_raw);
@@ -575,10 +576,96 @@ Plan plan_of(int G, const Layout &L, bool allow_split) {
   return p;
 }
 
-// Scratch after the split operands: the partial sums and counters of the split tiles.
-size_t sk_bytes(const Plan &p) {
-  return (size_t)p.sk_tiles * p.sk_split * BM * Sh::BN * sizeof(float) + (size_t)p.sk_tiles * sizeof(unsigned) +
-         256;
+// Scratch after the split operands: the partial sums of the split tiles, then
+// one arrival counter per split tile (plus slack for alignment).
+size_t sk_partial_bytes(const Plan &p) { return (size_t)p.sk_tiles * p.sk_split * BM * Sh::BN * sizeof(float); }
+size_t sk_bytes(const Plan &p) { return sk_partial_bytes(p) + (size_t)p.sk_tiles * sizeof(unsigned) + 256; }
+
+// Splits op(A) (tiles_a blocks) and/or op(B) on stream `s`, zeroing n_counters
+// split-tile counters first.
+wg_status launch_pack(wg_device *d, cudaStream_t s, const PackArgs &pa, const PackArgs &pb, int64_t k, int64_t kp,
+                      unsigned *counters, int64_t n_counters) {
+  const int64_t blocks = pa.tiles_r + pb.tiles_r;
+  if (blocks == 0) return WG_OK;
+  wg_launch_scope scope(d, "sgemm_tf32x3_pack", s);
+  tf32x3_pack<<<(unsigned)blocks, 256, 0, s>>>(pa, pb, k, kp, pa.tiles_r, counters, n_counters);
+  WG_CUDA(cudaGetLastError());
+  return WG_OK;
+}
+
+// The MMA launch over split operands already in place, then the FFMA launch
+// that computes C instead when `gate` is open; both on d->stream. The last
+// wave's tiles are split along k when sk_room bytes at `sk` hold the plan's
+// partial sums and counters (counters at sk + counter_offset, zeroed
+// beforehand), whole otherwise.
+wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
+                     const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
+                     float *ahi, float *alo, float *bhi, float *blo, char *sk, size_t partial_room,
+                     int64_t counter_room, const wg_gate &gate) {
+  const Layout L = layout_of(m, n, k);
+  const int G = wg_tf32x3_sms(d);
+  Plan plan = plan_of(G, L, true);
+  if (sk_partial_bytes(plan) > partial_room || plan.sk_tiles > counter_room) plan = plan_of(G, L, false);
+  const bool split = plan.sk_tiles > 0;
+  float *partials = split ? reinterpret_cast<float *>(sk) : nullptr;
+  unsigned *counters = split ? reinterpret_cast<unsigned *>(sk + partial_room) : nullptr;
+  CUtensorMap maps[4];
+  if (!make_map(&maps[0], ahi, L.mp, L.kp, BM) || !make_map(&maps[1], alo, L.mp, L.kp, BM) ||
+      !make_map(&maps[2], bhi, L.np, L.kp, Sh::BN) || !make_map(&maps[3], blo, L.np, L.kp, Sh::BN))
+    return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
+  MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, gate, L.tiles_m, L.tiles_n, L.kt, plan.dp_tiles,
+               plan.sk_tiles, plan.sk_split, partials, counters};
+  auto kern = tf32x3_mma<Sh>;
+  WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
+  {
+    wg_launch_scope scope(d, "sgemm_tf32x3_mma");
+    kern<<<plan.grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
+    WG_CUDA(cudaGetLastError());
+  }
+  {
+    // Device-side fallback: exits at once unless the split flagged these operands.
+    wg_launch_scope scope(d, "sgemm_simt_fallback");
+    WG_CUDA(wg_launch_gemm_simt<float>(d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
+                                       d->dwords, &gate));
+  }
+  return WG_OK;
+}
+
+// op(A)(i, p): K-contiguous when transA (A[p + i*lda]); op(B)(p, j) as row j of
+// the N x K operand: K-contiguous when !transB (B[p + j*ldb]).
+PackArgs pack_a_args(int transA, const float *A, int64_t lda, int64_t m, const Layout &L, float *hi, float *lo,
+                     unsigned *flag, uint32_t epoch) {
+  return PackArgs{A, lda, transA ? 1 : 0, m, L.mp, hi, lo, (L.mp / 32) * (L.kp / 32), flag, epoch};
+}
+PackArgs pack_b_args(int transB, const float *B, int64_t ldb, int64_t n, const Layout &L, float *hi, float *lo,
+                     unsigned *flag, uint32_t epoch) {
+  return PackArgs{B, ldb, transB ? 0 : 1, n, L.np, hi, lo, (L.np / 32) * (L.kp / 32), flag, epoch};
+}
+PackArgs no_pack() { return PackArgs{nullptr, 0, 0, 0, 0, nullptr, nullptr, 0, nullptr, 0}; }
+
+// Scratch of a panelled product: op(A)'s split, two alternating op(B) split
+// buffers sized for the widest panel, and the split-K room of the most
+// demanding panel.
+struct ProductLayout {
+  size_t a_region, slot_bytes, partial_room;
+  int64_t counter_room;
+  size_t total;
+};
+
+ProductLayout product_layout(int G, int64_t m, int64_t k, const int64_t *widths, size_t count) {
+  ProductLayout P{0, 0, 0, 0, 0};
+  int64_t widest = 0;
+  for (size_t i = 0; i < count; i++) widest = widths[i] > widest ? widths[i] : widest;
+  const Layout W = layout_of(m, widest > 0 ? widest : 1, k);
+  P.a_region = 2 * W.a_bytes;
+  P.slot_bytes = 2 * W.b_bytes;
+  for (size_t i = 0; i < count; i++) {
+    const Plan p = plan_of(G, layout_of(m, widths[i], k), true);
+    P.partial_room = sk_partial_bytes(p) > P.partial_room ? sk_partial_bytes(p) : P.partial_room;
+    P.counter_room = p.sk_tiles > P.counter_room ? p.sk_tiles : P.counter_room;
+  }
+  P.total = P.a_region + 2 * P.slot_bytes + P.partial_room + (size_t)P.counter_room * sizeof(unsigned) + 256;
+  return P;
 }
 
 }  // namespace
@@ -630,57 +717,6 @@ extern "C" wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_
   return WG_OK;
 }
 
-wg_status wg_sgemm_tf32x3_panel(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
-                                float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
-                                float *C, int64_t ldc, void *ws, size_t ws_bytes, bool pack_a, uint32_t epoch) {
-  const Layout L = layout_of(m, n, k);
-  float *ahi = static_cast<float *>(ws);
-  float *alo = ahi + L.a_bytes / sizeof(float);
-  float *bhi = alo + L.a_bytes / sizeof(float);
-  float *blo = bhi + L.b_bytes / sizeof(float);
-  // Split the last wave's tiles when the workspace has room for their partial sums.
-  Plan plan = plan_of(wg_tf32x3_sms(d), L, true);
-  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(wg_tf32x3_sms(d), L, false);
-  const bool split = plan.sk_tiles > 0;
-  const int grid = plan.grid;
-  float *partials = split ? reinterpret_cast<float *>(static_cast<char *>(ws) + L.operands) : nullptr;
-  unsigned *counters =
-      split ? reinterpret_cast<unsigned *>(partials + (size_t)plan.sk_tiles * plan.sk_split * BM * Sh::BN) : nullptr;
-
-  // op(A)(i, p): K-contiguous when transA (A[p + i*lda]); op(B)(p, j) as row j of
-  // the N x K operand: K-contiguous when !transB (B[p + j*ldb]).
-  PackArgs pa{A, lda, transA ? 1 : 0, m, L.mp, ahi, alo, pack_a ? (L.mp / 32) * (L.kp / 32) : 0};
-  PackArgs pb{B, ldb, transB ? 0 : 1, n, L.np, bhi, blo, (L.np / 32) * (L.kp / 32)};
-  const int64_t blocks = pa.tiles_r + pb.tiles_r;
-  {
-    wg_launch_scope scope(d, "sgemm_tf32x3_pack");
-    tf32x3_pack<<<(unsigned)blocks, 256, 0, d->stream>>>(pa, pb, k, L.kp, pa.tiles_r, d->dwords, epoch, counters,
-                                                         split ? (int64_t)plan.sk_tiles : 0);
-    WG_CUDA(cudaGetLastError());
-  }
-
-  CUtensorMap maps[4];
-  if (!make_map(&maps[0], ahi, L.mp, L.kp, BM) || !make_map(&maps[1], alo, L.mp, L.kp, BM) ||
-      !make_map(&maps[2], bhi, L.np, L.kp, Sh::BN) || !make_map(&maps[3], blo, L.np, L.kp, Sh::BN))
-    return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
-  MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, epoch, L.tiles_m, L.tiles_n, L.kt, plan.dp_tiles,
-               plan.sk_tiles, plan.sk_split, partials, counters};
-  auto kern = tf32x3_mma<Sh>;
-  WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
-  {
-    wg_launch_scope scope(d, "sgemm_tf32x3_mma");
-    kern<<<grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
-    WG_CUDA(cudaGetLastError());
-  }
-  {
-    // Device-side fallback: exits at once unless a pack pass flagged this epoch.
-    wg_launch_scope scope(d, "sgemm_simt_fallback");
-    WG_CUDA(wg_launch_gemm_simt<float>(d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
-                                       d->dwords, epoch));
-  }
-  return WG_OK;
-}
-
 uint32_t wg_next_epoch(wg_device *d) {
   if (++d->epoch == 0) d->epoch = 1;
   return d->epoch;
@@ -689,6 +725,113 @@ uint32_t wg_next_epoch(wg_device *d) {
 wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
                           const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C,
                           int64_t ldc, void *ws, size_t ws_bytes) {
-  return wg_sgemm_tf32x3_panel(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, ws_bytes, true,
-                               wg_next_epoch(d));
+  const Layout L = layout_of(m, n, k);
+  float *ahi = static_cast<float *>(ws);
+  float *alo = ahi + L.a_bytes / sizeof(float);
+  float *bhi = alo + L.a_bytes / sizeof(float);
+  float *blo = bhi + L.b_bytes / sizeof(float);
+  // Split the last wave's tiles when the workspace has room for their partial sums.
+  Plan plan = plan_of(wg_tf32x3_sms(d), L, true);
+  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(wg_tf32x3_sms(d), L, false);
+  char *sk = static_cast<char *>(ws) + L.operands;
+  const size_t partial_room = sk_partial_bytes(plan);
+  unsigned *counters = reinterpret_cast<unsigned *>(sk + partial_room);
+  const uint32_t epoch = wg_next_epoch(d);
+  unsigned *flag = d->dwords + WG_DW_FALLBACK;
+  wg_status st = launch_pack(d, d->stream, pack_a_args(transA, A, lda, m, L, ahi, alo, flag, epoch),
+                             pack_b_args(transB, B, ldb, n, L, bhi, blo, flag, epoch), k, L.kp, counters,
+                             plan.sk_tiles);
+  if (st != WG_OK) return st;
+  const wg_gate gate{flag, flag, epoch, epoch};
+  return launch_mma(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ahi, alo, bhi, blo, sk,
+                    partial_room, plan.sk_tiles, gate);
+}
+
+// ---- panelled products ----------------------------------------------------
+
+size_t wg_tc_product_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count) {
+  return product_layout(wg_tf32x3_sms(d), m, k, widths, count).total;
+}
+
+namespace {
+enum { EV_ENTRY = 0, EV_A_READY = 1, EV_PACKED = 2, EV_SLOT0 = 3, EV_SLOT1 = 4 };
+}
+
+wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int transB, int64_t m, int64_t k,
+                              float alpha, const float *A, int64_t lda, float beta, const int64_t *widths,
+                              size_t count, cudaEvent_t a_ready) {
+  const ProductLayout P = product_layout(wg_tf32x3_sms(d), m, k, widths, count);
+  void *ws = nullptr;
+  wg_status st = wg_workspace(d, P.total, &ws);
+  if (st != WG_OK) return st;
+  if (!d->side) WG_CUDA(cudaStreamCreateWithFlags(&d->side, cudaStreamNonBlocking));
+  for (cudaEvent_t &e : d->tc_ev)
+    if (!e) WG_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  p->d = d;
+  p->transA = transA;
+  p->transB = transB;
+  p->m = m;
+  p->k = k;
+  p->alpha = alpha;
+  p->beta = beta;
+  p->A = A;
+  p->lda = lda;
+  p->ws = static_cast<char *>(ws);
+  p->a_region = P.a_region;
+  p->slot_bytes = P.slot_bytes;
+  p->partial_room = P.partial_room;
+  p->counter_room = P.counter_room;
+  p->panels = 0;
+  // The splits run on the side stream after everything queued so far on the
+  // device stream (earlier users of the workspace) and after op(A) is in place.
+  WG_CUDA(cudaEventRecord(d->tc_ev[EV_ENTRY], d->stream));
+  WG_CUDA(cudaStreamWaitEvent(d->side, d->tc_ev[EV_ENTRY], 0));
+  if (a_ready) WG_CUDA(cudaStreamWaitEvent(d->side, a_ready, 0));
+  p->epoch_a = wg_next_epoch(d);
+  const Layout LA = layout_of(m, 1, k);
+  float *ahi = reinterpret_cast<float *>(p->ws);
+  float *alo = ahi + LA.a_bytes / sizeof(float);
+  unsigned *counters = reinterpret_cast<unsigned *>(p->ws + P.a_region + 2 * P.slot_bytes + P.partial_room);
+  st = launch_pack(d, d->side, pack_a_args(transA, A, lda, m, LA, ahi, alo, d->dwords + WG_DW_FALLBACK_A, p->epoch_a),
+                   no_pack(), k, LA.kp, counters, P.counter_room);
+  if (st != WG_OK) return st;
+  d->stats.calls++;
+  return WG_OK;
+}
+
+wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, int64_t ldb, float *C, int64_t ldc,
+                              cudaEvent_t b_ready) {
+  wg_device *d = p->d;
+  const int slot = (int)(p->panels & 1);
+  const Layout L = layout_of(p->m, cols, p->k);
+  float *ahi = reinterpret_cast<float *>(p->ws);
+  float *alo = ahi + L.a_bytes / sizeof(float);
+  float *bhi = reinterpret_cast<float *>(p->ws + p->a_region + (size_t)slot * p->slot_bytes);
+  float *blo = bhi + L.b_bytes / sizeof(float);
+  // Split buffer `slot` is free once the MMA two panels back has read it.
+  if (p->panels >= 2) WG_CUDA(cudaStreamWaitEvent(d->side, d->tc_ev[EV_SLOT0 + slot], 0));
+  if (b_ready) WG_CUDA(cudaStreamWaitEvent(d->side, b_ready, 0));
+  unsigned *flag_b = d->dwords + WG_DW_FALLBACK_B0 + slot;
+  const uint32_t epoch_b = wg_next_epoch(d);
+  wg_status st = launch_pack(d, d->side, no_pack(), pack_b_args(p->transB, B, ldb, cols, L, bhi, blo, flag_b, epoch_b),
+                             p->k, L.kp, nullptr, 0);
+  if (st != WG_OK) return st;
+  WG_CUDA(cudaEventRecord(d->tc_ev[EV_PACKED], d->side));
+  WG_CUDA(cudaStreamWaitEvent(d->stream, d->tc_ev[EV_PACKED], 0));
+  char *sk = p->ws + p->a_region + 2 * p->slot_bytes;
+  const wg_gate gate{d->dwords + WG_DW_FALLBACK_A, flag_b, p->epoch_a, epoch_b};
+  st = launch_mma(d, p->transA, p->transB, p->m, cols, p->k, p->alpha, p->A, p->lda, B, ldb, p->beta, C, ldc, ahi,
+                  alo, bhi, blo, sk, p->partial_room, p->counter_room, gate);
+  if (st != WG_OK) return st;
+  WG_CUDA(cudaEventRecord(d->tc_ev[EV_SLOT0 + slot], d->stream));
+  d->stats.tf32x3_launches++;
+  p->panels++;
+  return WG_OK;
+}
+
+void wg_tc_product_join(wg_tc_product *p) {
+  wg_device *d = p->d;
+  if (!d || !d->side) return;
+  if (cudaEventRecord(d->tc_ev[EV_PACKED], d->side) == cudaSuccess)
+    cudaStreamWaitEvent(d->stream, d->tc_ev[EV_PACKED], 0);
 }

@@ -316,29 +316,43 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
   // This rank's panels run on the 3xTF32 kernel when its own block allows it.
   const bool tc = std::is_same<T, float>::value && m_local > 0 && !transB &&
                   wg_sgemm_panel_on_tc(d, (float)alpha, m_local, widest, k);
-  const size_t ws = tc ? wg_tf32x3_panels_workspace(d, m_local, k, widths.data(), widths.size()) : 0;
-  const uint32_t epoch = wg_next_epoch(d);
   // B must be ready on root, and earlier readers of B done on every rank, before it is overwritten.
   WG_CUDA(cudaEventRecord(c->entry, d->stream));
   WG_CUDA(cudaStreamWaitEvent(c->stream, c->entry, 0));
+  // On the tensor cores the panels form one product: op(A) is split once, and
+  // each arriving panel's split overlaps the previous panel's MMA.
+  wg_tc_product prod{};
+  wg_status st = WG_OK;
+  if (tc)
+    st = wg_tc_product_begin(&prod, d, transA, transB, m_local, k, (float)alpha, (const float *)A, lda, (float)beta,
+                             widths.data(), widths.size(), nullptr);
   int64_t j0 = 0;
-  for (size_t j = 0; j < widths.size(); j++) {
+  for (size_t j = 0; st == WG_OK && j < widths.size(); j++) {
     const int64_t cols = widths[j];
     // Column panel of a column-major k x n B (transB = 0), or all of the n x k B.
     const size_t count = transB ? (size_t)((k - 1) * ldb + n) : (size_t)((cols - 1) * ldb + k);
     T *bp = B + (transB ? 0 : j0 * ldb);
-    wg_status st = settle(c, N->Broadcast(bp, bp, count, nccl_type<T>(), root, c->comm, c->stream), "ncclBroadcast");
-    if (st != WG_OK) return st;
+    st = settle(c, N->Broadcast(bp, bp, count, nccl_type<T>(), root, c->comm, c->stream), "ncclBroadcast");
+    if (st != WG_OK) break;
     cudaEvent_t ev = panel_event(c, j);
-    WG_CUDA(cudaEventRecord(ev, c->stream));
-    WG_CUDA(cudaStreamWaitEvent(d->stream, ev, 0));
-    if (m_local > 0) {
-      st = wg_gemm_panel<T>(d, j == 0, epoch, transA, transB, m_local, cols, k, alpha, A, lda, bp, ldb, beta,
-                            C + (transB ? 0 : j0 * ldc), ldc, ws);
-      if (st != WG_OK) return st;
+    cudaError_t e = cudaEventRecord(ev, c->stream);
+    if (e != cudaSuccess) {
+      st = wg_fail(WG_ERR_CUDA, "cudaEventRecord failed: %s", cudaGetErrorString(e));
+      break;
+    }
+    T *cp = C + (transB ? 0 : j0 * ldc);
+    if (tc) {
+      st = wg_tc_product_panel(&prod, cols, (const float *)bp, ldb, (float *)cp, ldc, ev);
+    } else {
+      e = cudaStreamWaitEvent(d->stream, ev, 0);
+      if (e != cudaSuccess) st = wg_fail(WG_ERR_CUDA, "cudaStreamWaitEvent failed: %s", cudaGetErrorString(e));
+      else if (m_local > 0)
+        st = wg_gemm_panel<T>(d, transA, transB, m_local, cols, k, alpha, A, lda, bp, ldb, beta, cp, ldc);
     }
     j0 += cols;
   }
+  if (tc) wg_tc_product_join(&prod);
+  if (st != WG_OK) return st;
   WG_CUDA(cudaEventRecord(c->done, d->stream));
   return WG_OK;
 }
