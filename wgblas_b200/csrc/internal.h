@@ -47,7 +47,6 @@ struct wg_device {
   cudaStream_t stream;  // the stream work is ordered on (own_stream or the caller's)
   cudaEvent_t ev_start, ev_stop;
   int sm_count;
-  int tc_grid_cap;  // > 0: at most this many CTAs in the 3xTF32 persistent grid
   int cc_major, cc_minor;
   size_t total_mem;
   char name[256];
@@ -198,9 +197,6 @@ cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T bet
 // alone (whole-tile scheduling), or with the stream-K partial sums and counters.
 size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
 size_t wg_tf32x3_workspace_bytes_sk(const wg_device *dev, int64_t m, int64_t n, int64_t k);
-// SMs the 3xTF32 kernel's persistent grid may use on this handle (all of them
-// unless tc_grid_cap holds some back, e.g. for NCCL kernels running alongside).
-int wg_tf32x3_sms(const wg_device *dev);
 // Modelled run time of the 3xTF32 kernel for one m x n x k product on G SMs, in
 // units of one 16-deep k-block of one tile's MMAs (about 0.5 us on B200).
 double wg_tf32x3_cost(int G, int64_t m, int64_t n, int64_t k);

@@ -603,7 +603,7 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
                      float *ahi, float *alo, float *bhi, float *blo, char *sk, size_t partial_room,
                      int64_t counter_room, const wg_gate &gate) {
   const Layout L = layout_of(m, n, k);
-  const int G = wg_tf32x3_sms(d);
+  const int G = d->sm_count;
   Plan plan = plan_of(G, L, true);
   if (sk_partial_bytes(plan) > partial_room || plan.sk_tiles > counter_room) plan = plan_of(G, L, false);
   const bool split = plan.sk_tiles > 0;
@@ -672,13 +672,9 @@ ProductLayout product_layout(int G, int64_t m, int64_t k, const int64_t *widths,
 
 size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) { return layout_of(m, n, k).operands; }
 
-int wg_tf32x3_sms(const wg_device *d) {
-  return d->tc_grid_cap > 0 && d->tc_grid_cap < d->sm_count ? d->tc_grid_cap : d->sm_count;
-}
-
 size_t wg_tf32x3_workspace_bytes_sk(const wg_device *d, int64_t m, int64_t n, int64_t k) {
   const Layout L = layout_of(m, n, k);
-  return L.operands + sk_bytes(plan_of(wg_tf32x3_sms(d), L, true));
+  return L.operands + sk_bytes(plan_of(d->sm_count, L, true));
 }
 
 double wg_tf32x3_cost(int G, int64_t m, int64_t n, int64_t k) {
@@ -731,8 +727,8 @@ wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64
   float *bhi = alo + L.a_bytes / sizeof(float);
   float *blo = bhi + L.b_bytes / sizeof(float);
   // Split the last wave's tiles when the workspace has room for their partial sums.
-  Plan plan = plan_of(wg_tf32x3_sms(d), L, true);
-  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(wg_tf32x3_sms(d), L, false);
+  Plan plan = plan_of(d->sm_count, L, true);
+  if (ws_bytes < L.operands + sk_bytes(plan)) plan = plan_of(d->sm_count, L, false);
   char *sk = static_cast<char *>(ws) + L.operands;
   const size_t partial_room = sk_partial_bytes(plan);
   unsigned *counters = reinterpret_cast<unsigned *>(sk + partial_room);
@@ -750,7 +746,7 @@ wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64
 // ---- panelled products ----------------------------------------------------
 
 size_t wg_tc_product_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count) {
-  return product_layout(wg_tf32x3_sms(d), m, k, widths, count).total;
+  return product_layout(d->sm_count, m, k, widths, count).total;
 }
 
 namespace {
@@ -760,7 +756,7 @@ enum { EV_ENTRY = 0, EV_A_READY = 1, EV_PACKED = 2, EV_SLOT0 = 3, EV_SLOT1 = 4 }
 wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int transB, int64_t m, int64_t k,
                               float alpha, const float *A, int64_t lda, float beta, const int64_t *widths,
                               size_t count, cudaEvent_t a_ready) {
-  const ProductLayout P = product_layout(wg_tf32x3_sms(d), m, k, widths, count);
+  const ProductLayout P = product_layout(d->sm_count, m, k, widths, count);
   void *ws = nullptr;
   wg_status st = wg_workspace(d, P.total, &ws);
   if (st != WG_OK) return st;

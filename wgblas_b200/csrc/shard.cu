@@ -176,25 +176,6 @@ cudaEvent_t panel_event(wg_comm *c, size_t i) {
   return c->ev[i];
 }
 
-// SMs left out of the 3xTF32 persistent grid while a sharded product runs on
-// more than one rank and the broadcast is a large share of the work, so the
-// broadcast of the next panel (an NCCL kernel) finds SMs to run on instead of
-// waiting for the current panel's GEMM to end. Measured on 8 x B200 at
-// 16384^3: 8 reserved SMs gave 5.94 ms per product against 6.23 ms with none
-// (2048 rows per rank); with 4096 or 8192 rows per rank, reserving cost 2-4 %.
-constexpr int kNcclSms = 8;
-
-// True when broadcasting one tile column of B (256 x k at about 400 GB/s) takes
-// more than half as long as this rank's GEMM on it (m_local rows at about
-// 0.5 us per 16-deep k-block of a tile, on G SMs).
-bool reserve_for_nccl(int nranks, int G, int64_t m_local, int64_t k) {
-  if (nranks <= 1 || G <= 2 * kNcclSms) return false;
-  const double bcast = 256.0 * (double)k * 4.0 / 400e9;
-  const double tiles = (double)((m_local + 127) / 128);
-  const double gemm = tiles / G * (double)((k + 31) / 32 * 2) * 0.5e-6;
-  return bcast > 0.5 * gemm;
-}
-
 // Column panels of a sharded sgemm on the 3xTF32 kernel. Panel j's GEMM starts
 // when both the previous panel's GEMM and panel j's broadcast are done; with
 // the broadcast of consecutive panels back to back on the communicator's
@@ -248,7 +229,7 @@ wg_status agreed_panels(wg_comm *c, int64_t m_local, int64_t n, int64_t k, std::
     out = c->plan_widths;
     return WG_OK;
   }
-  int64_t m_max = m_local, g_min = wg_tf32x3_sms(c->dev);
+  int64_t m_max = m_local, g_min = c->dev->sm_count;
   if (c->nranks > 1) {
     c->agree_host[0] = m_local;
     c->agree_host[1] = -g_min;
@@ -271,14 +252,6 @@ wg_status agreed_panels(wg_comm *c, int64_t m_local, int64_t n, int64_t k, std::
   return WG_OK;
 }
 
-// Restores the device's 3xTF32 grid cap when a sharded call returns.
-struct GridCap {
-  wg_device *d;
-  int saved;
-  GridCap(wg_device *dev, int cap) : d(dev), saved(dev->tc_grid_cap) { d->tc_grid_cap = cap; }
-  ~GridCap() { d->tc_grid_cap = saved; }
-};
-
 template <typename T>
 wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n, int64_t k, T alpha, const T *A,
                   int64_t lda, T *B, int64_t ldb, int root, T beta, T *C, int64_t ldc, int64_t panel) {
@@ -297,7 +270,6 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
   NcclApi *N = nccl();
   wg_device *d = c->dev;
   wg_device_guard guard(d->ordinal);
-  GridCap cap(d, reserve_for_nccl(c->nranks, d->sm_count, m_local, k) ? d->sm_count - kNcclSms : 0);
   // Panel widths, the same on every rank: one panel for a transposed B (its
   // columns are not contiguous), the caller's width when given, planned widths
   // for an sgemm the 3xTF32 kernel can take, else one panel.
@@ -412,8 +384,7 @@ extern "C" wg_status wg_sharded_panel_plan(int sm_count, int nranks, int64_t m_l
                                            int64_t *widths, size_t capacity, size_t *count) {
   if (!count || sm_count <= 0 || nranks < 1 || m_local <= 0 || n <= 0 || k < 64 || (capacity && !widths))
     return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
-  const int G = reserve_for_nccl(nranks, sm_count, m_local, k) ? sm_count - kNcclSms : sm_count;
-  const std::vector<int64_t> w = plan_panels(G, nranks, m_local, n, k);
+  const std::vector<int64_t> w = plan_panels(sm_count, nranks, m_local, n, k);
   *count = w.size();
   if (capacity < w.size()) return wg_fail(WG_ERR_INVALID_ARGUMENT, "widths holds %zu, the plan has %zu panels",
                                           capacity, w.size());
