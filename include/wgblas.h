@@ -92,6 +92,14 @@ wg_status wg_device_sync(wg_device *dev);
 /* Waits, then reports (and clears) a device-side error word: WG_ERR_KERNEL_TIMEOUT
  * when a kernel's bounded wait gave up since the last check. */
 wg_status wg_device_check(wg_device *dev);
+/* Failure-detection self-test (no counterpart in the reference). Queues one
+ * CTA that waits, with the same clock-bounded mbarrier wait the tensor-core
+ * kernels use, on a barrier nothing completes: after about budget_us
+ * microseconds (at most 1 s) of SM clock the wait gives up, the kernel records
+ * the timeout in the device error word and returns. The next wg_device_check
+ * reports WG_ERR_KERNEL_TIMEOUT (and clears the word); the context stays usable. */
+wg_status wg_selftest_bounded_wait(wg_device *dev, unsigned budget_us);
+
 
 /* Counters of the sgemm dispatcher since the handle was opened (synchronises). */
 typedef struct wg_sgemm_stats {

@@ -37,7 +37,8 @@ __device__ __forceinline__ bool wg_gate_open(const wg_gate &g) {
 enum {
   WG_DERR_TMA_WAIT = 1u,  // producer or consumer gave up waiting on a pipeline stage
   WG_DERR_MMA_WAIT = 2u,  // the epilogue gave up waiting for the accumulator
-  WG_DERR_TMEM = 4u       // TMEM allocation returned an unusable address
+  WG_DERR_TMEM = 4u,      // TMEM allocation returned an unusable address
+  WG_DERR_SELFTEST = 8u   // wg_selftest_bounded_wait's wait ran out, as it is meant to
 };
 
 struct wg_device {

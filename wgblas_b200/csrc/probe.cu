@@ -6,6 +6,7 @@
 // SM, a long loop so the issue rate is all that is measured); the copy probe
 // streams a buffer much larger than L2 through 16-byte loads and stores.
 #include "internal.h"
+#include "tcgen05.cuh"
 
 namespace {
 
@@ -151,7 +152,31 @@ wg_status copy_probe(wg_device *d, double *gbs) {
   return WG_OK;
 }
 
+// One thread waits, with the tensor-core kernels' clock-bounded mbarrier wait,
+// on a barrier no thread or copy ever completes; when the budget runs out it
+// records the timeout in the device error word and returns.
+__global__ void bounded_wait_selftest(unsigned *dwords, long long budget) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  wgtc::mbar_init(&bar, 1);
+  wgtc::fence_barrier_init();
+  if (!wgtc::mbar_wait_bounded(&bar, 0, budget)) atomicOr(dwords + WG_DW_ERROR, WG_DERR_SELFTEST);
+}
+
 }  // namespace
+
+extern "C" wg_status wg_selftest_bounded_wait(wg_device *d, unsigned budget_us) {
+  if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  if (budget_us == 0 || budget_us > 1000000) return wg_fail(WG_ERR_INVALID_ARGUMENT, "budget_us must be in (0, 1e6]");
+  wg_device_guard guard(d->ordinal);
+  int khz = 0;
+  WG_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, d->ordinal));
+  const long long budget = (long long)budget_us * (khz > 0 ? khz / 1000 : 2000);
+  wg_launch_scope scope(d, "selftest_bounded_wait");
+  bounded_wait_selftest<<<1, 32, 0, d->stream>>>(d->dwords, budget);
+  WG_CUDA(cudaGetLastError());
+  return WG_OK;
+}
 
 extern "C" wg_status wg_probe_peak(wg_device *d, int kind, double *value) {
   if (!d || !value) return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
