@@ -256,13 +256,13 @@ def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
     rnd = wg.randomFloat64Array if dt == np.float64 else wg.randomFloat32Array
     GA = wg.GpuMatrix.from_(dev, rnd(mr * k, -1, 1, 10 + rank), mr, k, mr, "column-major")
     GC = wg.GpuMatrix.from_(dev, rnd(mr * n, -1, 1, 30 + rank), mr, n, mr, "column-major")
-    GB = (wg.GpuMatrix.from_(dev, rnd(k * n, -1, 1, 2), k, n, k, "column-major") if rank == 0
-          else wg.GpuMatrix.empty(dev, k, n, k, "column-major", dt))
+    # B lives on the root only; the other ranks receive it into the library's buffer.
+    GB = wg.GpuMatrix.from_(dev, rnd(k * n, -1, 1, 2), k, n, k, "column-major") if rank == 0 else None
     stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
 
     def step():
         gemm_sharded(comm, w["transA"], w["transB"], mr, n, k, w["alpha"], GA, GB, w["beta"], GC, root=0,
-                     panel_cols=PANEL_COLS)
+                     panel_cols=PANEL_COLS, ldb=k)
 
     try:
         with torch.cuda.stream(stream):
@@ -295,7 +295,8 @@ def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
             ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     finally:
         for g in (GA, GB, GC):
-            g.destroy()
+            if g is not None:
+                g.destroy()
     return ms, prof, launches, wall
 
 

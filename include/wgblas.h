@@ -271,11 +271,13 @@ wg_status wg_comm_rank(const wg_comm *comm, int *rank, int *nranks);
 wg_status wg_comm_wait(wg_comm *comm);
 /* This rank's block of C (m_local x n, device pointer, ldc) := alpha * op(A_local)
  * (m_local x k) * op(B) + beta * C_local. B (column-major k x n, or n x k when
- * transB) holds the operand on `root` and is overwritten with it on the other
- * ranks: it is broadcast in panels of panel_cols columns (<= 0: one panel), and
- * the GEMM of each panel starts as soon as that panel has arrived. n, k, ldb,
- * transB, root and panel_cols must agree on every rank. Queued on the device
- * stream; wg_comm_wait or wg_device_sync waits for it. */
+ * transB, leading dimension ldb) is read on `root` only; it may be NULL on the
+ * other ranks, which receive root's B into the communicator's own buffer. B is
+ * sent in column panels (panel_cols wide; <= 0: the planned widths of
+ * wg_sharded_panel_plan for an sgemm with k >= 64 and transB = 0, else one
+ * panel), and the GEMM of each panel starts as soon as that panel has arrived.
+ * n, k, ldb, transB, root and panel_cols must agree on every rank. Queued on the
+ * device stream; wg_comm_wait or wg_device_sync waits for it. */
 wg_status wg_sgemm_sharded(wg_comm *comm, int transA, int transB, int64_t m_local, int64_t n, int64_t k,
                            float alpha, const float *A_local, int64_t lda, float *B, int64_t ldb, int root,
                            float beta, float *C_local, int64_t ldc, int64_t panel_cols);

@@ -35,10 +35,12 @@ def run(dev, comm, rank, world, routine, m, n, k, ta, tb, alpha, beta, panel):
     GA = wg.GpuMatrix.from_(dev, A_loc, a_rows, a_cols, lda_loc, "column-major")
     GC = wg.GpuMatrix.from_(dev, C_loc, mr, n, ldc_loc, "column-major")
     b_rows, b_cols = (n, k) if tb else (k, n)
-    GB = wg.GpuMatrix.from_(dev, B if rank == 0 else np.zeros_like(B), b_rows, b_cols, ldb, "column-major")
+    # B on the root only; odd ranks pass none at all, even ones a zeroed matrix
+    GB = (wg.GpuMatrix.from_(dev, B if rank == 0 else np.zeros_like(B), b_rows, b_cols, ldb, "column-major")
+          if rank % 2 == 0 else None)
     GF = wg.GpuMatrix.empty(dev, m, n, m, "column-major", dt) if rank == 0 else None
     try:
-        gemm_sharded(comm, ta, tb, mr, n, k, alpha, GA, GB, beta, GC, root=0, panel_cols=panel)
+        gemm_sharded(comm, ta, tb, mr, n, k, alpha, GA, GB, beta, GC, root=0, panel_cols=panel, ldb=ldb)
         comm.wait()
         gather_rows(comm, GC, mr, n, offs, root=0, C_full=GF)
         dev.synchronize()

@@ -17,6 +17,8 @@ enum {
   WG_DW_FALLBACK_A = 3,   // panelled products: epoch of the latest op(A) that ruled out 3xTF32
   WG_DW_FALLBACK_B0 = 4,  // panelled products: the same for the op(B) panels of split buffer 0
   WG_DW_FALLBACK_B1 = 5,  // ... and of split buffer 1
+  WG_DW_NEXT_UNIT0 = 6,   // work counter of the 3xTF32 kernel (single calls, products' buffer 0)
+  WG_DW_NEXT_UNIT1 = 7,   // ... of products' split buffer 1
   WG_DW_COUNT = 8
 };
 

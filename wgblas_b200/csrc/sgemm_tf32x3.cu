@@ -23,8 +23,10 @@
 //     store C column by column (32 rows = 128 contiguous bytes per warp store),
 //     so a tile's epilogue overlaps the next tile's main loop. Tiles are
 //     visited in groups of GROUP_M tile rows for L2 reuse.
-//     Work split: whole tiles round-robin (c, c+G, ...) for every full wave,
-//     which keeps the SMs on neighbouring tiles for L2 reuse; the leftover
+//     Work split: units are handed out in raster order from a work counter
+//     (each CTA's first is its blockIdx.x), so CTAs running together work on
+//     neighbouring tiles for L2 reuse and an SM slowed by other kernels (NCCL,
+//     operand splits of the next panel) simply takes fewer; the leftover
 //     tiles of a partial last wave are cut into s equal k-segments when that
 //     shortens the wave (plan_of), and the segments are dealt out so CTAs
 //     running together share a k range. A split tile is finished by whichever
@@ -96,11 +98,14 @@ struct PackArgs {
 // whichever dimension the source stores contiguously (through shared memory
 // when that is the row dimension).
 __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64_t k, int64_t kp,
-                                                   int64_t tiles_a, unsigned *counters, int64_t n_counters) {
+                                                   int64_t tiles_a, unsigned *counters, int64_t n_counters,
+                                                   unsigned *next_unit) {
   __shared__ float tile[32][33];
-  // The stream-K tile counters of the MMA launch that follows start at zero.
-  if (blockIdx.x == 0)
+  // The split-tile counters and the work counter of the MMA launch that follows start at zero.
+  if (blockIdx.x == 0) {
     for (int64_t i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
+    if (next_unit && threadIdx.x == 0) *next_unit = 0;
+  }
   const bool is_a = blockIdx.x < tiles_a;
   const PackArgs &P = is_a ? a : b;
   const int64_t t = is_a ? blockIdx.x : blockIdx.x - tiles_a;
@@ -156,6 +161,8 @@ struct MmaArgs {
   int sk_split;
   float *partials;           // split tiles: [sk_tiles * sk_split][BN][BM] partial sums
   unsigned *counters;        // split tiles: one arrival counter each
+  unsigned *next_unit;       // work counter: units handed out beyond the first gridDim.x
+  int units;                 // dp_tiles + sk_tiles * sk_split
 };
 
 // Tile t -> (tile row, tile column), GROUP_M tile rows at a time.
@@ -174,33 +181,30 @@ struct Unit {
   int t, kb0, kb1, seg;
 };
 
-// Walks this CTA's units in order — whole tiles c, c+G, ... then split units
-// c, c+G, ... — and every role calls it with the same state. Split unit u is
-// segment u / sk_tiles of split tile u % sk_tiles, so CTAs running at the same
-// time work on neighbouring tiles over the same k range.
-struct Units {
-  int t;  // whole-tile cursor
-  int u;  // split-unit cursor
-  __device__ __forceinline__ Units(const MmaArgs &) : t(blockIdx.x), u(blockIdx.x) {}
-  __device__ __forceinline__ bool next(const MmaArgs &a, Unit &x) {
-    if (t < a.dp_tiles) {
-      x.t = t;
-      x.kb0 = 0;
-      x.kb1 = a.kt;
-      x.seg = -1;
-      t += gridDim.x;
-      return true;
-    }
-    if (u >= a.sk_tiles * a.sk_split) return false;
-    const int local = u % a.sk_tiles;
-    x.seg = u / a.sk_tiles;
-    x.t = a.dp_tiles + local;
-    x.kb0 = (int)((int64_t)a.kt * x.seg / a.sk_split);
-    x.kb1 = (int)((int64_t)a.kt * (x.seg + 1) / a.sk_split);
-    u += gridDim.x;
-    return true;
+// Units are numbered whole tiles first (0 .. dp_tiles-1, in raster order), then
+// the split units: unit dp_tiles + v is segment v / sk_tiles of split tile
+// v % sk_tiles, so units handed out together cover neighbouring tiles over the
+// same k range.
+__device__ __forceinline__ Unit decode(const MmaArgs &a, int u) {
+  Unit x;
+  if (u < a.dp_tiles) {
+    x.t = u;
+    x.kb0 = 0;
+    x.kb1 = a.kt;
+    x.seg = -1;
+    return x;
   }
-};
+  const int v = u - a.dp_tiles;
+  x.seg = v / a.sk_tiles;
+  x.t = a.dp_tiles + v % a.sk_tiles;
+  x.kb0 = (int)((int64_t)a.kt * x.seg / a.sk_split);
+  x.kb1 = (int)((int64_t)a.kt * (x.seg + 1) / a.sk_split);
+  return x;
+}
+
+// Depth of the queue through which the producer hands each unit it takes to the
+// MMA issuer and the epilogue.
+constexpr int UQ = 4;
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // True on every epilogue thread iff `v` is true on all of them, so a decision to
@@ -237,7 +241,10 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   uint64_t *empty = full + S::STAGES;
   uint64_t *acc_full = empty + S::STAGES;  // [2]: accumulator b holds a finished unit
   uint64_t *acc_empty = acc_full + 2;      // [2]: the epilogue has drained accumulator b
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *uq_full = acc_empty + 2;       // [UQ]: the producer has written unit slot i
+  uint64_t *uq_empty = uq_full + UQ;       // [UQ]: the MMA issuer and the epilogue have read it
+  volatile int *uq = reinterpret_cast<volatile int *>(uq_empty + UQ);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(const_cast<int *>(uq) + UQ);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile unsigned *last_flag = reinterpret_cast<volatile unsigned *>(tmem_slot + 2);
 
@@ -251,6 +258,10 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
     for (int b = 0; b < 2; b++) {
       wgtc::mbar_init(&acc_full[b], 1);
       wgtc::mbar_init(&acc_empty[b], 32 * EPI_WARPS);
+    }
+    for (int i = 0; i < UQ; i++) {
+      wgtc::mbar_init(&uq_full[i], 1);
+      wgtc::mbar_init(&uq_empty[i], 2);
     }
     *abort_flag = 0;
     wgtc::fence_barrier_init();
@@ -271,12 +282,25 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer: one continuous ring across this CTA's units ----
-    Units it(args);
-    Unit u;
+    // ---- TMA producer: takes units (its first is blockIdx.x, later ones from the
+    // work counter, so SMs slowed by other kernels take fewer), hands each to the
+    // other roles, and streams its k-blocks into one continuous ring ----
     int64_t g = 0;
     bool ok = true;
-    while (ok && it.next(args, u)) {
+    for (int n = 0; ok; n++) {
+      const int slot = n % UQ;
+      const uint32_t uph = (uint32_t)(n / UQ) & 1u;
+      int un = n == 0 ? (int)blockIdx.x : (int)gridDim.x + (int)atomicAdd(args.next_unit, 1u);
+      if (un >= args.units) un = -1;  // no work left: tells the other roles to stop
+      if (!wgtc::mbar_wait_bounded(&uq_empty[slot], uph ^ 1u, WAIT_BUDGET) || *abort_flag) {
+        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      uq[slot] = un;
+      mbar_arrive(&uq_full[slot]);
+      if (un < 0) break;
+      const Unit u = decode(args, un);
       int tm, tn;
       raster(args, u.t, tm, tn);
       for (int kb = u.kb0; kb < u.kb1; kb++, g++) {
@@ -303,12 +327,19 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     constexpr uint32_t idesc = wgtc::idesc_tf32(BM, S::BN);
-    Units it(args);
-    Unit u;
     int64_t g = 0;
-    int n_units = 0;
     bool ok = true;
-    while (ok && it.next(args, u)) {
+    for (int n_units = 0; ok; n_units++) {
+      const int slot = n_units % UQ;
+      if (!wgtc::mbar_wait_bounded(&uq_full[slot], (uint32_t)(n_units / UQ) & 1u, WAIT_BUDGET) || *abort_flag) {
+        atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      const int un = uq[slot];
+      mbar_arrive(&uq_empty[slot]);
+      if (un < 0) break;
+      const Unit u = decode(args, un);
       const int b = n_units & 1;
       const uint32_t use = (uint32_t)(n_units >> 1);
       if (!wgtc::mbar_wait_bounded(&acc_empty[b], (use & 1u) ^ 1u, WAIT_BUDGET) || *abort_flag) {
@@ -346,21 +377,29 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
         wgtc::mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
       wgtc::mma_commit(&acc_full[b]);  // accumulator b complete once all its MMAs finish
-      n_units++;
     }
   } else if (warp >= 2) {
     // ---- epilogue: TMEM -> registers -> C (or a partial-sum slot) ----
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     const float alpha = args.alpha, beta = args.beta;
-    Units it(args);
-    Unit u;
-    int n_units = 0;
-    while (it.next(args, u)) {
+    for (int n_units = 0;; n_units++) {
+      const int slot = n_units % UQ;
+      const bool got = wgtc::mbar_wait_bounded(&uq_full[slot], (uint32_t)(n_units / UQ) & 1u, WAIT_BUDGET);
+      const int un = got ? uq[slot] : -1;
+      // One decision for all 128 epilogue threads (tcgen05.ld is warp-collective and
+      // the partial-sum path below meets at a named barrier); it also means every
+      // thread has read the slot before it is released.
+      if (!epi_all(got && *abort_flag == 0)) {
+        if (!got) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      if (threadIdx.x == 64) mbar_arrive(&uq_empty[slot]);
+      if (un < 0) break;
+      const Unit u = decode(args, un);
       const int b = n_units & 1;
       const uint32_t use = (uint32_t)(n_units >> 1);
-      // One decision for all 128 epilogue threads (tcgen05.ld is warp-collective and
-      // the partial-sum path below meets at a named barrier).
       const bool ready = wgtc::mbar_wait_bounded(&acc_full[b], use & 1u, WAIT_BUDGET);
       if (!epi_all(ready && *abort_flag == 0)) {
         if (!ready) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
@@ -467,7 +506,6 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       }
       wgtc::tc_fence_before();
       mbar_arrive(&acc_empty[b]);  // accumulator b may be refilled
-      n_units++;
     }
   }
 
@@ -582,13 +620,13 @@ size_t sk_partial_bytes(const Plan &p) { return (size_t)p.sk_tiles * p.sk_split 
 size_t sk_bytes(const Plan &p) { return sk_partial_bytes(p) + (size_t)p.sk_tiles * sizeof(unsigned) + 256; }
 
 // Splits op(A) (tiles_a blocks) and/or op(B) on stream `s`, zeroing n_counters
-// split-tile counters first.
+// split-tile counters and the MMA launch's work counter (when given) first.
 wg_status launch_pack(wg_device *d, cudaStream_t s, const PackArgs &pa, const PackArgs &pb, int64_t k, int64_t kp,
-                      unsigned *counters, int64_t n_counters) {
+                      unsigned *counters, int64_t n_counters, unsigned *next_unit) {
   const int64_t blocks = pa.tiles_r + pb.tiles_r;
   if (blocks == 0) return WG_OK;
   wg_launch_scope scope(d, "sgemm_tf32x3_pack", s);
-  tf32x3_pack<<<(unsigned)blocks, 256, 0, s>>>(pa, pb, k, kp, pa.tiles_r, counters, n_counters);
+  tf32x3_pack<<<(unsigned)blocks, 256, 0, s>>>(pa, pb, k, kp, pa.tiles_r, counters, n_counters, next_unit);
   WG_CUDA(cudaGetLastError());
   return WG_OK;
 }
@@ -596,12 +634,12 @@ wg_status launch_pack(wg_device *d, cudaStream_t s, const PackArgs &pa, const Pa
 // The MMA launch over split operands already in place, then the FFMA launch
 // that computes C instead when `gate` is open; both on d->stream. The last
 // wave's tiles are split along k when sk_room bytes at `sk` hold the plan's
-// partial sums and counters (counters at sk + counter_offset, zeroed
-// beforehand), whole otherwise.
+// partial sums and counters (counters at sk + partial_room, zeroed
+// beforehand), whole otherwise. next_unit is the work counter, zeroed beforehand.
 wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
                      const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
                      float *ahi, float *alo, float *bhi, float *blo, char *sk, size_t partial_room,
-                     int64_t counter_room, const wg_gate &gate) {
+                     int64_t counter_room, unsigned *next_unit, const wg_gate &gate) {
   const Layout L = layout_of(m, n, k);
   const int G = d->sm_count;
   Plan plan = plan_of(G, L, true);
@@ -614,7 +652,8 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
       !make_map(&maps[2], bhi, L.np, L.kp, Sh::BN) || !make_map(&maps[3], blo, L.np, L.kp, Sh::BN))
     return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
   MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, gate, L.tiles_m, L.tiles_n, L.kt, plan.dp_tiles,
-               plan.sk_tiles, plan.sk_split, partials, counters};
+               plan.sk_tiles, plan.sk_split, partials, counters, next_unit,
+               plan.dp_tiles + plan.sk_tiles * plan.sk_split};
   auto kern = tf32x3_mma<Sh>;
   WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
   {
@@ -734,13 +773,14 @@ wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64
   unsigned *counters = reinterpret_cast<unsigned *>(sk + partial_room);
   const uint32_t epoch = wg_next_epoch(d);
   unsigned *flag = d->dwords + WG_DW_FALLBACK;
+  unsigned *next_unit = d->dwords + WG_DW_NEXT_UNIT0;
   wg_status st = launch_pack(d, d->stream, pack_a_args(transA, A, lda, m, L, ahi, alo, flag, epoch),
                              pack_b_args(transB, B, ldb, n, L, bhi, blo, flag, epoch), k, L.kp, counters,
-                             plan.sk_tiles);
+                             plan.sk_tiles, next_unit);
   if (st != WG_OK) return st;
   const wg_gate gate{flag, flag, epoch, epoch};
   return launch_mma(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ahi, alo, bhi, blo, sk,
-                    partial_room, plan.sk_tiles, gate);
+                    partial_room, plan.sk_tiles, next_unit, gate);
 }
 
 // ---- panelled products ----------------------------------------------------
@@ -789,7 +829,7 @@ wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int tr
   float *alo = ahi + LA.a_bytes / sizeof(float);
   unsigned *counters = reinterpret_cast<unsigned *>(p->ws + P.a_region + 2 * P.slot_bytes + P.partial_room);
   st = launch_pack(d, d->side, pack_a_args(transA, A, lda, m, LA, ahi, alo, d->dwords + WG_DW_FALLBACK_A, p->epoch_a),
-                   no_pack(), k, LA.kp, counters, P.counter_room);
+                   no_pack(), k, LA.kp, counters, P.counter_room, nullptr);
   if (st != WG_OK) return st;
   d->stats.calls++;
   return WG_OK;
@@ -809,15 +849,16 @@ wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, in
   if (b_ready) WG_CUDA(cudaStreamWaitEvent(d->side, b_ready, 0));
   unsigned *flag_b = d->dwords + WG_DW_FALLBACK_B0 + slot;
   const uint32_t epoch_b = wg_next_epoch(d);
+  unsigned *next_unit = d->dwords + WG_DW_NEXT_UNIT0 + slot;
   wg_status st = launch_pack(d, d->side, no_pack(), pack_b_args(p->transB, B, ldb, cols, L, bhi, blo, flag_b, epoch_b),
-                             p->k, L.kp, nullptr, 0);
+                             p->k, L.kp, nullptr, 0, next_unit);
   if (st != WG_OK) return st;
   WG_CUDA(cudaEventRecord(d->tc_ev[EV_PACKED], d->side));
   WG_CUDA(cudaStreamWaitEvent(d->stream, d->tc_ev[EV_PACKED], 0));
   char *sk = p->ws + p->a_region + 2 * p->slot_bytes;
   const wg_gate gate{d->dwords + WG_DW_FALLBACK_A, flag_b, p->epoch_a, epoch_b};
   st = launch_mma(d, p->transA, p->transB, p->m, cols, p->k, p->alpha, p->A, p->lda, B, ldb, p->beta, C, ldc, ahi,
-                  alo, bhi, blo, sk, p->partial_room, p->counter_room, gate);
+                  alo, bhi, blo, sk, p->partial_room, p->counter_room, next_unit, gate);
   if (st != WG_OK) return st;
   WG_CUDA(cudaEventRecord(d->tc_ev[EV_SLOT0 + slot], d->stream));
   d->stats.tf32x3_launches++;

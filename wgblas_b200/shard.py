@@ -5,8 +5,9 @@ The reference drives several GPUs only as independent devices
 of its multi-GPU target on top of the C ABI's communicator (wg_comm_*,
 wgblas_b200/csrc/shard.cu). One process per GPU: every rank holds its row
 block of op(A) and of C resident on its GPU (scattered once), and B lives on
-the root; each call broadcasts B in column panels, the GEMM of each panel
-starting as soon as the panel has arrived.
+the root; each call sends B in column panels to the other ranks (a copy-engine
+chain over NVLink, or ncclBroadcast), the GEMM of each panel starting as soon
+as the panel has arrived.
 
 The host-side planning here (``plan_rows``, ``row_block``, ``place_rows``) is
 pure Python/numpy and is what the CPU multi-process tests check.
@@ -118,15 +119,22 @@ def _ptr(g: GpuMatrix) -> ct.c_void_p:
 
 
 def gemm_sharded(comm: Comm, transA: bool, transB: bool, m_local: int, n: int, k: int, alpha, A_local: GpuMatrix,
-                 B: GpuMatrix, beta, C_local: GpuMatrix, root: int = 0, panel_cols: int = 0) -> None:
+                 B: GpuMatrix | None, beta, C_local: GpuMatrix, root: int = 0, panel_cols: int = 0,
+                 ldb: int | None = None) -> None:
     """Queues this rank's C_local := alpha*op(A_local)*op(B) + beta*C_local with B
-    broadcast from `root` (column-major GpuMatrix operands; B is overwritten with
-    root's B on the other ranks). dtype follows the operands (float32 -> sgemm)."""
+    sent from `root` (column-major GpuMatrix operands). B is read on the root
+    only: other ranks may pass None (then give ``ldb``, the root's leading
+    dimension) and receive root's B into the communicator's buffer. dtype follows
+    the operands (float32 -> sgemm)."""
     f64 = np.dtype(C_local.dtype) == np.float64
     fn = nat.lib.wg_dgemm_sharded if f64 else nat.lib.wg_sgemm_sharded
     al, be = (float(alpha), float(beta)) if f64 else (np.float32(alpha), np.float32(beta))
+    if ldb is None:
+        if B is None:
+            raise ValueError("ldb is required when B is None")
+        ldb = B.lda
     nat.check(fn(comm.handle, int(bool(transA)), int(bool(transB)), m_local, n, k, al,
-                 _ptr(A_local) if m_local else None, A_local.lda, _ptr(B), B.lda, root, be,
+                 _ptr(A_local) if m_local else None, A_local.lda, _ptr(B) if B is not None else None, ldb, root, be,
                  _ptr(C_local) if m_local else None, C_local.lda, panel_cols))
 
 
