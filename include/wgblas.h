@@ -125,6 +125,14 @@ typedef struct wg_tc_plan {
 } wg_tc_plan;
 wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_t k, wg_tc_plan *out);
 
+/* Triangle selector of the gemmtr family (sgemmtr/ssyrk/ssyr2k and the d
+ * variants): only that triangle of C is read or written. In the column-major
+ * frame of this API: LOWER is C(i, j) with j <= i, UPPER j >= i (C need not be
+ * square). FULL is plain GEMM. */
+#define WG_UPLO_FULL 0
+#define WG_UPLO_LOWER 1
+#define WG_UPLO_UPPER 2
+
 /* sgemm kernel choice: AUTO picks by shape and alignment; the others force one
  * kernel (tests and benchmarks). */
 #define WG_SGEMM_AUTO 0
@@ -248,6 +256,34 @@ wg_status wg_dgemm_host(wg_device *dev, int transA, int transB, int64_t m, int64
 wg_status wg_sharded_panel_plan(int sm_count, int nranks, int64_t m_local, int64_t n, int64_t k, int64_t *widths,
                                 size_t capacity, size_t *count);
 
+
+/* ---- the gemmtr family ------------------------------------------------------
+ * sgemm / dgemm restricted to one triangle of C: C := uplo(alpha*op(A)*op(B) +
+ * beta*C), only the WG_UPLO_LOWER or WG_UPLO_UPPER triangle (column-major frame)
+ * read or written, tiles wholly outside it skipped. Replaces sgemmtr/dgemmtr
+ * (src/sgemmtr/sgemmtr.mjs:25-278, src/dgemmtr/dgemmtr.mjs); the reference's
+ * ssyrk/ssyr2k/dsyrk/dsyr2k are compositions of these (B := A; two passes, the
+ * second with beta = 1) and are composed the same way by the language layer.
+ * dgemmtr keeps dgemm's quick return ((alpha == 0 or k == 0) and beta == 1). */
+wg_status wg_sgemmtr(wg_device *dev, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
+                     const wg_buffer *A, int64_t offA, int64_t lda, const wg_buffer *B, int64_t offB, int64_t ldb,
+                     float beta, wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms);
+wg_status wg_dgemmtr(wg_device *dev, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                     double alpha, const wg_buffer *A, int64_t offA, int64_t lda, const wg_buffer *B, int64_t offB,
+                     int64_t ldb, double beta, wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms);
+wg_status wg_sgemmtr_dev(wg_device *dev, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                         float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                         float *C, int64_t ldc);
+wg_status wg_dgemmtr_dev(wg_device *dev, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                         double alpha, const double *A, int64_t lda, const double *B, int64_t ldb, double beta,
+                         double *C, int64_t ldc);
+/* Host arrays; C_out receives C_in with the triangle updated. */
+wg_status wg_sgemmtr_host(wg_device *dev, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                          float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                          const float *C_in, float *C_out, int64_t ldc, float *gpu_ms);
+wg_status wg_dgemmtr_host(wg_device *dev, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                          double alpha, const double *A, int64_t lda, const double *B, int64_t ldb, double beta,
+                          const double *C_in, double *C_out, int64_t ldc, float *gpu_ms);
 
 /* ---- multi-GPU: C sharded by row blocks, B broadcast over NVLink (NCCL) ---- */
 /* The reference drives several GPUs only as independent devices with no data

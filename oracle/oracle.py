@@ -226,6 +226,30 @@ def dense(x, m, n):
     return np.asarray(x).reshape(m, n, order="F")
 
 
+def tri_merge(uplo, full, C, m, n, ldc):
+    """gemmtr's write mask (src/shaders/sgemm_large.wgsl:293-297) in the
+    column-major frame: the elements of `full` in the uplo triangle of the m x n
+    block (1 = lower, j <= i; 2 = upper, j >= i), C's own values elsewhere."""
+    out = np.array(C, copy=True)
+    for j in range(n):
+        lo, hi = (j, m) if uplo == 1 else (0, min(j + 1, m))
+        if lo < hi:
+            out[j * ldc + lo: j * ldc + hi] = full[j * ldc + lo: j * ldc + hi]
+    return out
+
+
+def sgemmtr(uplo, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, variant=1, threads=0):
+    """The reference's sgemmtr: sgemm's per-element arithmetic, written only in the triangle."""
+    full = sgemm(transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, variant, threads)
+    return tri_merge(uplo, full, _need(C, np.float32), m, n, ldc)
+
+
+def dgemmtr_fma(uplo, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, threads=0):
+    """dgemmtr in native fp64 (sequential FMA per element), written only in the triangle."""
+    full = dgemm_fma(transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, threads)
+    return tri_merge(uplo, full, _need(C, np.float64), m, n, ldc)
+
+
 def sgemm_bound(m, n, k, alpha, absab, beta, C, ldc):
     """Per-element north-star bound 2*K*2^-24*(|alpha||A||B| + |beta||C|), shape (m, n).
 

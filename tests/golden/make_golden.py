@@ -9,7 +9,14 @@ Outputs
 gemm_edge_cases.json
     Every case of the reference's tests/{sgemm,dgemm}/edge-cases.json and
     edge-cases-column-major.json (inputs copied as data), each with the exact
-    expected C. The reference checks these bit for bit against stdlib
+    expected C.
+gemmtr_edge_cases.json
+    The same for the gemmtr family, tests/{s,d}{gemmtr,syrk,syr2k}/edge-cases*.json:
+    only the uplo triangle of C (col <= row for 'lower', col >= row for 'upper',
+    in C's own terms) changes; syrk is gemmtr with B := A and the other
+    transpose, syr2k two gemmtr passes, the second with beta = 1
+    (src/ssyrk/ssyrk.mjs:29-31, src/ssyr2k/ssyr2k.mjs:25-26), each pass checked
+    to be exact in f32. The reference checks these bit for bit against stdlib
     (tests/sgemm/src/test.sgemm.js:126-164,354-394; tests/dgemm/src/test.dgemm.js).
     Their values are small integers, so the expected output is computed here
     with exact rational arithmetic and then checked to be representable in f32:
@@ -22,8 +29,8 @@ dd_lanes.json
     a non-finite hi.
 validation_params.json
     The parameter specs the reference's sgemm/dgemm validation tests load
-    (tests/validation/params/{device,trans,layout,m,n,k,alpha,beta,A,B,C,ld}.json,
-    read by tests/sgemm/src/test.sgemm.js:23-56), copied as data: the invalid
+    (tests/validation/params/{device,trans,layout,m,n,k,alpha,beta,A,B,C,ld,uplo}.json,
+    read by tests/sgemm/src/test.sgemm.js:23-56 and tests/sgemmtr/src/test.sgemmtr.js), copied as data: the invalid
     values with their expected error substrings and the edge values that must
     not throw. tests/validation_runner.py replays them.
 mulberry32.json
@@ -61,13 +68,15 @@ def c_index(ldc, layout, row, col):
     return col * ldc + row if layout == "column-major" else row * ldc + col
 
 
-def exact_gemm(case):
+def exact_gemm(case, uplo=None):
     layout = case.get("layout", "row-major")
     m, n, k = case["m"], case["n"], case["k"]
     alpha, beta = Fraction(case["alpha"]), Fraction(case["beta"])
     out = list(case["C"])
     for i in range(m):
         for j in range(n):
+            if (uplo == "lower" and j > i) or (uplo == "upper" and j < i):
+                continue
             acc = Fraction(0)
             for p in range(k):
                 acc += Fraction(op_elem(case["A"], case["lda"], layout, case["transA"], i, p)) * \
@@ -93,6 +102,44 @@ def edge_cases(ref):
                     case["routine"] = routine
                     case["source"] = f"tests/{routine}/{fname}"
                     case["expected"] = exact_gemm(case)
+                    cases.append(case)
+    return cases
+
+
+def _flip(trans):
+    return "no-transpose" if trans == "transpose" else "transpose"
+
+
+def exact_tr(case):
+    """Expected C of a gemmtr / syrk / syr2k case (see the module docstring)."""
+    r = case["routine"][1:]
+    g = dict(case)
+    if r == "gemmtr":
+        return exact_gemm(g, case["uplo"])
+    g.update(m=case["n"], transA=case["trans"], transB=_flip(case["trans"]))
+    if r == "syrk":
+        g.update(B=case["A"], ldb=case["lda"])
+        return exact_gemm(g, case["uplo"])
+    first = exact_gemm(g, case["uplo"])
+    g.update(A=case["B"], lda=case["ldb"], B=case["A"], ldb=case["lda"], beta=1, C=first)
+    return exact_gemm(g, case["uplo"])
+
+
+def gemmtr_edge_cases(ref):
+    cases = []
+    keys = {"gemmtr": ("label", "uplo", "transA", "transB", "m", "n", "k", "alpha", "A", "lda", "B", "ldb",
+                       "beta", "C", "ldc"),
+            "syrk": ("label", "uplo", "trans", "n", "k", "alpha", "A", "lda", "beta", "C", "ldc"),
+            "syr2k": ("label", "uplo", "trans", "n", "k", "alpha", "A", "lda", "B", "ldb", "beta", "C", "ldc")}
+    for routine in ("sgemmtr", "dgemmtr", "ssyrk", "dsyrk", "ssyr2k", "dsyr2k"):
+        for fname in ("edge-cases.json", "edge-cases-column-major.json"):
+            with open(os.path.join(ref, "tests", routine, fname)) as fh:
+                for tc in json.load(fh):
+                    case = {k: tc[k] for k in keys[routine[1:]]}
+                    case["layout"] = tc.get("layout", "row-major")
+                    case["routine"] = routine
+                    case["source"] = f"tests/{routine}/{fname}"
+                    case["expected"] = exact_tr(case)
                     cases.append(case)
     return cases
 
@@ -175,7 +222,7 @@ def _dump(obj, name):
 
 
 def validation_params(ref):
-    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld"]
+    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld", "uplo"]
     out = {}
     for name in names:
         with open(os.path.join(ref, "tests", "validation", "params", f"{name}.json")) as fh:
@@ -186,6 +233,7 @@ def validation_params(ref):
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.path.join(HERE, "..", "..", "..", "reference")
     _dump(edge_cases(ref), "gemm_edge_cases.json")
+    _dump(gemmtr_edge_cases(ref), "gemmtr_edge_cases.json")
     _dump(dd_lanes(), "dd_lanes.json")
     _dump(validation_params(ref), "validation_params.json")
     seeds = [0, 1, 2, 3, 42, 100, 111, 112, 113, 200, 300]

@@ -1,12 +1,15 @@
-"""Replays the reference's spec-driven argument validation for sgemm / dgemm.
+"""Replays the reference's spec-driven argument validation for sgemm / dgemm and
+the gemmtr family (sgemmtr, ssyrk, ssyr2k and their d twins).
 
 Follows tests/helpers/validation.js (runValidation, :455-560): a baseline
 argument set is built from the specs in tests/golden/validation_params.json
 (the reference's tests/validation/params/*.json); each invalid entry replaces
 exactly one argument and must raise an error whose message contains the
 entry's text, and each edge entry must not raise. The spec set per routine is
-the one tests/sgemm/src/test.sgemm.js:23-56 and tests/dgemm/src/test.dgemm.js:36-88
-assemble.
+the one tests/sgemm/src/test.sgemm.js:23-56, tests/dgemm/src/test.dgemm.js:36-88,
+tests/sgemmtr/src/test.sgemmtr.js, tests/ssyrk/src/test.ssyrk.js and
+tests/ssyr2k/src/test.ssyr2k.js assemble (the d twins derive the Float64Array
+specs the same way).
 """
 from __future__ import annotations
 
@@ -40,23 +43,37 @@ def _derive64(spec):
 
 def build_specs(routine: str) -> dict:
     P = load_golden("validation_params.json", decode=False)
+    rank = routine[1:] in ("syrk", "syr2k")
     n_spec = copy.deepcopy(P["n"])
     n_spec["baseline"] = 2
     n_spec["edge"] = [e for e in n_spec["edge"] if e.get("value") != -1]
     n_spec["invalid"] = n_spec["invalid"] + [
-        {"value": -1, "error": "m, n, and k must be non-negative", "label": "negative"}]
+        {"value": -1, "error": "must be non-negative" if rank else "m, n, and k must be non-negative",
+         "label": "negative"}]
     m_spec = copy.deepcopy(P["m"])
     m_spec["baseline"] = 2
     a_base = copy.deepcopy(P["A"])
     lvl3 = a_base.pop("level-3")
     a_spec = {**a_base, **lvl3}
-    specs = {
-        "device": P["device"], "transA": P["trans"], "transB": P["trans"], "layout": P["layout"],
-        "m": m_spec, "n": n_spec, "k": P["k"], "alpha": P["alpha"], "beta": P["beta"],
-        "A": a_spec, "lda": P["ld"], "B": P["B"], "ldb": P["ld"], "C": P["C"], "ldc": P["ld"],
-    }
-    if routine == "dgemm":
-        a64 = copy.deepcopy(a_spec)
+    if rank:
+        specs = {"device": P["device"], "uplo": P["uplo"], "trans": P["trans"], "layout": P["layout"],
+                 "n": n_spec, "k": P["k"], "alpha": P["alpha"], "beta": P["beta"],
+                 "A": {**a_spec, "dependsOn": ["n", "k", "lda", "trans"]}, "lda": P["ld"]}
+        if routine[1:] == "syr2k":
+            specs["B"] = {**copy.deepcopy(P["B"]), "dependsOn": ["n", "k", "ldb", "trans"]}
+            specs["ldb"] = P["ld"]
+        specs["C"] = {**copy.deepcopy(P["C"]), "dependsOn": ["n", "ldc"]}
+        specs["ldc"] = P["ld"]
+    else:
+        specs = {
+            "device": P["device"], "transA": P["trans"], "transB": P["trans"], "layout": P["layout"],
+            "m": m_spec, "n": n_spec, "k": P["k"], "alpha": P["alpha"], "beta": P["beta"],
+            "A": a_spec, "lda": P["ld"], "B": P["B"], "ldb": P["ld"], "C": P["C"], "ldc": P["ld"],
+        }
+        if routine.endswith("gemmtr"):
+            specs = {"device": specs.pop("device"), "uplo": P["uplo"], **specs}
+    if routine.startswith("d"):
+        a64 = copy.deepcopy(specs["A"])
         a64["type"] = "float64array"
         for e in a64["invalid"]:
             e["error"] = e["error"].replace("Float32Array", "Float64Array")
@@ -64,8 +81,9 @@ def build_specs(routine: str) -> dict:
                                "error": "must be a Float64Array-backed GpuMatrix",
                                "label": "GpuMatrix backed by the wrong dtype (Float32Array)"})
         specs["A"] = a64
-        specs["B"] = _derive64(P["B"])
-        specs["C"] = _derive64(P["C"])
+        if "B" in specs:
+            specs["B"] = {**_derive64(P["B"]), "dependsOn": specs["B"]["dependsOn"]}
+        specs["C"] = {**_derive64(P["C"]), "dependsOn": specs["C"]["dependsOn"]}
     return specs
 
 
@@ -83,8 +101,10 @@ def _matrix_len(depends_on, dims):
         rows, cols = (dims[d2], dims[d1]) if cm else (dims[d1], dims[d2])
         no_t = dims.get(trans_key, "no-transpose") == "no-transpose"
         outer, inner = (rows, cols) if no_t else (cols, rows)
-    else:  # plain m x n (C)
+    elif "m" in depends_on:  # plain m x n (C)
         outer, inner = (dims["n"], dims["m"]) if cm else (dims["m"], dims["n"])
+    else:  # n x n (the C of syrk / syr2k)
+        outer = inner = dims["n"]
     return max(0, (outer - 1) * dims[ld_key] + inner)
 
 
@@ -136,5 +156,12 @@ def cases(routine, device, kind, make_wrong_dtype_matrix=None):
 
 
 def call(fn, a):
-    return fn(a["device"], a["transA"], a["transB"], a["m"], a["n"], a["k"], a["alpha"], a["A"],
+    if "trans" in a:  # syrk / syr2k
+        if "B" in a:
+            return fn(a["device"], a["uplo"], a["trans"], a["n"], a["k"], a["alpha"], a["A"], a["lda"], a["B"],
+                      a["ldb"], a["beta"], a["C"], a["ldc"], a["layout"])
+        return fn(a["device"], a["uplo"], a["trans"], a["n"], a["k"], a["alpha"], a["A"], a["lda"], a["beta"],
+                  a["C"], a["ldc"], a["layout"])
+    head = (a["device"], a["uplo"]) if "uplo" in a else (a["device"],)
+    return fn(*head, a["transA"], a["transB"], a["m"], a["n"], a["k"], a["alpha"], a["A"],
               a["lda"], a["B"], a["ldb"], a["beta"], a["C"], a["ldc"], a["layout"])

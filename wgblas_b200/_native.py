@@ -117,6 +117,20 @@ _sig("wg_sgemm_host", _st, *_gemm_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void
      ct.c_void_p, ct.c_void_p, _i64, _f32p)
 _sig("wg_dgemm_host", _st, *_gemm_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double,
      ct.c_void_p, ct.c_void_p, _i64, _f32p)
+WG_UPLO_FULL, WG_UPLO_LOWER, WG_UPLO_UPPER = 0, 1, 2
+_tr_dims = [c_dev_p, ct.c_int] + _gemm_dims[1:]
+_sig("wg_sgemmtr", _st, *_tr_dims, ct.c_float, c_buf_p, _i64, _i64, c_buf_p, _i64, _i64, ct.c_float,
+     c_buf_p, _i64, _i64, _f32p)
+_sig("wg_dgemmtr", _st, *_tr_dims, ct.c_double, c_buf_p, _i64, _i64, c_buf_p, _i64, _i64, ct.c_double,
+     c_buf_p, _i64, _i64, _f32p)
+_sig("wg_sgemmtr_dev", _st, *_tr_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_float,
+     ct.c_void_p, _i64)
+_sig("wg_dgemmtr_dev", _st, *_tr_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double,
+     ct.c_void_p, _i64)
+_sig("wg_sgemmtr_host", _st, *_tr_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_float,
+     ct.c_void_p, ct.c_void_p, _i64, _f32p)
+_sig("wg_dgemmtr_host", _st, *_tr_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double,
+     ct.c_void_p, ct.c_void_p, _i64, _f32p)
 c_comm_p = ct.c_void_p
 _sig("wg_comm_unique_id", _st, ct.c_char_p, ct.c_size_t)
 _sig("wg_comm_init_rank", _st, c_dev_p, ct.c_int, ct.c_int, ct.c_char_p, ct.c_size_t, ct.c_int, ct.POINTER(c_comm_p))

@@ -41,7 +41,10 @@ __device__ __forceinline__ void dmma_16x8x8(double (&d)[4], const double (&a)[4]
 template <int TA, int TB>
 __global__ void __launch_bounds__(NT, 1)
 dgemm_dmma_kernel(int64_t m, int64_t n, int64_t k, double alpha, const double *__restrict__ A, int64_t lda,
-                  const double *__restrict__ B, int64_t ldb, double beta, double *__restrict__ C, int64_t ldc) {
+                  const double *__restrict__ B, int64_t ldb, double beta, double *__restrict__ C, int64_t ldc,
+                  int uplo) {
+  // gemmtr: a tile with no element in the triangle writes nothing (uniform exit, before any barrier).
+  if (wg_tile_outside(uplo, (int64_t)blockIdx.x * BM, BM, (int64_t)blockIdx.y * BN, BN)) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   double *As = reinterpret_cast<double *>(smem_raw);  // [2][BK][LDS_A]
   double *Bs = As + 2 * BK * LDS_A;                  // [2][BK][LDS_B]
@@ -146,7 +149,7 @@ dgemm_dmma_kernel(int64_t m, int64_t n, int64_t k, double alpha, const double *_
       for (int v = 0; v < 4; v++) {
         const int64_t row = m0 + wm + mt * 16 + g + 8 * (v >> 1);
         const int64_t col = n0 + wn + nt * 8 + 2 * t + (v & 1);
-        old[nt][v] = (beta != 0.0 && row < m && col < n) ? C[row + col * ldc] : 0.0;
+        old[nt][v] = (beta != 0.0 && row < m && col < n && wg_in_triangle(uplo, row, col)) ? C[row + col * ldc] : 0.0;
       }
 #pragma unroll
     for (int nt = 0; nt < 4; nt++)
@@ -154,7 +157,7 @@ dgemm_dmma_kernel(int64_t m, int64_t n, int64_t k, double alpha, const double *_
       for (int v = 0; v < 4; v++) {
         const int64_t row = m0 + wm + mt * 16 + g + 8 * (v >> 1);
         const int64_t col = n0 + wn + nt * 8 + 2 * t + (v & 1);
-        if (row < m && col < n) {
+        if (row < m && col < n && wg_in_triangle(uplo, row, col)) {
           const double s = (alpha == 0.0) ? 0.0 : __dmul_rn(alpha, acc[mt][nt][v]);
           C[row + col * ldc] = (beta != 0.0) ? __fma_rn(beta, old[nt][v], s) : s;
         }
@@ -164,12 +167,12 @@ dgemm_dmma_kernel(int64_t m, int64_t n, int64_t k, double alpha, const double *_
 
 template <int TA, int TB>
 cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, double alpha, const double *A, int64_t lda,
-                      const double *B, int64_t ldb, double beta, double *C, int64_t ldc) {
+                      const double *B, int64_t ldb, double beta, double *C, int64_t ldc, int uplo) {
   auto kern = dgemm_dmma_kernel<TA, TB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
-  kern<<<grid, NT, SMEM, s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+  kern<<<grid, NT, SMEM, s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
   return cudaGetLastError();
 }
 
@@ -177,11 +180,11 @@ cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, double al
 
 cudaError_t wg_launch_dgemm_dmma(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
                                  double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
-                                 double beta, double *C, int64_t ldc) {
+                                 double beta, double *C, int64_t ldc, int uplo) {
   if ((n + BN - 1) / BN > 65535) return cudaErrorInvalidConfiguration;
   if (transA)
-    return transB ? launch_tt<1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc)
-                  : launch_tt<1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
-  return transB ? launch_tt<0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc)
-                : launch_tt<0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+    return transB ? launch_tt<1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo)
+                  : launch_tt<1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
+  return transB ? launch_tt<0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo)
+                : launch_tt<0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
 }

@@ -59,14 +59,14 @@ wg_status check_arch(const wg_device *d) {
 
 template <typename T>
 wg_status gemm_launch(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
-                      const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+                      const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc, int uplo = 0);
 }  // namespace
 
 template <typename T>
 wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
-                          const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc) {
+                          const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc, int uplo) {
   if (m == 0 || n == 0) return WG_OK;
-  return gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+  return gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
 }
 
 namespace {
@@ -78,11 +78,11 @@ namespace {
 template <>
 wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                              float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
-                             float beta, float *C, int64_t ldc) {
+                             float beta, float *C, int64_t ldc, int uplo) {
   cudaStream_t s = d->stream;
   if (alpha == 0.0f || k == 0) {
     wg_launch_scope scope(d, "scale");
-    WG_CUDA(wg_launch_scale<float>(s, m, n, alpha, beta, C, ldc));
+    WG_CUDA(wg_launch_scale<float>(s, m, n, alpha, beta, C, ldc, uplo));
     return WG_OK;
   }
   d->stats.calls++;
@@ -100,7 +100,7 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
     const size_t bytes = wg_tf32x3_workspace_bytes_sk(d, m, n, k);
     wg_status st = wg_workspace(d, bytes, &ws);
     if (st != WG_OK) return st;
-    st = wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes);
+    st = wg_sgemm_tf32x3(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes, uplo);
     if (st != WG_OK) return st;
     d->stats.tf32x3_launches++;
     return WG_OK;
@@ -108,18 +108,18 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
   d->stats.simt_launches++;
   wg_launch_scope scope(d, "sgemm_simt");
   WG_CUDA(wg_launch_gemm_simt<float>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
-                                     d->dwords, nullptr));
+                                     d->dwords, nullptr, uplo));
   return WG_OK;
 }
 
 template <>
 wg_status gemm_launch<double>(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                               double alpha, const double *A, int64_t lda, const double *B,
-                              int64_t ldb, double beta, double *C, int64_t ldc) {
+                              int64_t ldb, double beta, double *C, int64_t ldc, int uplo) {
   cudaStream_t s = d->stream;
   if (alpha == 0.0 || k == 0) {
     wg_launch_scope scope(d, "scale");
-    WG_CUDA(wg_launch_scale<double>(s, m, n, alpha, beta, C, ldc));
+    WG_CUDA(wg_launch_scale<double>(s, m, n, alpha, beta, C, ldc, uplo));
     return WG_OK;
   }
   // The DMMA kernel needs a few k steps and a grid worth filling; small calls run
@@ -128,12 +128,12 @@ wg_status gemm_launch<double>(wg_device *d, int transA, int transB, int64_t m, i
                     (d->dgemm_path == WG_DGEMM_AUTO && k >= 16 && (double)m * (double)n >= 128.0 * 128.0);
   if (dmma) {
     wg_launch_scope scope(d, "dgemm_dmma");
-    WG_CUDA(wg_launch_dgemm_dmma(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc));
+    WG_CUDA(wg_launch_dgemm_dmma(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo));
     return WG_OK;
   }
   wg_launch_scope scope(d, "dgemm_simt");
   WG_CUDA(wg_launch_gemm_simt<double>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C,
-                                      ldc, d->dwords, nullptr));
+                                      ldc, d->dwords, nullptr, uplo));
   return WG_OK;
 }
 
@@ -150,10 +150,10 @@ bool quick_return<double>(int64_t k, double alpha, double beta) {
 template <typename T>
 wg_status gemm_timed(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                      const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                     float *gpu_ms) {
+                     float *gpu_ms, int uplo) {
   const bool timing = gpu_ms && (d->flags & WG_DEVICE_TIMING);
   if (timing) WG_CUDA(cudaEventRecord(d->ev_start, d->stream));
-  wg_status st = gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+  wg_status st = gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
   if (st != WG_OK) return st;
   if (timing) {
     WG_CUDA(cudaEventRecord(d->ev_stop, d->stream));
@@ -166,9 +166,12 @@ wg_status gemm_timed(wg_device *d, int transA, int transB, int64_t m, int64_t n,
 template <typename T>
 wg_status gemm_buffers(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                        const wg_buffer *A, int64_t offA, int64_t lda, const wg_buffer *B, int64_t offB,
-                       int64_t ldb, T beta, wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms) {
+                       int64_t ldb, T beta, wg_buffer *C, int64_t offC, int64_t ldc, float *gpu_ms,
+                       int uplo = WG_UPLO_FULL) {
   if (gpu_ms) *gpu_ms = 0.0f;
   if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  if (uplo < WG_UPLO_FULL || uplo > WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
   wg_status st = check_dims(transA, transB, m, n, k, lda, ldb, ldc);
   if (st != WG_OK) return st;
   if (m == 0 || n == 0) return WG_OK;  // src/sgemm/sgemm.mjs:83
@@ -190,13 +193,16 @@ wg_status gemm_buffers(wg_device *d, int transA, int transB, int64_t m, int64_t 
   if (st != WG_OK) return st;
   wg_device_guard guard(d->ordinal);
   return gemm_timed<T>(d, transA, transB, m, n, k, alpha, (const T *)A->ptr + offA, lda,
-                       (const T *)B->ptr + offB, ldb, beta, (T *)C->ptr + offC, ldc, gpu_ms);
+                       (const T *)B->ptr + offB, ldb, beta, (T *)C->ptr + offC, ldc, gpu_ms, uplo);
 }
 
 template <typename T>
 wg_status gemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
-                   const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc) {
+                   const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
+                   int uplo = WG_UPLO_FULL) {
   if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  if (uplo < WG_UPLO_FULL || uplo > WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
   wg_status st = check_dims(transA, transB, m, n, k, lda, ldb, ldc);
   if (st != WG_OK) return st;
   if (m == 0 || n == 0 || quick_return<T>(k, alpha, beta)) return WG_OK;
@@ -205,7 +211,7 @@ wg_status gemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, i
   st = check_arch(d);
   if (st != WG_OK) return st;
   wg_device_guard guard(d->ordinal);
-  return gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
+  return gemm_launch<T>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
 }
 
 // Copies the rows x cols block of a column-major host matrix (leading dimension
@@ -266,15 +272,18 @@ struct HostPipe {
 template <typename T>
 wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
                     const T *A, int64_t lda, const T *B, int64_t ldb, T beta, const T *C_in, T *C_out,
-                    int64_t ldc, float *gpu_ms) {
+                    int64_t ldc, float *gpu_ms, int uplo = WG_UPLO_FULL) {
   if (gpu_ms) *gpu_ms = 0.0f;
   if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  if (uplo < WG_UPLO_FULL || uplo > WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
   wg_status st = check_dims(transA, transB, m, n, k, lda, ldb, ldc);
   if (st != WG_OK) return st;
   if (!C_out) return wg_fail(WG_ERR_INVALID_ARGUMENT, "C_out is NULL");
   if (m == 0 || n == 0) return WG_OK;
   const bool reads_ab = k > 0 && alpha != T(0);
-  const bool reads_c = beta != T(0);
+  // gemmtr leaves C outside the triangle as it came in, so C always goes up.
+  const bool reads_c = beta != T(0) || uplo != WG_UPLO_FULL;
   if ((reads_ab && (!A || !B)) || (reads_c && !C_in))
     return wg_fail(WG_ERR_INVALID_ARGUMENT, "operand pointer is NULL");
   if (quick_return<T>(k, alpha, beta)) {
@@ -295,7 +304,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   const size_t nb = reads_ab ? (size_t)(sb.rows * sb.cols) : 0;
   const size_t nc = (size_t)(m * n);
   const int64_t lda_d = sa.rows > 0 ? sa.rows : 1, ldb_d = sb.rows > 0 ? sb.rows : 1;
-  const int64_t panel = reads_ab ? host_panel_cols(m, n, k) : n;
+  const int64_t panel = reads_ab && uplo == WG_UPLO_FULL ? host_panel_cols(m, n, k) : n;
   const int64_t panels = (n + panel - 1) / panel;
   // sgemm panels on the tensor cores run as one wg_tc_product, whose op(B)
   // splits overlap the previous panel's MMA.
@@ -350,7 +359,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
     } else {
       e = cudaStreamWaitEvent(s, pipe.ev_b[j], 0);
       if (e != cudaSuccess) break;
-      st = panels == 1 ? gemm_launch<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta, dC, m)
+      st = panels == 1 ? gemm_launch<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta, dC, m, uplo)
                        : wg_gemm_panel<T>(d, transA, transB, m, cols, k, alpha, dA, lda_d, bp, ldb_d, beta,
                                           dC + j0 * m, m);
     }
@@ -398,10 +407,10 @@ template wg_status wg_gemm_panel<double>(wg_device *, int, int, int64_t, int64_t
                                          int64_t, const double *, int64_t, double, double *, int64_t);
 
 template wg_status wg_gemm_enqueue<float>(wg_device *, int, int, int64_t, int64_t, int64_t, float, const float *,
-                                          int64_t, const float *, int64_t, float, float *, int64_t);
+                                          int64_t, const float *, int64_t, float, float *, int64_t, int);
 template wg_status wg_gemm_enqueue<double>(wg_device *, int, int, int64_t, int64_t, int64_t, double,
                                            const double *, int64_t, const double *, int64_t, double, double *,
-                                           int64_t);
+                                           int64_t, int);
 
 extern "C" wg_status wg_sgemm(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                               float alpha, const wg_buffer *A, int64_t offA, int64_t lda,
@@ -444,4 +453,65 @@ extern "C" wg_status wg_dgemm_host(wg_device *d, int transA, int transB, int64_t
                                    int64_t ldc, float *gpu_ms) {
   return gemm_host<double>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C_in, C_out, ldc,
                            gpu_ms);
+}
+
+// ---- the gemmtr family (src/sgemmtr/sgemmtr.mjs, src/dgemmtr/dgemmtr.mjs) ----
+// sgemm/dgemm with only the `uplo` triangle of C read or written; ssyrk/ssyr2k
+// and the d variants are built on these, as the reference builds them on its
+// gemmtr kernel (src/ssyrk/ssyrk.mjs:31, src/ssyr2k/ssyr2k.mjs:25-26).
+
+extern "C" wg_status wg_sgemmtr(wg_device *d, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                float alpha, const wg_buffer *A, int64_t offA, int64_t lda, const wg_buffer *B,
+                                int64_t offB, int64_t ldb, float beta, wg_buffer *C, int64_t offC, int64_t ldc,
+                                float *gpu_ms) {
+  if (uplo != WG_UPLO_LOWER && uplo != WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
+  return gemm_buffers<float>(d, transA, transB, m, n, k, alpha, A, offA, lda, B, offB, ldb, beta, C, offC, ldc,
+                             gpu_ms, uplo);
+}
+
+extern "C" wg_status wg_dgemmtr(wg_device *d, int uplo, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                double alpha, const wg_buffer *A, int64_t offA, int64_t lda, const wg_buffer *B,
+                                int64_t offB, int64_t ldb, double beta, wg_buffer *C, int64_t offC, int64_t ldc,
+                                float *gpu_ms) {
+  if (uplo != WG_UPLO_LOWER && uplo != WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
+  return gemm_buffers<double>(d, transA, transB, m, n, k, alpha, A, offA, lda, B, offB, ldb, beta, C, offC, ldc,
+                              gpu_ms, uplo);
+}
+
+extern "C" wg_status wg_sgemmtr_dev(wg_device *d, int uplo, int transA, int transB, int64_t m, int64_t n,
+                                    int64_t k, float alpha, const float *A, int64_t lda, const float *B,
+                                    int64_t ldb, float beta, float *C, int64_t ldc) {
+  if (uplo != WG_UPLO_LOWER && uplo != WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
+  return gemm_dev<float>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
+}
+
+extern "C" wg_status wg_dgemmtr_dev(wg_device *d, int uplo, int transA, int transB, int64_t m, int64_t n,
+                                    int64_t k, double alpha, const double *A, int64_t lda, const double *B,
+                                    int64_t ldb, double beta, double *C, int64_t ldc) {
+  if (uplo != WG_UPLO_LOWER && uplo != WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
+  return gemm_dev<double>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
+}
+
+extern "C" wg_status wg_sgemmtr_host(wg_device *d, int uplo, int transA, int transB, int64_t m, int64_t n,
+                                     int64_t k, float alpha, const float *A, int64_t lda, const float *B,
+                                     int64_t ldb, float beta, const float *C_in, float *C_out, int64_t ldc,
+                                     float *gpu_ms) {
+  if (uplo != WG_UPLO_LOWER && uplo != WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
+  return gemm_host<float>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C_in, C_out, ldc, gpu_ms,
+                          uplo);
+}
+
+extern "C" wg_status wg_dgemmtr_host(wg_device *d, int uplo, int transA, int transB, int64_t m, int64_t n,
+                                     int64_t k, double alpha, const double *A, int64_t lda, const double *B,
+                                     int64_t ldb, double beta, const double *C_in, double *C_out, int64_t ldc,
+                                     float *gpu_ms) {
+  if (uplo != WG_UPLO_LOWER && uplo != WG_UPLO_UPPER)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "uplo must be 'lower' or 'upper'.");
+  return gemm_host<double>(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C_in, C_out, ldc, gpu_ms,
+                           uplo);
 }

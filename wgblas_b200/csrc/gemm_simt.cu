@@ -82,12 +82,14 @@ template <typename T, int TA, int TB>
 __global__ void __launch_bounds__(NT, 1)
 gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__ A, int64_t lda,
                  const T *__restrict__ B, int64_t ldb, T beta, T *__restrict__ C, int64_t ldc,
-                 unsigned *dwords, wg_gate gate, int gated) {
+                 unsigned *dwords, wg_gate gate, int gated, int uplo) {
   if (gated) {
     // Device-side fallback of the 3xTF32 path: run only if its operand check failed.
     if (!wg_gate_open(gate)) return;
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicAdd(dwords + WG_DW_FALLBACKS, 1u);
   }
+  // gemmtr: a tile with no element in the triangle writes nothing (uniform exit, before any barrier).
+  if (wg_tile_outside(uplo, (int64_t)blockIdx.x * BM, BM, (int64_t)blockIdx.y * BN, BN)) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T *As = reinterpret_cast<T *>(smem_raw);       // [2][BK][lda_s]
   T *Bs = As + 2 * BK * lda_s<T>();             // [2][BK][ldb_s]
@@ -182,7 +184,8 @@ gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__
         if (gi >= m) continue;
         T *cp = C + gi + gj * ldc;
         T v[4], old[4] = {T(0), T(0), T(0), T(0)};
-        const bool full = gi + 3 < m && (reinterpret_cast<uintptr_t>(cp) % 16 == 0);
+        const bool full = gi + 3 < m && (reinterpret_cast<uintptr_t>(cp) % 16 == 0) &&
+                          wg_in_triangle(uplo, gi, gj) && wg_in_triangle(uplo, gi + 3, gj);
         if (full) {
           if (beta != T(0)) Vec4<T>::load(old, cp);
 #pragma unroll
@@ -191,7 +194,7 @@ gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__
         } else {
 #pragma unroll
           for (int q = 0; q < 4; q++)
-            if (gi + q < m) {
+            if (gi + q < m && wg_in_triangle(uplo, gi + q, gj)) {
               T o = (beta != T(0)) ? cp[q] : T(0);
               cp[q] = epilogue(acc[h * 4 + q][g * 4 + r], alpha, beta, o);
             }
@@ -202,11 +205,12 @@ gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__
 
 // C = epilogue(0) elementwise: the k == 0 and alpha == 0 cases.
 template <typename T>
-__global__ void scale_kernel(int64_t m, int64_t n, T alpha, T beta, T *__restrict__ C, int64_t ldc) {
+__global__ void scale_kernel(int64_t m, int64_t n, T alpha, T beta, T *__restrict__ C, int64_t ldc, int uplo) {
   const int64_t total = m * n;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = e % m, j = e / m;
+    if (!wg_in_triangle(uplo, i, j)) continue;
     T *cp = C + i + j * ldc;
     const T old = (beta != T(0)) ? *cp : T(0);
     *cp = epilogue(T(0), alpha, beta, old);
@@ -216,7 +220,7 @@ __global__ void scale_kernel(int64_t m, int64_t n, T alpha, T beta, T *__restric
 template <typename T, int TA, int TB>
 cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, T alpha, const T *A,
                       int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                      unsigned *dwords, const wg_gate *gate) {
+                      unsigned *dwords, const wg_gate *gate, int uplo) {
   auto kern = gemm_simt_kernel<T, TA, TB>;
   // Per-device attribute: set on every launch so each device that runs the kernel has it.
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -225,7 +229,7 @@ cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, T alpha, 
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
   const wg_gate g = gate ? *gate : wg_gate{nullptr, nullptr, 0u, 0u};
   kern<<<grid, NT, smem_bytes<T>(), s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, g,
-                                          gate ? 1 : 0);
+                                          gate ? 1 : 0, uplo);
   return cudaGetLastError();
 }
 
@@ -235,31 +239,31 @@ template <typename T>
 cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t m, int64_t n,
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
-                                const wg_gate *gate) {
+                                const wg_gate *gate, int uplo) {
   if ((n + BN - 1) / BN > 65535) return cudaErrorInvalidConfiguration;
   if (transA) {
-    return transB ? launch_tt<T, 1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate)
-                  : launch_tt<T, 1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate);
+    return transB ? launch_tt<T, 1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo)
+                  : launch_tt<T, 1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo);
   }
-  return transB ? launch_tt<T, 0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate)
-                : launch_tt<T, 0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate);
+  return transB ? launch_tt<T, 0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo)
+                : launch_tt<T, 0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo);
 }
 
 template <typename T>
-cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T beta, T *C, int64_t ldc) {
+cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T beta, T *C, int64_t ldc, int uplo) {
   const int64_t total = m * n;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
-  scale_kernel<T><<<(unsigned)blocks, 256, 0, s>>>(m, n, alpha, beta, C, ldc);
+  scale_kernel<T><<<(unsigned)blocks, 256, 0, s>>>(m, n, alpha, beta, C, ldc, uplo);
   return cudaGetLastError();
 }
 
 template cudaError_t wg_launch_gemm_simt<float>(cudaStream_t, int, int, int64_t, int64_t, int64_t, float,
                                                 const float *, int64_t, const float *, int64_t, float,
-                                                float *, int64_t, unsigned *, const wg_gate *);
+                                                float *, int64_t, unsigned *, const wg_gate *, int);
 template cudaError_t wg_launch_gemm_simt<double>(cudaStream_t, int, int, int64_t, int64_t, int64_t, double,
                                                  const double *, int64_t, const double *, int64_t, double,
-                                                 double *, int64_t, unsigned *, const wg_gate *);
-template cudaError_t wg_launch_scale<float>(cudaStream_t, int64_t, int64_t, float, float, float *, int64_t);
-template cudaError_t wg_launch_scale<double>(cudaStream_t, int64_t, int64_t, double, double, double *, int64_t);
+                                                 double *, int64_t, unsigned *, const wg_gate *, int);
+template cudaError_t wg_launch_scale<float>(cudaStream_t, int64_t, int64_t, float, float, float *, int64_t, int);
+template cudaError_t wg_launch_scale<double>(cudaStream_t, int64_t, int64_t, double, double, double *, int64_t, int);

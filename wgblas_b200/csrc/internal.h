@@ -30,6 +30,24 @@ struct wg_gate {
   const unsigned *a, *b;
   uint32_t ea, eb;
 };
+
+// The triangle of an m x n C that gemmtr-style calls update, in the column-major
+// frame: WG_UPLO_FULL every element, WG_UPLO_LOWER C(i, j) with j <= i,
+// WG_UPLO_UPPER j >= i (src/shaders/sgemm_large.wgsl:293-297).
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline bool wg_in_triangle(int uplo, int64_t i, int64_t j) {
+  return uplo == WG_UPLO_FULL || (uplo == WG_UPLO_LOWER ? j <= i : j >= i);
+}
+// True when no element of the block [i0, i0 + h) x [j0, j0 + w) is in the triangle
+// (such a tile is skipped: src/shaders/sgemm_large.wgsl:78-83).
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline bool wg_tile_outside(int uplo, int64_t i0, int64_t h, int64_t j0, int64_t w) {
+  return (uplo == WG_UPLO_LOWER && j0 > i0 + h - 1) || (uplo == WG_UPLO_UPPER && j0 + w - 1 < i0);
+}
 #ifdef __CUDACC__
 __device__ __forceinline__ bool wg_gate_open(const wg_gate &g) {
   return *(volatile const unsigned *)g.a == g.ea || *(volatile const unsigned *)g.b == g.eb;
@@ -125,7 +143,7 @@ struct wg_device_guard {
 // dispatcher (no argument checks, no dgemm quick return: callers check).
 template <typename T>
 wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, T alpha,
-                          const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc);
+                          const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc, int uplo = 0);
 
 // One column panel (cols columns) of a product queued panel by panel on
 // d->stream, through the dispatcher (sgemm products on the tensor cores use
@@ -184,17 +202,17 @@ template <typename T>
 cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t m, int64_t n,
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
-                                const wg_gate *gate);
+                                const wg_gate *gate, int uplo = 0);
 
 // dgemm on the FP64 tensor-core (DMMA) path, mma.sync.m16n8k8.f64 (dgemm_dmma.cu).
 cudaError_t wg_launch_dgemm_dmma(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
                                  double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
-                                 double beta, double *C, int64_t ldc);
+                                 double beta, double *C, int64_t ldc, int uplo = 0);
 
 // C = (alpha == 0 ? 0 : alpha*0) + beta*C elementwise — the k == 0 / alpha == 0 cases.
 template <typename T>
 cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T beta, T *C,
-                            int64_t ldc);
+                            int64_t ldc, int uplo = 0);
 
 // Bytes of scratch the 3xTF32 path needs for this shape: the split operands
 // alone (whole-tile scheduling), or with the stream-K partial sums and counters.
@@ -212,5 +230,5 @@ bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 // partial sums (wg_tf32x3_workspace_bytes_sk), whole tiles otherwise.
 wg_status wg_sgemm_tf32x3(wg_device *dev, int transA, int transB, int64_t m, int64_t n,
                           int64_t k, float alpha, const float *A, int64_t lda, const float *B,
-                          int64_t ldb, float beta, float *C, int64_t ldc, void *ws, size_t ws_bytes);
+                          int64_t ldb, float beta, float *C, int64_t ldc, void *ws, size_t ws_bytes, int uplo = 0);
 uint32_t wg_next_epoch(wg_device *dev);

@@ -163,6 +163,7 @@ struct MmaArgs {
   unsigned *counters;        // split tiles: one arrival counter each
   unsigned *next_unit;       // work counter: units handed out beyond the first gridDim.x
   int units;                 // dp_tiles + sk_tiles * sk_split
+  int uplo;                  // WG_UPLO_*: tiles with no element in the triangle are skipped
 };
 
 // Tile t -> (tile row, tile column), GROUP_M tile rows at a time.
@@ -291,6 +292,13 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       const int slot = n % UQ;
       const uint32_t uph = (uint32_t)(n / UQ) & 1u;
       int un = n == 0 ? (int)blockIdx.x : (int)gridDim.x + (int)atomicAdd(args.next_unit, 1u);
+      // gemmtr: tiles with no element in the triangle are not computed at all.
+      while (args.uplo != WG_UPLO_FULL && un < args.units) {
+        int tm0, tn0;
+        raster(args, decode(args, un).t, tm0, tn0);
+        if (!wg_tile_outside(args.uplo, (int64_t)tm0 * BM, BM, (int64_t)tn0 * S::BN, S::BN)) break;
+        un = (int)gridDim.x + (int)atomicAdd(args.next_unit, 1u);
+      }
       if (un >= args.units) un = -1;  // no work left: tells the other roles to stop
       if (!wgtc::mbar_wait_bounded(&uq_empty[slot], uph ^ 1u, WAIT_BUDGET) || *abort_flag) {
         atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
@@ -490,13 +498,13 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
 #pragma unroll
               for (int j = 0; j < 32; j++) {
                 const int64_t col = n0 + c + j;
-                old[j] = col < args.n ? args.C[row + col * args.ldc] : 0.0f;
+                old[j] = col < args.n && wg_in_triangle(args.uplo, row, col) ? args.C[row + col * args.ldc] : 0.0f;
               }
             }
 #pragma unroll
             for (int j = 0; j < 32; j++) {
               const int64_t col = n0 + c + j;
-              if (col < args.n) {
+              if (col < args.n && wg_in_triangle(args.uplo, row, col)) {
                 const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc[j]);
                 args.C[row + col * args.ldc] = (beta != 0.0f) ? __fmaf_rn(beta, old[j], s) : s;
               }
@@ -639,7 +647,7 @@ wg_status launch_pack(wg_device *d, cudaStream_t s, const PackArgs &pa, const Pa
 wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
                      const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
                      float *ahi, float *alo, float *bhi, float *blo, char *sk, size_t partial_room,
-                     int64_t counter_room, unsigned *next_unit, const wg_gate &gate) {
+                     int64_t counter_room, unsigned *next_unit, const wg_gate &gate, int uplo) {
   const Layout L = layout_of(m, n, k);
   const int G = d->sm_count;
   Plan plan = plan_of(G, L, true);
@@ -653,7 +661,7 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
     return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
   MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, gate, L.tiles_m, L.tiles_n, L.kt, plan.dp_tiles,
                plan.sk_tiles, plan.sk_split, partials, counters, next_unit,
-               plan.dp_tiles + plan.sk_tiles * plan.sk_split};
+               plan.dp_tiles + plan.sk_tiles * plan.sk_split, uplo};
   auto kern = tf32x3_mma<Sh>;
   WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
   {
@@ -665,7 +673,7 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
     // Device-side fallback: exits at once unless the split flagged these operands.
     wg_launch_scope scope(d, "sgemm_simt_fallback");
     WG_CUDA(wg_launch_gemm_simt<float>(d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
-                                       d->dwords, &gate));
+                                       d->dwords, &gate, uplo));
   }
   return WG_OK;
 }
@@ -759,7 +767,7 @@ uint32_t wg_next_epoch(wg_device *d) {
 
 wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
                           const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C,
-                          int64_t ldc, void *ws, size_t ws_bytes) {
+                          int64_t ldc, void *ws, size_t ws_bytes, int uplo) {
   const Layout L = layout_of(m, n, k);
   float *ahi = static_cast<float *>(ws);
   float *alo = ahi + L.a_bytes / sizeof(float);
@@ -780,7 +788,7 @@ wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64
   if (st != WG_OK) return st;
   const wg_gate gate{flag, flag, epoch, epoch};
   return launch_mma(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ahi, alo, bhi, blo, sk,
-                    partial_room, plan.sk_tiles, next_unit, gate);
+                    partial_room, plan.sk_tiles, next_unit, gate, uplo);
 }
 
 // ---- panelled products ----------------------------------------------------
@@ -858,7 +866,7 @@ wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, in
   char *sk = p->ws + p->a_region + 2 * p->slot_bytes;
   const wg_gate gate{d->dwords + WG_DW_FALLBACK_A, flag_b, p->epoch_a, epoch_b};
   st = launch_mma(d, p->transA, p->transB, p->m, cols, p->k, p->alpha, p->A, p->lda, B, ldb, p->beta, C, ldc, ahi,
-                  alo, bhi, blo, sk, p->partial_room, p->counter_room, next_unit, gate);
+                  alo, bhi, blo, sk, p->partial_room, p->counter_room, next_unit, gate, WG_UPLO_FULL);
   if (st != WG_OK) return st;
   WG_CUDA(cudaEventRecord(d->tc_ev[EV_SLOT0 + slot], d->stream));
   d->stats.tf32x3_launches++;

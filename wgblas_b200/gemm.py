@@ -33,6 +33,7 @@ from ._runtime import Error, require_gpu_device, require_same_device
 from .classes import GpuMatrix, _is_int, is_f32_array, is_f64_array
 
 _TRANS = ("no-transpose", "transpose")
+_UPLO = ("lower", "upper")
 _LAYOUTS = ("row-major", "column-major")
 
 
@@ -40,12 +41,13 @@ def _is_number(x) -> bool:
     return isinstance(x, (int, float, np.integer, np.floating)) and not isinstance(x, (bool, np.bool_))
 
 
-def _validate(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, layout):
-    """The checks of src/sgemm/sgemm.mjs:42-149 (dgemm.mjs:40-149), in order.
+def _validate(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, layout, uplo=None):
+    """The checks of src/sgemm/sgemm.mjs:42-149 (dgemm.mjs:40-149), in order; with
+    ``uplo`` those of src/sgemmtr/sgemmtr.mjs:42-160 (the uplo check first).
 
     Returns None to proceed or the quick-return value for m == 0 or n == 0.
     """
-    f64 = routine == "dgemm"
+    f64 = routine.startswith("d")
     is_arr = is_f64_array if f64 else is_f32_array
     arr_name = "Float64Array" if f64 else "Float32Array"
     a_gpu = isinstance(A, GpuMatrix)
@@ -54,6 +56,8 @@ def _validate(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, b
 
     require_gpu_device(device)
     require_same_device(device, routine, {"A": A, "B": B, "C": C})
+    if routine.endswith("gemmtr") and uplo not in _UPLO:
+        raise Error("uplo must be 'lower' or 'upper'.")
     if transA not in _TRANS:
         raise Error("transA must be 'no-transpose' or 'transpose'.")
     if transB not in _TRANS:
@@ -156,12 +160,19 @@ def to_column_major_frame(transA, transB, m, n, A, lda, B, ldb, la, lb, lc):
 
 
 def _gemm(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, layout,
-          out=None):
+          out=None, uplo=None):
     early = _validate(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
-                      layout)
+                      layout, uplo)
     if early is not None:
         return early
-    f64 = routine == "dgemm"
+    return _execute(routine.startswith("d"), device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C,
+                    ldc, layout, out, uplo)
+
+
+def _execute(f64, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, layout, out=None,
+             uplo=None):
+    """Runs a validated call: the quick return, the layout mapping onto the
+    column-major frame, and the C-ABI call (with ``uplo``, the gemmtr entry points)."""
     m, n, k, lda, ldb, ldc = (int(v) for v in (m, n, k, lda, ldb, ldc))
     if f64:
         alpha, beta = float(alpha), float(beta)
@@ -177,11 +188,21 @@ def _gemm(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta,
     lc = C.layout if c_gpu else layout
     ta, tb, mm, nn, AA, lda2, BB, ldb2 = to_column_major_frame(transA, transB, m, n, A, lda, B, ldb,
                                                                la, lb, lc)
+    # The triangle is named in C's own (row, col) terms; a row-major C is computed
+    # as C^T in the column-major frame, where it is the other triangle (the twin of
+    # the column-major flip at src/sgemmtr/sgemmtr.mjs:178).
+    tri = ()
+    if uplo is not None:
+        lower = (uplo == "lower") == (lc == "column-major")
+        tri = (nat.WG_UPLO_LOWER if lower else nat.WG_UPLO_UPPER,)
     ms = ct.c_float(0.0)
     ms_p = ct.byref(ms) if device.benchmark else None
     if c_gpu:
-        fn = nat.lib.wg_dgemm if f64 else nat.lib.wg_sgemm
-        nat.check(fn(device.handle, ta, tb, mm, nn, k, alpha, AA._buf, 0, lda2, BB._buf, 0, ldb2,
+        if uplo is None:
+            fn = nat.lib.wg_dgemm if f64 else nat.lib.wg_sgemm
+        else:
+            fn = nat.lib.wg_dgemmtr if f64 else nat.lib.wg_sgemmtr
+        nat.check(fn(device.handle, *tri, ta, tb, mm, nn, k, alpha, AA._buf, 0, lda2, BB._buf, 0, ldb2,
                      beta, C._buf, 0, ldc, ms_p))
         if not device.benchmark:
             nat.check(nat.lib.wg_device_sync(device.handle))
@@ -194,9 +215,12 @@ def _gemm(routine, device, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta,
     elif not (isinstance(out, np.ndarray) and out.dtype == C.dtype and out.ndim == 1 and
               out.size >= C.size):
         raise Error("out must be a 1-D array of C's type and at least C's length.")
-    fn = nat.lib.wg_dgemm_host if f64 else nat.lib.wg_sgemm_host
+    if uplo is None:
+        fn = nat.lib.wg_dgemm_host if f64 else nat.lib.wg_sgemm_host
+    else:
+        fn = nat.lib.wg_dgemmtr_host if f64 else nat.lib.wg_sgemmtr_host
     ptr = ct.c_void_p
-    nat.check(fn(device.handle, ta, tb, mm, nn, k, alpha, ptr(AA.ctypes.data), lda2, ptr(BB.ctypes.data),
+    nat.check(fn(device.handle, *tri, ta, tb, mm, nn, k, alpha, ptr(AA.ctypes.data), lda2, ptr(BB.ctypes.data),
                  ldb2, beta, ptr(C.ctypes.data), ptr(out.ctypes.data), ldc, ms_p))
     device.check()
     res = {"C": out}
