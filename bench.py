@@ -59,11 +59,21 @@ WORKLOADS = {
                        lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
     "shard16384d": dict(routine="dgemm", config_index=4, transA=0, transB=0, m=16384, n=16384, k=16384,
                         lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
+    # The gemmtr family at the reference's own benchmark shape (benchmarks/sgemmtr/wgblas/sgemmtr.js,
+    # benchmarks/ssyrk/wgblas/ssyrk.js: m = n = k, lower, alpha 1, beta 0), counted as it counts them.
+    "sgemmtr4096": dict(routine="sgemm", config_index=None, transA=0, transB=0, m=4096, n=4096, k=4096,
+                        lda=4096, ldb=4096, ldc=4096, alpha=1.0, beta=0.0, data="uniform", uplo=1),
+    "ssyrk4096": dict(routine="sgemm", config_index=None, transA=0, transB=1, m=4096, n=4096, k=4096,
+                      lda=4096, ldb=4096, ldc=4096, alpha=1.0, beta=0.0, data="uniform", uplo=1, syrk=True),
+    "dsyrk4096": dict(routine="dgemm", config_index=None, transA=0, transB=1, m=4096, n=4096, k=4096,
+                      lda=4096, ldb=4096, ldc=4096, alpha=1.0, beta=0.0, data="uniform", uplo=1, syrk=True),
 }
 PANEL_COLS = 0  # B broadcast panels of the sharded workloads: 0 = the library's plan
 
 
 def flops(w):
+    if w.get("uplo"):  # the triangle only: k multiply-adds for each of n(n+1)/2 elements
+        return float(w["n"]) * (w["n"] + 1) * w["k"]
     return 2.0 * w["m"] * w["n"] * w["k"] + 2.0 * w["m"] * w["n"]
 
 
@@ -195,6 +205,13 @@ def barrier(world):
 def gemm_enqueue(wg, dev, w, GA, GB, GC):
     """One step on resident operands, queued on the device stream (no host sync)."""
     nat = wg._native
+    if w.get("uplo"):
+        # gemmtr; syrk is gemmtr with B := A and the other transpose, as ssyrk composes it
+        fn = nat.lib.wg_dgemmtr if w["routine"] == "dgemm" else nat.lib.wg_sgemmtr
+        B, ldb = (GA, w["lda"]) if w.get("syrk") else (GB, w["ldb"])
+        nat.check(fn(dev.handle, w["uplo"], w["transA"], w["transB"], w["m"], w["n"], w["k"], w["alpha"], GA._buf, 0,
+                     w["lda"], B._buf, 0, ldb, w["beta"], GC._buf, 0, w["ldc"], None))
+        return
     fn = nat.lib.wg_dgemm if w["routine"] == "dgemm" else nat.lib.wg_sgemm
     nat.check(fn(dev.handle, w["transA"], w["transB"], w["m"], w["n"], w["k"], w["alpha"], GA._buf, 0, w["lda"],
                  GB._buf, 0, w["ldb"], w["beta"], GC._buf, 0, w["ldc"], None))
@@ -422,7 +439,8 @@ def config_of(w, name, world=1):
     if w.get("sharded"):
         shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 in column panels "
                  f"{panel_plan(w, world)} (NCCL over NVLink)")
-    return {"workload": f"configs[{w['config_index']}] {w['routine']} {w['m']}x{w['n']}x{w['k']} "
+    label = f"configs[{w['config_index']}]" if w.get("config_index") is not None else name
+    return {"workload": f"{label} {w['routine']} {w['m']}x{w['n']}x{w['k']} "
                         f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major{shard}",
             "parallelism": f"row-sharded x{world}" if w.get("sharded") else "single GPU",
             "m": w["m"], "n": w["n"], "k": w["k"], "lda": w["lda"], "ldb": w["ldb"], "ldc": w["ldc"],
@@ -503,7 +521,7 @@ def main():
                            "fp64_dmma_tflops": fp64_dmma, "hbm_copy_gbs": hbm,
                            "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
         extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
-        for name in ("dgemm4096", "sgemm512", "ragged") if world == 1 else ():
+        for name in ("dgemm4096", "sgemm512", "ragged", "sgemmtr4096", "ssyrk4096", "dsyrk4096") if world == 1 else ():
             if name == pick_workload(args, world):
                 continue
             wx = WORKLOADS[name]

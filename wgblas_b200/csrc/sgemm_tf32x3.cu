@@ -591,9 +591,13 @@ struct Plan {
 // MMA time (about 0.5 us on B200), the last wave costs ceil(s*rem/G) rounds of
 // kt/s k-blocks, plus the split's overhead: partial-tile writes, the finishing
 // segment's reads of the other s-1 partial tiles at the end of the wave, and the
-// round imbalance. Measured on B200 over s = 2..16 and kt = 64..1024, that
-// overhead is about 28(s-1) + 8 k-blocks. s (at most kt/4 and MAX_SEG) minimises
-// the total, and s = 1 keeps the tiles whole.
+// round imbalance, about (s-1)*c + 8. Measured on B200, c is about 28 for deep
+// tiles (kt = 1024: 128 tiles over 148 SMs ran fastest whole) and about 4 for
+// shallow ones (kt <= 64: 512^3 and 1024^3 ran fastest in 4 segments), so c
+// steps from 4 to 28 at kt = 512. s (at most kt/4 and MAX_SEG) minimises the
+// total, and s = 1 keeps the tiles whole.
+double split_overhead(int kt, int s) { return (kt >= 512 ? 28.0 : 4.0) * (s - 1) + 8.0; }
+
 Plan plan_of(int G, const Layout &L, bool allow_split) {
   const int T = L.tiles_m * L.tiles_n;
   Plan p;
@@ -607,7 +611,7 @@ Plan plan_of(int G, const Layout &L, bool allow_split) {
   int best_s = 1;
   double best = (double)L.kt;
   for (int s = 2; s <= smax; s++) {
-    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s) + 28.0 * (s - 1) + 8.0;
+    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s) + split_overhead(L.kt, s);
     if (cost < best - 1e-9) {
       best = cost;
       best_s = s;
@@ -730,7 +734,7 @@ double wg_tf32x3_cost(int G, int64_t m, int64_t n, int64_t k) {
   if (p.sk_tiles == 0) return (double)((p.dp_tiles + G - 1) / G) * L.kt;  // whole tiles only
   const int s = p.sk_split;
   const int64_t rounds = ((int64_t)s * p.sk_tiles + G - 1) / G;
-  return (double)(p.dp_tiles / G) * L.kt + (double)rounds * ((double)L.kt / s) + 28.0 * (s - 1) + 8.0;
+  return (double)(p.dp_tiles / G) * L.kt + (double)rounds * ((double)L.kt / s) + split_overhead(L.kt, s);
 }
 
 bool wg_tf32x3_supported(const wg_device *d, int64_t m, int64_t n, int64_t k) {
