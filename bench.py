@@ -438,7 +438,7 @@ def config_of(w, name, world=1):
     shard = ""
     if w.get("sharded"):
         shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 in column panels "
-                 f"{panel_plan(w, world)} (NCCL over NVLink)")
+                 f"{panel_plan(w, world)} (copy-engine chain over NVLink)")
     label = f"configs[{w['config_index']}]" if w.get("config_index") is not None else name
     return {"workload": f"{label} {w['routine']} {w['m']}x{w['n']}x{w['k']} "
                         f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major{shard}",

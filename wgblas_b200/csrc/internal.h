@@ -215,7 +215,7 @@ cudaError_t wg_launch_scale(cudaStream_t s, int64_t m, int64_t n, T alpha, T bet
                             int64_t ldc, int uplo = 0);
 
 // Bytes of scratch the 3xTF32 path needs for this shape: the split operands
-// alone (whole-tile scheduling), or with the stream-K partial sums and counters.
+// alone (whole-tile scheduling), or with the split-K partial sums and counters.
 size_t wg_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
 size_t wg_tf32x3_workspace_bytes_sk(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 // Modelled run time of the 3xTF32 kernel for one m x n x k product on G SMs, in
@@ -226,7 +226,7 @@ bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
 // Splits op(A), op(B) into tf32 hi/lo operands in `ws`, then runs the tcgen05 kernel.
 // Operands outside the split's exact range make the kernel exit and the FFMA
 // kernel (launched right after, gated on the same epoch) compute C instead.
-// `ws` holds ws_bytes: stream-K scheduling is used when it also fits the
+// `ws` holds ws_bytes: the last wave is split along k when it also fits the
 // partial sums (wg_tf32x3_workspace_bytes_sk), whole tiles otherwise.
 wg_status wg_sgemm_tf32x3(wg_device *dev, int transA, int transB, int64_t m, int64_t n,
                           int64_t k, float alpha, const float *A, int64_t lda, const float *B,

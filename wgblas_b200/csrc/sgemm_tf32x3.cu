@@ -9,12 +9,13 @@
 // The alpha/beta epilogue is the reference's (src/shaders/sgemm_large.wgsl:299-304)
 // in fp32 with the beta term fused.
 //
-// Two launches per call:
+// Two launches per call (plus the gated fallback):
 //  1. tf32x3_pack: reads op(A) and op(B) in any transpose / leading dimension,
 //     writes K-major, zero-padded hi and lo operands to the scratch workspace,
-//     and flags (dwords[WG_DW_FALLBACK] = epoch) any element that is not finite
-//     or whose magnitude lies outside [2^-50, 2^50] — there the split loses its
-//     accuracy (subnormal lo parts) or IEEE semantics (Inf*0 in a cross term).
+//     and flags (writes the call's epoch into a device word) any element that
+//     is not finite or whose magnitude lies outside [2^-50, 2^50] — there the
+//     split loses its accuracy (subnormal lo parts) or IEEE semantics (Inf*0 in
+//     a cross term).
 //  2. tf32x3_mma: a persistent grid, one CTA per SM, over 128 x BN tiles of C.
 //     Warp 0 streams the four operand tiles of each k-block into a
 //     STAGES-deep shared-memory ring with TMA (no multicast); warp 1 issues
@@ -25,17 +26,20 @@
 //     visited in groups of GROUP_M tile rows for L2 reuse.
 //     Work split: units are handed out in raster order from a work counter
 //     (each CTA's first is its blockIdx.x), so CTAs running together work on
-//     neighbouring tiles for L2 reuse and an SM slowed by other kernels (NCCL,
-//     operand splits of the next panel) simply takes fewer; the leftover
-//     tiles of a partial last wave are cut into s equal k-segments when that
-//     shortens the wave (plan_of), and the segments are dealt out so CTAs
-//     running together share a k range. A split tile is finished by whichever
-//     segment arrives last (a per-tile atomic counter): the others leave their
-//     fp32 partial sums in the workspace, and the last adds all segments in k
-//     order — no CTA ever waits for another, and the result does not depend
-//     on arrival order. Without room for the partial sums all tiles go whole.
-//     If the flag carries this call's epoch the kernel exits at once, and the
-//     FFMA kernel launched after it (gated on the same epoch) computes C.
+//     neighbouring tiles for L2 reuse and an SM slowed by other kernels
+//     (operand splits of the next panel, a broadcast) simply takes fewer; the
+//     leftover tiles of a partial last wave are cut into s equal k-segments
+//     when that shortens the wave (plan_of), numbered so units handed out
+//     together share a k range. A split tile is finished by whichever segment
+//     arrives last (a per-tile atomic counter): the others leave their fp32
+//     partial sums in the workspace, and the last adds all segments in k order
+//     — no CTA ever waits for another, and the result does not depend on
+//     arrival order. Without room for the partial sums all tiles go whole.
+//     gemmtr calls skip the units whose tile has no element in the triangle
+//     and mask the diagonal tiles' stores.
+//  When the pack flagged the operands (the gate: a flag word holding the
+//  call's epoch) the MMA kernel exits at once and the FFMA kernel launched
+//  after it, gated on the same words, computes C instead.
 #include <cuda.h>
 
 #include "internal.h"
