@@ -285,6 +285,25 @@ wg_status wg_dgemmtr_host(wg_device *dev, int uplo, int transA, int transB, int6
                           double alpha, const double *A, int64_t lda, const double *B, int64_t ldb, double beta,
                           const double *C_in, double *C_out, int64_t ldc, float *gpu_ms);
 
+/* ---- operand passes of ssymm/dsymm and strmm/dtrmm -------------------------
+ * The reference runs these routines as a pass that materializes a dense copy of
+ * the symmetric / triangular operand followed by a plain GEMM
+ * (src/ssymm/ssymm.mjs:26-28, src/strmm/strmm.mjs); the language layer does the
+ * same with these passes and the GEMM entry points. Column-major frame; n x n
+ * matrices of elem_bytes (4: f32, 8: f64) at element offsets and leading
+ * dimensions; `uplo` names the stored triangle (WG_UPLO_LOWER: i >= j). */
+/* out := the symmetric matrix whose `uplo` triangle A holds. */
+wg_status wg_symmetrize(wg_device *dev, int elem_bytes, int uplo, int64_t n, const wg_buffer *A, int64_t offA,
+                        int64_t lda, wg_buffer *out, int64_t offO, int64_t ldo);
+/* out := T or T^T (trans), where T is A's `uplo` triangle with zeros elsewhere and,
+ * when unit = 1, ones on the diagonal (A's diagonal not read). */
+wg_status wg_triangularize(wg_device *dev, int elem_bytes, int uplo, int trans, int unit, int64_t n,
+                           const wg_buffer *A, int64_t offA, int64_t lda, wg_buffer *out, int64_t offO, int64_t ldo);
+/* Copies `rows` rows of `width` bytes between device buffers (byte offsets and
+ * pitches), queued on the device stream. */
+wg_status wg_buffer_copy_2d(wg_device *dev, const wg_buffer *src, size_t src_off, size_t src_pitch, wg_buffer *dst,
+                            size_t dst_off, size_t dst_pitch, size_t width, size_t rows);
+
 /* ---- multi-GPU: C sharded by row blocks, B broadcast over NVLink (NCCL) ---- */
 /* The reference drives several GPUs only as independent devices with no data
  * exchange (src/init.mjs:14-29, examples/init-two-gpus/init-two-gpus.js); this

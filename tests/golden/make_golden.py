@@ -16,7 +16,12 @@ gemmtr_edge_cases.json
     in C's own terms) changes; syrk is gemmtr with B := A and the other
     transpose, syr2k two gemmtr passes, the second with beta = 1
     (src/ssyrk/ssyrk.mjs:29-31, src/ssyr2k/ssyr2k.mjs:25-26), each pass checked
-    to be exact in f32. The reference checks these bit for bit against stdlib
+    to be exact in f32.
+symm_trmm_edge_cases.json
+    The same for tests/{s,d}{symm,trmm}/edge-cases*.json: symm reads A's uplo
+    triangle as a symmetric matrix (C := alpha*A*B + beta*C, or alpha*B*A + beta*C
+    for side 'right'); trmm reads its uplo triangle, ones on the diagonal for
+    diag 'unit', and overwrites B with alpha*op(A)*B (or alpha*B*op(A)). The reference checks these bit for bit against stdlib
     (tests/sgemm/src/test.sgemm.js:126-164,354-394; tests/dgemm/src/test.dgemm.js).
     Their values are small integers, so the expected output is computed here
     with exact rational arithmetic and then checked to be representable in f32:
@@ -144,6 +149,67 @@ def gemmtr_edge_cases(ref):
     return cases
 
 
+def _elem(M, ld, layout, r, c):
+    return M[c * ld + r] if layout == "column-major" else M[r * ld + c]
+
+
+def exact_special(case):
+    """Expected result (C for symm, B for trmm) of a symm / trmm edge case."""
+    layout = case.get("layout", "row-major")
+    m, n, side, uplo = case["m"], case["n"], case["side"], case["uplo"]
+    order = m if side == "left" else n
+    lower = uplo == "lower"
+    trmm = case["routine"].endswith("trmm")
+
+    def a(i, j):  # the symmetric / triangular operand, op applied for trmm
+        if trmm and case["transA"] == "transpose":
+            i, j = j, i
+        if trmm:
+            if i == j:
+                return Fraction(1) if case["diag"] == "unit" else Fraction(_elem(case["A"], case["lda"], layout, i, i))
+            inside = i > j if lower else i < j
+            return Fraction(_elem(case["A"], case["lda"], layout, i, j)) if inside else Fraction(0)
+        stored = i >= j if lower else i <= j
+        return Fraction(_elem(case["A"], case["lda"], layout, i, j) if stored else
+                        _elem(case["A"], case["lda"], layout, j, i))
+
+    def b(i, j):
+        return Fraction(_elem(case["B"], case["ldb"], layout, i, j))
+
+    alpha = Fraction(case["alpha"])
+    out = list(case["B"] if trmm else case["C"])
+    ld = case["ldb"] if trmm else case["ldc"]
+    for i in range(m):
+        for j in range(n):
+            acc = sum((a(i, p) * b(p, j) for p in range(order)), Fraction(0)) if side == "left" else \
+                sum((b(i, p) * a(p, j) for p in range(order)), Fraction(0))
+            val = alpha * acc
+            if not trmm and case["beta"] != 0:
+                val += Fraction(case["beta"]) * Fraction(_elem(case["C"], ld, layout, i, j))
+            fv = float(val)
+            if Fraction(fv) != val or f32(fv) != fv:
+                raise ValueError(f"{case['label']}: result {val} is not exact in f32")
+            out[(j * ld + i) if layout == "column-major" else (i * ld + j)] = fv
+    return out
+
+
+def symm_trmm_edge_cases(ref):
+    cases = []
+    keys = {"symm": ("label", "side", "uplo", "m", "n", "alpha", "A", "lda", "B", "ldb", "beta", "C", "ldc"),
+            "trmm": ("label", "side", "uplo", "transA", "diag", "m", "n", "alpha", "A", "lda", "B", "ldb")}
+    for routine in ("ssymm", "dsymm", "strmm", "dtrmm"):
+        for fname in ("edge-cases.json", "edge-cases-column-major.json"):
+            with open(os.path.join(ref, "tests", routine, fname)) as fh:
+                for tc in json.load(fh):
+                    case = {k: tc[k] for k in keys[routine[1:]]}
+                    case["layout"] = tc.get("layout", "row-major")
+                    case["routine"] = routine
+                    case["source"] = f"tests/{routine}/{fname}"
+                    case["expected"] = exact_special(case)
+                    cases.append(case)
+    return cases
+
+
 # ---- double-double lane cases (tests/shaders/src/test.dekker.js:98-138) ----
 
 def dd_lanes():
@@ -222,7 +288,7 @@ def _dump(obj, name):
 
 
 def validation_params(ref):
-    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld", "uplo"]
+    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld", "uplo", "side", "diag"]
     out = {}
     for name in names:
         with open(os.path.join(ref, "tests", "validation", "params", f"{name}.json")) as fh:
@@ -234,6 +300,7 @@ def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.path.join(HERE, "..", "..", "..", "reference")
     _dump(edge_cases(ref), "gemm_edge_cases.json")
     _dump(gemmtr_edge_cases(ref), "gemmtr_edge_cases.json")
+    _dump(symm_trmm_edge_cases(ref), "symm_trmm_edge_cases.json")
     _dump(dd_lanes(), "dd_lanes.json")
     _dump(validation_params(ref), "validation_params.json")
     seeds = [0, 1, 2, 3, 42, 100, 111, 112, 113, 200, 300]

@@ -23,7 +23,8 @@ def fake_device(wg):
     return Fake(object(), 0, False, {}, "fake")
 
 
-@pytest.mark.parametrize("routine", ["sgemm", "dgemm", "sgemmtr", "dgemmtr", "ssyrk", "dsyrk", "ssyr2k", "dsyr2k"])
+@pytest.mark.parametrize("routine", ["sgemm", "dgemm", "sgemmtr", "dgemmtr", "ssyrk", "dsyrk", "ssyr2k", "dsyr2k",
+                                     "ssymm", "dsymm", "strmm", "dtrmm"])
 def test_invalid_arguments_raise_reference_messages(wg, fake_device, routine):
     fn = getattr(wg, routine)
     n = 0

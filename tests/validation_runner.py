@@ -55,7 +55,20 @@ def build_specs(routine: str) -> dict:
     a_base = copy.deepcopy(P["A"])
     lvl3 = a_base.pop("level-3")
     a_spec = {**a_base, **lvl3}
-    if rank:
+    if routine[1:] in ("symm", "trmm"):
+        # tests/ssymm/src/test.ssymm.js and tests/strmm/src/test.strmm.js
+        n_spec["invalid"][-1]["error"] = "must be non-negative"
+        specs = {"device": P["device"], "side": P["side"], "uplo": P["uplo"]}
+        if routine[1:] == "trmm":
+            specs.update(transA=P["trans"], diag=P["diag"])
+        specs.update(layout=P["layout"], m=m_spec, n=n_spec, alpha=P["alpha"])
+        if routine[1:] == "symm":
+            specs["beta"] = P["beta"]
+        specs.update(A={**a_base, "dependsOn": ["m", "n", "lda", "side"]}, lda=P["ld"],
+                     B={**copy.deepcopy(P["B"]), "dependsOn": ["m", "n", "ldb"]}, ldb=P["ld"])
+        if routine[1:] == "symm":
+            specs.update(C=copy.deepcopy(P["C"]), ldc=P["ld"])
+    elif rank:
         specs = {"device": P["device"], "uplo": P["uplo"], "trans": P["trans"], "layout": P["layout"],
                  "n": n_spec, "k": P["k"], "alpha": P["alpha"], "beta": P["beta"],
                  "A": {**a_spec, "dependsOn": ["n", "k", "lda", "trans"]}, "lda": P["ld"]}
@@ -74,6 +87,7 @@ def build_specs(routine: str) -> dict:
             specs = {"device": specs.pop("device"), "uplo": P["uplo"], **specs}
     if routine.startswith("d"):
         a64 = copy.deepcopy(specs["A"])
+        a64.pop("level-3", None)
         a64["type"] = "float64array"
         for e in a64["invalid"]:
             e["error"] = e["error"].replace("Float32Array", "Float64Array")
@@ -83,7 +97,8 @@ def build_specs(routine: str) -> dict:
         specs["A"] = a64
         if "B" in specs:
             specs["B"] = {**_derive64(P["B"]), "dependsOn": specs["B"]["dependsOn"]}
-        specs["C"] = {**_derive64(P["C"]), "dependsOn": specs["C"]["dependsOn"]}
+        if "C" in specs:
+            specs["C"] = {**_derive64(P["C"]), "dependsOn": specs["C"]["dependsOn"]}
     return specs
 
 
@@ -96,6 +111,9 @@ def _matrix_len(depends_on, dims):
     ld_key = next(d for d in depends_on if d.startswith("ld"))
     trans_key = next((d for d in depends_on if d.startswith("trans")), None)
     cm = dims.get("layout") == "column-major"
+    if "side" in depends_on:  # the square operand of symm / trmm: order m (left) or n (right)
+        order = dims["m"] if dims.get("side", "left") == "left" else dims["n"]
+        return max(0, (order - 1) * dims[ld_key] + order)
     if trans_key and "k" in depends_on:
         d1, d2 = [d for d in depends_on if d in ("m", "n", "k")]
         rows, cols = (dims[d2], dims[d1]) if cm else (dims[d1], dims[d2])
@@ -156,6 +174,12 @@ def cases(routine, device, kind, make_wrong_dtype_matrix=None):
 
 
 def call(fn, a):
+    if "side" in a:  # symm / trmm
+        if "diag" in a:
+            return fn(a["device"], a["side"], a["uplo"], a["transA"], a["diag"], a["m"], a["n"], a["alpha"], a["A"],
+                      a["lda"], a["B"], a["ldb"], a["layout"])
+        return fn(a["device"], a["side"], a["uplo"], a["m"], a["n"], a["alpha"], a["A"], a["lda"], a["B"], a["ldb"],
+                  a["beta"], a["C"], a["ldc"], a["layout"])
     if "trans" in a:  # syrk / syr2k
         if "B" in a:
             return fn(a["device"], a["uplo"], a["trans"], a["n"], a["k"], a["alpha"], a["A"], a["lda"], a["B"],

@@ -85,6 +85,11 @@ _sig("wg_sgemm_tc_plan", _st, ct.c_int, ct.c_int64, ct.c_int64, ct.c_int64, ct.P
 _sig("wg_sharded_panel_plan", _st, ct.c_int, ct.c_int, ct.c_int64, ct.c_int64, ct.c_int64,
      ct.POINTER(ct.c_int64), ct.c_size_t, ct.POINTER(ct.c_size_t))
 _sig("wg_selftest_bounded_wait", _st, c_dev_p, ct.c_uint)
+_sig("wg_symmetrize", _st, c_dev_p, ct.c_int, ct.c_int, _i64, c_buf_p, _i64, _i64, c_buf_p, _i64, _i64)
+_sig("wg_triangularize", _st, c_dev_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _i64, c_buf_p, _i64, _i64, c_buf_p,
+     _i64, _i64)
+_sig("wg_buffer_copy_2d", _st, c_dev_p, c_buf_p, ct.c_size_t, ct.c_size_t, c_buf_p, ct.c_size_t, ct.c_size_t,
+     ct.c_size_t, ct.c_size_t)
 WG_PROBE_FP32_FMA, WG_PROBE_FP64_FMA, WG_PROBE_HBM_COPY, WG_PROBE_FP64_DMMA = 0, 1, 2, 3
 _sig("wg_device_set_profiling", _st, c_dev_p, ct.c_int)
 _sig("wg_device_profile_read", _st, c_dev_p, ct.POINTER(KernelProfile), ct.c_int, ct.POINTER(ct.c_int))
