@@ -260,6 +260,48 @@ def time_resident(wg, dev, w, steps, warmup, world, flush):
     return ms, prof, launches, wall
 
 
+def time_special(wg, dev, name, steps, warmup, flush):
+    """ssymm / strmm at 4096 (the reference's benchmark defaults: side left, uplo
+    lower, trmm non-unit no-transpose; benchmarks/ssymm/wgblas/ssymm.js,
+    benchmarks/strmm/wgblas/strmm.js) through the public API on resident
+    GpuMatrix operands, with the reference's FLOP counts."""
+    import torch
+
+    n = 4096
+    A = wg.randomFloat32Array(n * n, -1, 1, 1)
+    B = wg.randomFloat32Array(n * n, -1, 1, 2)
+    GA = wg.GpuMatrix.from_(dev, A, n, n, n, "column-major")
+    GB = wg.GpuMatrix.from_(dev, B, n, n, n, "column-major")
+    GC = wg.GpuMatrix.from_(dev, wg.randomFloat32Array(n * n, -1, 1, 3), n, n, n, "column-major")
+    if name == "ssymm4096":
+        fn = lambda: wg.ssymm(dev, "left", "lower", n, n, 1.0, GA, n, GB, n, 0.0, GC, n, "column-major")  # noqa: E731
+        work = 2.0 * n * n * n + 2.0 * n * n
+    else:
+        fn = lambda: wg.strmm(dev, "left", "lower", "no-transpose", "non-unit", n, n, 1.0, GA, n, GB, n, "column-major")  # noqa: E731
+        work = 2.0 * n * n * n + 1.0 * n * n
+    stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                flush.add_(1.0)
+                fn()
+            dev.synchronize()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            for i in range(steps):
+                flush.add_(1.0)
+                starts[i].record(stream)
+                fn()
+                ends[i].record(stream)
+            dev.synchronize()
+            ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    finally:
+        for g in (GA, GB, GC):
+            g.destroy()
+    return {"tflops": work / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+            "note": "public API call incl. its scratch allocation and the dense operand pass"}
+
+
 def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
     """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs)."""
     import torch
@@ -532,6 +574,12 @@ def main():
                            f"pct_of_{'fp64' if wx['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf / pk,
                            "kernels": {k: v[1] / max(v[0], 1) for k, v in profx.items()}}
 
+    if not args.no_extra and world == 1 and not w.get("sharded"):
+        for name in ("ssymm4096", "strmm4096"):
+            try:
+                extra[name] = time_special(wg, dev, name, max(3, args.steps // 2), 3, flush)
+            except wg.Error as e:  # a secondary line: report it, keep the headline
+                extra[name] = {"error": str(e)}
     if not args.no_extra and world == 1 and not w.get("sharded"):
         # configs[4] on one GPU through the same sharded path (one rank): the N=1
         # reference point for the multi-GPU scaling of the sharded workload.
