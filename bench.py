@@ -302,6 +302,66 @@ def time_special(wg, dev, name, steps, warmup, flush):
             "note": "public API call incl. its scratch allocation and the dense operand pass"}
 
 
+def time_trsm(wg, dev, nrhs, steps, warmup, flush):
+    """strsm at order 4096, side left, lower, no-transpose, non-unit, column-major,
+    through the public API on resident GpuMatrix operands. nrhs = 64 is the
+    reference's base sweep (benchmarks/strsm/wgblas/strsm.js, order 4096 with a
+    64-column right-hand side); nrhs = 4096 a square solve. B is refreshed from
+    a pristine copy before every call, outside the timed events, as the
+    reference's benchmark refreshes it (the solve is in place). A: off-diagonals
+    in [-1/order, 1/order), diagonal in [5, 15) (diagonally dominant, so repeated
+    solves stay finite). FLOPs: m*n*order (the reference's count)."""
+    import ctypes as ct
+
+    import torch
+
+    from wgblas_b200 import _native as nat
+
+    order = 4096
+    rng = np.random.default_rng(4)
+    A = ((rng.random(order * order) * 2 - 1) / order).astype(np.float32)
+    A[np.arange(order) * (order + 1)] = (5 + 10 * rng.random(order)).astype(np.float32)
+    B = wg.randomFloat32Array(order * nrhs, -1, 1, 2)
+    GA = wg.GpuMatrix.from_(dev, A, order, order, order, "column-major")
+    GB = wg.GpuMatrix.from_(dev, B, order, nrhs, order, "column-major")
+    G0 = wg.GpuMatrix.from_(dev, B, order, nrhs, order, "column-major")
+    pitch = order * 4
+
+    def refresh():
+        nat.check(nat.lib.wg_buffer_copy_2d(dev.handle, G0._buf, 0, pitch, GB._buf, 0, pitch, pitch, nrhs))
+
+    def solve():
+        wg.strsm(dev, "left", "lower", "no-transpose", "non-unit", order, nrhs, 1.0, GA, order, GB, order,
+                 "column-major")
+
+    stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                flush.add_(1.0)
+                refresh()
+                solve()
+            dev.synchronize()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            for i in range(steps):
+                flush.add_(1.0)
+                refresh()
+                starts[i].record(stream)
+                solve()
+                ends[i].record(stream)
+            dev.synchronize()
+            ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+            x = GB.read()
+    finally:
+        for g in (GA, GB, G0):
+            g.destroy()
+    work = float(order) * nrhs * order
+    return {"tflops": work / (ms * 1e-3) / 1e12, "ms_per_step": ms, "ms_per_block": ms / (order // 64),
+            "finite": bool(np.all(np.isfinite(x))), "nrhs": nrhs,
+            "note": "order 4096 left lower column-major; public API on GpuMatrix, B refreshed untimed"}
+
+
 def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
     """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs)."""
     import torch
@@ -580,6 +640,11 @@ def main():
                 extra[name] = time_special(wg, dev, name, max(3, args.steps // 2), 3, flush)
             except wg.Error as e:  # a secondary line: report it, keep the headline
                 extra[name] = {"error": str(e)}
+        for nrhs in (64, 4096):
+            try:
+                extra[f"strsm4096_n{nrhs}"] = time_trsm(wg, dev, nrhs, max(3, args.steps // 2), 3, flush)
+            except wg.Error as e:
+                extra[f"strsm4096_n{nrhs}"] = {"error": str(e)}
     if not args.no_extra and world == 1 and not w.get("sharded"):
         # configs[4] on one GPU through the same sharded path (one rank): the N=1
         # reference point for the multi-GPU scaling of the sharded workload.

@@ -304,6 +304,26 @@ wg_status wg_triangularize(wg_device *dev, int elem_bytes, int uplo, int trans, 
 wg_status wg_buffer_copy_2d(wg_device *dev, const wg_buffer *src, size_t src_off, size_t src_pitch, wg_buffer *dst,
                             size_t dst_off, size_t dst_pitch, size_t width, size_t rows);
 
+/* ---- strsm (src/strsm/strsm.mjs:160-583) -----------------------------------
+ * B := alpha * op(A)^-1 * B (side WG_SIDE_LEFT) or alpha * B * op(A)^-1
+ * (WG_SIDE_RIGHT) in place, in the column-major frame: B is m x n with ldb >= m,
+ * A is the order x order triangle (order = m for left, n for right) whose `uplo`
+ * triangle (WG_UPLO_LOWER / WG_UPLO_UPPER) is read; the other triangle is never
+ * read, nor the diagonal when diag is WG_DIAG_UNIT. transA: 0 = op(A) = A,
+ * 1 = A^T. alpha = 0 writes zeros to B without reading A or B. m or n = 0
+ * returns at once. Queued on the device stream; gpu_ms as for wg_sgemm. A
+ * singular A gives Infinity / NaN as substitution does, no error. */
+#define WG_SIDE_LEFT 0
+#define WG_SIDE_RIGHT 1
+#define WG_DIAG_NON_UNIT 0
+#define WG_DIAG_UNIT 1
+wg_status wg_strsm(wg_device *dev, int side, int uplo, int transA, int diag, int64_t m, int64_t n, float alpha,
+                   const wg_buffer *A, int64_t offA, int64_t lda, wg_buffer *B, int64_t offB, int64_t ldb,
+                   float *gpu_ms);
+/* The same on raw device pointers of the device (no size checks). */
+wg_status wg_strsm_dev(wg_device *dev, int side, int uplo, int transA, int diag, int64_t m, int64_t n, float alpha,
+                       const float *A, int64_t lda, float *B, int64_t ldb);
+
 /* ---- multi-GPU: C sharded by row blocks, B broadcast over NVLink (NCCL) ---- */
 /* The reference drives several GPUs only as independent devices with no data
  * exchange (src/init.mjs:14-29, examples/init-two-gpus/init-two-gpus.js); this

@@ -280,3 +280,108 @@ def forward_factor(got, truth, m, n, k, alpha, absab, beta, C, ldc, eps, kplus, 
     if np.all(zero):
         return 0.0
     return float(np.max(err[~zero] / bound[~zero]))
+
+
+# ---- strsm: the reference's own test oracle, restated -----------------------------
+
+def _index_grid(rows, cols, ld, layout):
+    """Flat indices of a rows x cols matrix stored with leading dimension ld, shape (rows, cols)."""
+    i = np.arange(rows)[:, None]
+    j = np.arange(cols)[None, :]
+    return (j * ld + i) if layout == "column-major" else (i * ld + j)
+
+
+def tri_dense(A, lda, order, uplo, transA, diag, layout="row-major"):
+    """op(A) as a dense float64 (order, order) matrix: denseTriangular of
+    tests/helpers/stdlib.js:607-641. The stored `uplo` triangle (read with op
+    applied), zeros outside it, ones on the diagonal for diag 'unit' (A's
+    diagonal then unread); elements outside the triangle are never read."""
+    A = np.asarray(A)
+    out = np.zeros((order, order))
+    if order == 0:
+        return out
+    i, j = np.meshgrid(np.arange(order), np.arange(order), indexing="ij")
+    nt = transA == "no-transpose"
+    lower = uplo == "lower"
+    meaningful = ((j <= i) if lower else (j >= i)) if nt else ((j >= i) if lower else (j <= i))
+    r, c = (i, j) if nt else (j, i)
+    idx = (c * lda + r) if layout == "column-major" else (r * lda + c)
+    off = meaningful & (i != j)
+    out[off] = A[idx[off]].astype(np.float64)
+    d = np.arange(order)
+    if diag == "unit":
+        out[d, d] = 1.0
+    else:
+        out[d, d] = A[idx[d, d]].astype(np.float64)
+    return out
+
+
+def strsm(side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout="row-major"):
+    """strsmReference / solveTriangular of tests/helpers/stdlib.js:692-775: B's
+    m x n block replaced by X with op(A)*X = alpha*B (side 'left') or
+    X*op(A) = alpha*B ('right'), by row (left) or column (right) substitution.
+    Each unknown is alpha*b minus the products with the unknowns already found,
+    subtracted one at a time in f64 (the reference's JavaScript numbers), divided
+    by the diagonal in f64 and stored rounded to f32; alpha = 0 gives zeros
+    (the whole array, as the reference returns a fresh zero array). Returns a
+    new float32 array the size of B; the padding keeps B's values."""
+    B = np.asarray(B, np.float32)
+    if alpha == 0:
+        return np.zeros(B.size, np.float32)
+    if m == 0 or n == 0:
+        return B.copy()
+    order = m if side == "left" else n
+    D = tri_dense(A, lda, order, uplo, transA, diag, layout)
+    op_lower = (transA == "no-transpose") == (uplo == "lower")
+    idx = _index_grid(m, n, ldb, layout)
+    Bm = B[idx].astype(np.float64)
+    out = Bm.copy()
+    with np.errstate(all="ignore"):
+        for step in range(order):
+            if side == "left":
+                i = step if op_lower else order - 1 - step
+                ks = np.arange(0, i) if op_lower else np.arange(i + 1, order)
+                terms = np.empty((len(ks) + 1, n))
+                terms[0] = alpha * Bm[i]
+                terms[1:] = -(D[i, ks][:, None] * out[ks, :])
+                acc = np.cumsum(terms, axis=0)[-1]  # strictly sequential, like the loop
+                out[i] = (acc / D[i, i]).astype(np.float32)
+            else:
+                j = order - 1 - step if op_lower else step
+                ks = np.arange(j + 1, order) if op_lower else np.arange(0, j)
+                terms = np.empty((len(ks) + 1, m))
+                terms[0] = alpha * Bm[:, j]
+                terms[1:] = -(out[:, ks].T * D[ks, j][:, None])
+                acc = np.cumsum(terms, axis=0)[-1]
+                out[:, j] = (acc / D[j, j]).astype(np.float32)
+    res = B.copy()
+    res[idx] = out.astype(np.float32)
+    return res
+
+
+def strsm_residual_factor(X, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout="row-major"):
+    """backwardResidualFactor of tests/strsm/helpers.js: max over the m x n block of
+    |op(A)*X - alpha*B| / (2^-23 * (order + 1) * |op(A)||X|) (X*op(A) for side
+    'right'), with alpha*B taken as 0 when alpha = 0; where the bound is 0 the
+    residual must be exactly 0, else the factor is infinite. The reference's
+    strsm tests require a factor <= 5."""
+    if m == 0 or n == 0:
+        return 0.0
+    order = m if side == "left" else n
+    D = tri_dense(A, lda, order, uplo, transA, diag, layout)
+    idx = _index_grid(m, n, ldb, layout)
+    Xm = np.asarray(X)[idx].astype(np.float64)
+    Bm = np.asarray(B)[idx].astype(np.float64)
+    if side == "left":
+        acc, dot = D @ Xm, np.abs(D) @ np.abs(Xm)
+    else:
+        acc, dot = Xm @ D, np.abs(Xm) @ np.abs(D)
+    rhs = np.zeros_like(Bm) if alpha == 0 else alpha * Bm
+    err = np.abs(acc - rhs)
+    bound = 2.0**-23 * (order + 1) * dot
+    zero = bound == 0
+    if np.any(err[zero] != 0):
+        return float("inf")
+    if np.all(zero):
+        return 0.0
+    return float(np.max(err[~zero] / bound[~zero]))

@@ -26,6 +26,13 @@ symm_trmm_edge_cases.json
     Their values are small integers, so the expected output is computed here
     with exact rational arithmetic and then checked to be representable in f32:
     any correct GEMM must reproduce it exactly.
+strsm_edge_cases.json
+    The cases of tests/strsm/edge-cases*.json (inputs copied as data), each with
+    X = op(A)^-1 * alpha*B solved in exact rational arithmetic and rounded to
+    f32 ("expected"), and whether that solution is exact in f32 ("exact"). The
+    reference checks strsm by its backward residual
+    (tests/strsm/helpers.js, factor <= 5 in tests/strsm/src/test.strsm.js), not
+    bit for bit; the exact solution pins the restated stdlib oracle.
 dd_lanes.json
     The lane cases of tests/shaders/src/test.dekker.js:98-138 (inputs and the
     expected result of twoSum, twoProdBit, ddAdd and ddMul per lane), restated
@@ -210,6 +217,65 @@ def symm_trmm_edge_cases(ref):
     return cases
 
 
+def exact_trsm(case):
+    """X with op(A) X = alpha B (left) or X op(A) = alpha B (right), exact rationals,
+    over a copy of B (padding kept); returns (values rounded to f32, all exact)."""
+    layout = case.get("layout", "row-major")
+    m, n, side = case["m"], case["n"], case["side"]
+    order = m if side == "left" else n
+    nt = case["transA"] == "no-transpose"
+    lower = case["uplo"] == "lower"
+
+    def op(i, j):  # op(A)(i, j), zero outside the stored triangle
+        r, c = (i, j) if nt else (j, i)
+        if r == c:
+            return Fraction(1) if case["diag"] == "unit" else Fraction(_elem(case["A"], case["lda"], layout, r, r))
+        inside = r > c if lower else r < c
+        return Fraction(_elem(case["A"], case["lda"], layout, r, c)) if inside else Fraction(0)
+
+    alpha = Fraction(case["alpha"])
+    rhs = [[alpha * Fraction(_elem(case["B"], case["ldb"], layout, i, j)) for j in range(n)] for i in range(m)]
+    X = [[None] * n for _ in range(m)]
+    op_lower = nt == lower
+    if side == "left":  # rows of X, in dependency order
+        rows = range(order) if op_lower else range(order - 1, -1, -1)
+        for i in rows:
+            for j in range(n):
+                acc = rhs[i][j] - sum((op(i, k) * X[k][j] for k in range(order) if k != i and X[k][j] is not None),
+                                      Fraction(0))
+                X[i][j] = acc / op(i, i)
+    else:  # columns of X
+        cols = range(order - 1, -1, -1) if op_lower else range(order)
+        for j in cols:
+            for i in range(m):
+                acc = rhs[i][j] - sum((X[i][k] * op(k, j) for k in range(order) if k != j and X[i][k] is not None),
+                                      Fraction(0))
+                X[i][j] = acc / op(j, j)
+    out = list(case["B"])
+    exact = True
+    for i in range(m):
+        for j in range(n):
+            fv = f32(float(X[i][j]))
+            exact = exact and Fraction(fv) == X[i][j]
+            out[(j * case["ldb"] + i) if layout == "column-major" else (i * case["ldb"] + j)] = fv
+    return out, exact
+
+
+def strsm_edge_cases(ref):
+    keys = ("label", "side", "uplo", "transA", "diag", "m", "n", "alpha", "A", "lda", "B", "ldb")
+    cases = []
+    for fname in ("edge-cases.json", "edge-cases-column-major.json"):
+        with open(os.path.join(ref, "tests", "strsm", fname)) as fh:
+            for tc in json.load(fh):
+                case = {k: tc[k] for k in keys}
+                case["layout"] = tc.get("layout", "row-major")
+                case["routine"] = "strsm"
+                case["source"] = f"tests/strsm/{fname}"
+                case["expected"], case["exact"] = exact_trsm(case)
+                cases.append(case)
+    return cases
+
+
 # ---- double-double lane cases (tests/shaders/src/test.dekker.js:98-138) ----
 
 def dd_lanes():
@@ -301,6 +367,7 @@ def main():
     _dump(edge_cases(ref), "gemm_edge_cases.json")
     _dump(gemmtr_edge_cases(ref), "gemmtr_edge_cases.json")
     _dump(symm_trmm_edge_cases(ref), "symm_trmm_edge_cases.json")
+    _dump(strsm_edge_cases(ref), "strsm_edge_cases.json")
     _dump(dd_lanes(), "dd_lanes.json")
     _dump(validation_params(ref), "validation_params.json")
     seeds = [0, 1, 2, 3, 42, 100, 111, 112, 113, 200, 300]

@@ -1,5 +1,6 @@
-"""Replays the reference's spec-driven argument validation for sgemm / dgemm and
-the gemmtr family (sgemmtr, ssyrk, ssyr2k and their d twins).
+"""Replays the reference's spec-driven argument validation for sgemm / dgemm, the
+gemmtr family (sgemmtr, ssyrk, ssyr2k and their d twins), ssymm / strmm (and
+d twins) and strsm.
 
 Follows tests/helpers/validation.js (runValidation, :455-560): a baseline
 argument set is built from the specs in tests/golden/validation_params.json
@@ -55,11 +56,13 @@ def build_specs(routine: str) -> dict:
     a_base = copy.deepcopy(P["A"])
     lvl3 = a_base.pop("level-3")
     a_spec = {**a_base, **lvl3}
-    if routine[1:] in ("symm", "trmm"):
-        # tests/ssymm/src/test.ssymm.js and tests/strmm/src/test.strmm.js
+    if routine[1:] in ("symm", "trmm", "trsm"):
+        # tests/ssymm/src/test.ssymm.js, tests/strmm/src/test.strmm.js and
+        # tests/strsm/src/test.strsm.js:32-63 (strsm's A spec adds a fill of
+        # well-conditioned triangles, which changes no validation outcome)
         n_spec["invalid"][-1]["error"] = "must be non-negative"
         specs = {"device": P["device"], "side": P["side"], "uplo": P["uplo"]}
-        if routine[1:] == "trmm":
+        if routine[1:] in ("trmm", "trsm"):
             specs.update(transA=P["trans"], diag=P["diag"])
         specs.update(layout=P["layout"], m=m_spec, n=n_spec, alpha=P["alpha"])
         if routine[1:] == "symm":

@@ -1,9 +1,10 @@
-"""``ssymm`` / ``dsymm`` and ``strmm`` / ``dtrmm`` with wgblas's arguments.
+"""``ssymm`` / ``dsymm``, ``strmm`` / ``dtrmm`` and ``strsm`` with wgblas's arguments.
 
-Mirrors src/ssymm/ssymm.mjs and src/strmm/strmm.mjs (and the d twins): the same
-argument order, validation order and messages, and return shapes. As in the
-reference, each runs as a pass that materializes a dense copy of the special
-operand followed by a plain GEMM on this library's kernels:
+Mirrors src/ssymm/ssymm.mjs, src/strmm/strmm.mjs (and the d twins) and
+src/strsm/strsm.mjs: the same argument order, validation order and messages,
+and return shapes. As in the reference, symm and trmm run as a pass that
+materializes a dense copy of the special operand followed by a plain GEMM on
+this library's kernels:
 
 * symm: ``wg_symmetrize`` mirrors A's stored ``uplo`` triangle into a dense
   matrix, then C := alpha*A*B + beta*C (side 'left') or alpha*B*A + beta*C
@@ -12,6 +13,10 @@ operand followed by a plain GEMM on this library's kernels:
   triangle, ones on the diagonal for ``diag='unit'``), the GEMM writes
   alpha*op(A)*B (or alpha*B*op(A)) into a scratch matrix with B's layout, and the
   block is copied back over B (B's leading-dimension padding is untouched).
+
+strsm is one call of ``wg_strsm``: a recursive blocked triangular solve in place
+on B, with substitution kernels on the 64-row diagonal blocks and GEMM updates
+between them.
 
 Plain arrays come back as new arrays (``{"C": ...}`` / ``{"B": ...}``); GpuMatrix
 operands are updated in place. The d variants compute in native fp64; dsymm
@@ -97,8 +102,9 @@ def _download_into(G, arr):
 
 def _validate_special(routine, device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, beta, C, ldc, layout):
     """The checks of src/ssymm/ssymm.mjs:46-118 (C given) or src/strmm/strmm.mjs:51-113
-    (transA and diag given), in order. Returns None to proceed or the quick-return value."""
-    trmm = C is None and routine.endswith("trmm")
+    and src/strsm/strsm.mjs:174-240 (transA and diag given), in order. Returns None
+    to proceed or the quick-return value."""
+    trmm = C is None and routine.endswith(("trmm", "trsm"))
     f64 = routine.startswith("d")
     is_arr = is_f64_array if f64 else is_f32_array
     arr_name = "Float64Array" if f64 else "Float32Array"
@@ -269,3 +275,55 @@ def strmm(device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout=
 def dtrmm(device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout="row-major"):
     """strmm in native fp64 (src/dtrmm/dtrmm.mjs)."""
     return _trmm("dtrmm", device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout)
+
+
+def _trsm(routine, device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout):
+    early = _validate_special(routine, device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, None, None,
+                              None, layout)
+    if early is not None:
+        return early
+    gpu = isinstance(B, GpuMatrix)
+    m, n, lda, ldb = (int(v) for v in (m, n, lda, ldb))
+    order = m if side == "left" else n
+    scratch = []
+    try:
+        if gpu:
+            GA, GB = A, B
+        else:
+            GA = _upload(device, A, order, order, lda, layout)
+            GB = _upload(device, B, m, n, ldb, layout)
+            scratch += [GA, GB]
+        # The column-major frame of B: a row-major B is B^T there, so the side
+        # and m/n swap and the operator becomes op(A)^T. A row-major A is A^T
+        # in that frame, which flips its stored triangle and once more the
+        # transpose (src/strsm/strsm.mjs:244-257 flips both for the same reason).
+        b_rm = GB.layout == "row-major"
+        a_rm = GA.layout == "row-major"
+        side_cm = (side == "left") != b_rm
+        trans_cm = ((transA == "transpose") != b_rm) != a_rm
+        lower_cm = (uplo == "lower") != a_rm
+        mc, nc = (n, m) if b_rm else (m, n)
+        ms = ct.c_float(0.0)
+        nat.check(nat.lib.wg_strsm(device.handle, nat.WG_SIDE_LEFT if side_cm else nat.WG_SIDE_RIGHT,
+                                   nat.WG_UPLO_LOWER if lower_cm else nat.WG_UPLO_UPPER, int(trans_cm),
+                                   nat.WG_DIAG_UNIT if diag == "unit" else nat.WG_DIAG_NON_UNIT, mc, nc, float(alpha),
+                                   GA._buf, 0, GA.lda, GB._buf, 0, GB.lda,
+                                   ct.byref(ms) if device.benchmark else None))
+        timed = {"gpuTimeMs": float(ms.value)} if device.benchmark else {}
+        if gpu:
+            nat.check(nat.lib.wg_device_sync(device.handle))
+            return timed
+        return {"B": _download_into(GB, B), **timed}
+    finally:
+        for G in scratch:
+            G.destroy()
+
+
+def strsm(device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout="row-major"):
+    """Solves op(A)*X = alpha*B (side 'left') or X*op(A) = alpha*B ('right') for X,
+    A triangular with its uplo triangle stored, overwriting B, in fp32
+    (src/strsm/strsm.mjs:160-583). Plain arrays come back as a new array
+    (``{"B": X}``); a GpuMatrix B is solved in place. alpha = 0 makes B a literal
+    zero without reading A or B. Infinity and NaN land where substitution puts
+    them (tests/strsm/src/test.strsm.js:498-578), for GpuMatrix operands too."""
+    return _trsm("strsm", device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb, layout)
