@@ -298,7 +298,8 @@ def time_special(wg, dev, name, steps, warmup, flush):
     finally:
         for g in (GA, GB, GC):
             g.destroy()
-    return {"tflops": work / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+    return {"tflops": work / (ms * 1e-3) / 1e12, "ms_per_step": ms, "routine": name[:5],
+            "shape": {"m": n, "n": n, "aOrder": n},
             "note": "public API call incl. its scratch allocation and the dense operand pass"}
 
 
@@ -358,7 +359,8 @@ def time_trsm(wg, dev, nrhs, steps, warmup, flush):
             g.destroy()
     work = float(order) * nrhs * order
     return {"tflops": work / (ms * 1e-3) / 1e12, "ms_per_step": ms, "ms_per_block": ms / (order // 64),
-            "finite": bool(np.all(np.isfinite(x))), "nrhs": nrhs,
+            "finite": bool(np.all(np.isfinite(x))), "routine": "strsm",
+            "shape": {"m": order, "n": nrhs, "aOrder": order},
             "note": "order 4096 left lower column-major; public API on GpuMatrix, B refreshed untimed"}
 
 
@@ -536,6 +538,18 @@ def panel_plan(w, world):
     return [int(widths[i]) for i in range(count.value)]
 
 
+def routine_of(w):
+    """The reference routine a workload times (the roofline tool's FLOP and byte counts)."""
+    prefix = w["routine"][0]
+    if w.get("syrk"):
+        return prefix + "syrk"
+    return prefix + "gemmtr" if w.get("uplo") else w["routine"]
+
+
+def shape_of(w):
+    return {"m": w["m"], "n": w["n"], "k": w["k"]}
+
+
 def config_of(w, name, world=1):
     shard = ""
     if w.get("sharded"):
@@ -547,7 +561,8 @@ def config_of(w, name, world=1):
             "parallelism": f"row-sharded x{world}" if w.get("sharded") else "single GPU",
             "m": w["m"], "n": w["n"], "k": w["k"], "lda": w["lda"], "ldb": w["ldb"], "ldc": w["ldc"],
             "alpha": w["alpha"], "beta": w["beta"], "inputs": "N(0,1) seeded" if w["data"] == "normal" else "U[-1,1] seeded",
-            "l2": "flushed between steps (512 MB device write outside the step events)"}
+            "l2": "flushed between steps (512 MB device write outside the step events)",
+            "routine": routine_of(w), "shape": shape_of(w)}
 
 
 _JSON_OUT = None
@@ -622,6 +637,11 @@ def main():
         extra["probes"] = {"fp32_ffma_tflops": fp32_peak, "fp64_dfma_tflops": fp64_dfma,
                            "fp64_dmma_tflops": fp64_dmma, "hbm_copy_gbs": hbm,
                            "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
+        for kind in ("hbm_read", "hbm_scale"):  # the other patterns of bandwidth.js
+            try:
+                extra["probes"][f"{kind}_gbs"] = dev.probe_peak(kind)
+            except wg.Error as e:
+                extra["probes"][f"{kind}_error"] = str(e)
         extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
         for name in ("dgemm4096", "sgemm512", "ragged", "sgemmtr4096", "ssyrk4096", "dsyrk4096") if world == 1 else ():
             if name == pick_workload(args, world):
@@ -630,7 +650,8 @@ def main():
             msx, profx, _, _ = time_resident(wg, dev, wx, max(3, args.steps // 2), 3, 1, flush)
             tf = flops(wx) / (statistics.mean(msx) * 1e-3) / 1e12
             pk = fp64_peak if wx["routine"] == "dgemm" else fp32_peak
-            extra[name] = {"tflops": tf, "ms_per_step": statistics.mean(msx),
+            extra[name] = {"tflops": tf, "ms_per_step": statistics.mean(msx), "routine": routine_of(wx),
+                           "shape": shape_of(wx),
                            f"pct_of_{'fp64' if wx['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf / pk,
                            "kernels": {k: v[1] / max(v[0], 1) for k, v in profx.items()}}
 
@@ -655,7 +676,8 @@ def main():
             ws = WORKLOADS["shard16384"]
             ms1, prof1, _, _ = time_sharded(wg, dev, c1, ws, 3, 3, 1, 0, flush)
             tf1 = flops(ws) / (statistics.mean(ms1) * 1e-3) / 1e12
-            extra["shard16384_1gpu"] = {"tflops": tf1, "ms_per_step": statistics.mean(ms1),
+            extra["shard16384_1gpu"] = {"tflops": tf1, "ms_per_step": statistics.mean(ms1), "routine": "sgemm",
+                                        "shape": shape_of(ws),
                                         "pct_of_fp32_peak": 100.0 * tf1 / fp32_peak if fp32_peak else None,
                                         "kernels": {k: v[1] / max(v[0], 1) for k, v in prof1.items()}}
         finally:

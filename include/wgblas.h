@@ -166,6 +166,8 @@ wg_status wg_device_kernel_launches(const wg_device *dev, uint64_t *launches);
 #define WG_PROBE_FP64_FMA 1 /* value: TFLOP/s of DFMA chains on every SM */
 #define WG_PROBE_HBM_COPY 2 /* value: GB/s (read + write) of a 2 GiB device copy */
 #define WG_PROBE_FP64_DMMA 3 /* value: TFLOP/s of FP64 tensor-core (mma.sync f64) chains */
+#define WG_PROBE_HBM_READ 4 /* value: GB/s of a 2 GiB read-only pass */
+#define WG_PROBE_HBM_SCALE 5 /* value: GB/s (read + write) of a 2 GiB in-place scale */
 wg_status wg_probe_peak(wg_device *dev, int kind, double *value);
 
 /* ---- device buffers: replace the storage of GpuMatrix / GpuVector ------- */

@@ -91,6 +91,7 @@ _sig("wg_triangularize", _st, c_dev_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _
 _sig("wg_buffer_copy_2d", _st, c_dev_p, c_buf_p, ct.c_size_t, ct.c_size_t, c_buf_p, ct.c_size_t, ct.c_size_t,
      ct.c_size_t, ct.c_size_t)
 WG_PROBE_FP32_FMA, WG_PROBE_FP64_FMA, WG_PROBE_HBM_COPY, WG_PROBE_FP64_DMMA = 0, 1, 2, 3
+WG_PROBE_HBM_READ, WG_PROBE_HBM_SCALE = 4, 5
 _sig("wg_device_set_profiling", _st, c_dev_p, ct.c_int)
 _sig("wg_device_profile_read", _st, c_dev_p, ct.POINTER(KernelProfile), ct.c_int, ct.POINTER(ct.c_int))
 _sig("wg_device_kernel_launches", _st, c_dev_p, ct.POINTER(ct.c_uint64))

@@ -103,9 +103,12 @@ class Device:
 
     def probe_peak(self, kind: str) -> float:
         """Roofline probe: 'fp32' / 'fp64' FMA-chain TFLOP/s, 'fp64_dmma' FP64 tensor-core
-        TFLOP/s, or 'hbm' copy GB/s."""
+        TFLOP/s, or HBM GB/s of a 2 GiB 'hbm' copy, 'hbm_read' read-only pass or
+        'hbm_scale' in-place read-modify-write (benchmarks/roofline/wgblas/bandwidth.js
+        takes the best of such patterns as the memory roof)."""
         code = {"fp32": nat.WG_PROBE_FP32_FMA, "fp64": nat.WG_PROBE_FP64_FMA, "hbm": nat.WG_PROBE_HBM_COPY,
-                "fp64_dmma": nat.WG_PROBE_FP64_DMMA}[kind]
+                "fp64_dmma": nat.WG_PROBE_FP64_DMMA, "hbm_read": nat.WG_PROBE_HBM_READ,
+                "hbm_scale": nat.WG_PROBE_HBM_SCALE}[kind]
         v = ct.c_double(0)
         nat.check(nat.lib.wg_probe_peak(self.handle, code, ct.byref(v)))
         return float(v.value)

@@ -1,10 +1,10 @@
-// Roofline probes: FP32 FFMA and FP64 DFMA peak rate and HBM copy bandwidth,
+// Roofline probes: FP32 FFMA, FP64 DFMA and DMMA peak rates and HBM bandwidth,
 // measured with CUDA events on the device handle's stream.
 //
 // The FMA probes follow the idea of the reference's benchmarks/roofline/wgblas/fma.js:1-72
 // (independent multiply-add chains per thread, enough threads to fill every
-// SM, a long loop so the issue rate is all that is measured); the copy probe
-// streams a buffer much larger than L2 through 16-byte loads and stores.
+// SM, a long loop so the issue rate is all that is measured); the bandwidth
+// probes stream a buffer much larger than L2 through 16-byte loads and stores.
 #include "internal.h"
 #include "tcgen05.cuh"
 
@@ -92,6 +92,29 @@ __global__ void copy_probe_kernel(const float4 *__restrict__ src, float4 *__rest
     dst[i] = src[i];
 }
 
+// Read-only stream: the store is guarded by a condition the (zeroed) data never
+// meets, so nothing is written, but the loads cannot be dropped.
+__global__ void read_probe_kernel(const float4 *__restrict__ src, float4 *__restrict__ sink, size_t n) {
+  float acc = 0.0f;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = src[i];
+    acc += (v.x + v.y) + (v.z + v.w);
+  }
+  if (acc == 1e30f) sink[0] = make_float4(acc, acc, acc, acc);
+}
+
+// In-place read-modify-write over one buffer (the sscal shape).
+__global__ void scale_probe_kernel(float4 *__restrict__ buf, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float4 v = buf[i];
+    v.x *= 1.0000001f;
+    v.y *= 1.0000001f;
+    v.z *= 1.0000001f;
+    v.w *= 1.0000001f;
+    buf[i] = v;
+  }
+}
+
 template <typename T>
 wg_status fma_probe(wg_device *d, double *tflops) {
   const int blocks = d->sm_count * 8, threads = 256, iters = 1 << 14;
@@ -119,24 +142,37 @@ wg_status fma_probe(wg_device *d, double *tflops) {
   return WG_OK;
 }
 
-wg_status copy_probe(wg_device *d, double *gbs) {
-  const size_t bytes = (size_t)1 << 31;  // 2 GiB each way, far above the 126 MB L2
+// Streams 2 GiB (far above the 126 MB L2) through 16-byte accesses in one of
+// three patterns, as the reference's benchmarks/roofline/wgblas/bandwidth.js:1-19
+// does, since no single pattern is fastest everywhere: a copy (read + write of
+// 2 GiB each), a read-only pass, or an in-place read-modify-write. GB/s counts
+// the bytes read plus the bytes written; best of three timed passes after a
+// warm-up pass.
+wg_status stream_probe(wg_device *d, int kind, double *gbs) {
+  const size_t bytes = (size_t)1 << 31;
   const size_t n = bytes / sizeof(float4);
   float4 *src = nullptr, *dst = nullptr;
   WG_CUDA(cudaMallocAsync((void **)&src, bytes, d->stream));
-  cudaError_t e = cudaMallocAsync((void **)&dst, bytes, d->stream);
+  cudaError_t e = kind == WG_PROBE_HBM_COPY ? cudaMallocAsync((void **)&dst, bytes, d->stream)
+                                            : cudaMallocAsync((void **)&dst, sizeof(float4), d->stream);
   if (e != cudaSuccess) {
     cudaFreeAsync(src, d->stream);
-    return wg_fail(WG_ERR_OUT_OF_MEMORY, "copy probe allocation failed: %s", cudaGetErrorString(e));
+    return wg_fail(WG_ERR_OUT_OF_MEMORY, "bandwidth probe allocation failed: %s", cudaGetErrorString(e));
   }
   WG_CUDA(cudaMemsetAsync(src, 0, bytes, d->stream));
   cudaEvent_t e0, e1;
   WG_CUDA(cudaEventCreate(&e0));
   WG_CUDA(cudaEventCreate(&e1));
   float best = 1e30f;
+  const unsigned blocks = (unsigned)d->sm_count * 16;
   for (int rep = 0; rep < 4; rep++) {
     cudaEventRecord(e0, d->stream);
-    copy_probe_kernel<<<d->sm_count * 16, 512, 0, d->stream>>>(src, dst, n);
+    if (kind == WG_PROBE_HBM_COPY)
+      copy_probe_kernel<<<blocks, 512, 0, d->stream>>>(src, dst, n);
+    else if (kind == WG_PROBE_HBM_READ)
+      read_probe_kernel<<<blocks, 512, 0, d->stream>>>(src, dst, n);
+    else
+      scale_probe_kernel<<<blocks, 512, 0, d->stream>>>(src, n);
     cudaEventRecord(e1, d->stream);
     WG_CUDA(cudaEventSynchronize(e1));
     float ms = 0;
@@ -148,7 +184,8 @@ wg_status copy_probe(wg_device *d, double *gbs) {
   cudaFreeAsync(src, d->stream);
   cudaFreeAsync(dst, d->stream);
   WG_CUDA(cudaStreamSynchronize(d->stream));
-  *gbs = 2.0 * (double)bytes / (best * 1e-3) / 1e9;
+  const double moved = kind == WG_PROBE_HBM_READ ? (double)bytes : 2.0 * (double)bytes;
+  *gbs = moved / (best * 1e-3) / 1e9;
   return WG_OK;
 }
 
@@ -184,7 +221,9 @@ extern "C" wg_status wg_probe_peak(wg_device *d, int kind, double *value) {
   switch (kind) {
     case WG_PROBE_FP32_FMA: return fma_probe<float>(d, value);
     case WG_PROBE_FP64_FMA: return fma_probe<double>(d, value);
-    case WG_PROBE_HBM_COPY: return copy_probe(d, value);
+    case WG_PROBE_HBM_COPY:
+    case WG_PROBE_HBM_READ:
+    case WG_PROBE_HBM_SCALE: return stream_probe(d, kind, value);
     case WG_PROBE_FP64_DMMA: return dmma_probe(d, value);
     default: return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown probe %d", kind);
   }
