@@ -364,6 +364,47 @@ def time_trsm(wg, dev, nrhs, steps, warmup, flush):
             "note": "order 4096 left lower column-major; public API on GpuMatrix, B refreshed untimed"}
 
 
+def time_gemv(wg, dev, routine, trans, steps, warmup, flush):
+    """sgemv / dgemv at 4096 x 4096, column-major A, unit strides (the layout of
+    the reference's base sweep, benchmarks/sgemv/wgblas/sgemv.js), through the
+    public API on a GpuMatrix and GpuVectors. A (64 / 128 MiB) is evicted from L2
+    before every step. Bytes: A once, x once, y read and written (the reference's
+    count); the HBM roof is the run's bandwidth probe."""
+    import torch
+
+    n = 4096
+    dt = np.float64 if routine == "dgemv" else np.float32
+    rnd = wg.randomFloat64Array if dt == np.float64 else wg.randomFloat32Array
+    GA = wg.GpuMatrix.from_(dev, rnd(n * n, -1, 1, 1), n, n, n, "column-major")
+    gx = wg.GpuVector.from_(dev, rnd(n, -1, 1, 2))
+    gy = wg.GpuVector.from_(dev, rnd(n, -1, 1, 3))
+    fn = getattr(wg, routine)
+    stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+    try:
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                flush.add_(1.0)
+                fn(dev, trans, n, n, 1.0, GA, n, gx, 1, 0.5, gy, 1)
+            dev.synchronize()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            for i in range(steps):
+                flush.add_(1.0)
+                starts[i].record(stream)
+                fn(dev, trans, n, n, 1.0, GA, n, gx, 1, 0.5, gy, 1)
+                ends[i].record(stream)
+            dev.synchronize()
+            ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    finally:
+        for g in (GA, gx, gy):
+            g.destroy()
+    item = np.dtype(dt).itemsize
+    nbytes = (n * n + 3 * n) * item
+    return {"gbs": nbytes / (ms * 1e-3) / 1e9, "tflops": 2.0 * n * n / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+            "routine": routine, "shape": {"m": n, "n": n, "trans": trans},
+            "note": "4096x4096 column-major, unit strides; public API on GpuMatrix/GpuVector; L2 flushed"}
+
+
 def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
     """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs)."""
     import torch
@@ -661,6 +702,15 @@ def main():
                 extra[name] = time_special(wg, dev, name, max(3, args.steps // 2), 3, flush)
             except wg.Error as e:  # a secondary line: report it, keep the headline
                 extra[name] = {"error": str(e)}
+        for routine in ("sgemv", "dgemv"):
+            for trans in ("no-transpose", "transpose"):
+                key = f"{routine}4096_{'N' if trans == 'no-transpose' else 'T'}"
+                try:
+                    extra[key] = time_gemv(wg, dev, routine, trans, max(3, args.steps // 2), 3, flush)
+                    if hbm:
+                        extra[key]["pct_of_hbm_copy"] = 100.0 * extra[key]["gbs"] / hbm
+                except wg.Error as e:
+                    extra[key] = {"error": str(e)}
         for nrhs in (64, 4096):
             try:
                 extra[f"strsm4096_n{nrhs}"] = time_trsm(wg, dev, nrhs, max(3, args.steps // 2), 3, flush)

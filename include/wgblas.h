@@ -326,6 +326,28 @@ wg_status wg_strsm(wg_device *dev, int side, int uplo, int transA, int diag, int
 wg_status wg_strsm_dev(wg_device *dev, int side, int uplo, int transA, int diag, int64_t m, int64_t n, float alpha,
                        const float *A, int64_t lda, float *B, int64_t ldb);
 
+/* ---- sgemv / dgemv (src/sgemv/sgemv.mjs, src/dgemv/dgemv.mjs) -------------
+ * y := alpha * op(A) * x + beta * y in the column-major frame: A is m x n with
+ * lda >= m; trans 0: op(A) = A, x has n entries, y has m; trans 1: op(A) = A^T,
+ * x has m entries, y has n. incx, incy > 0 (element strides); offsets in
+ * elements. m or n = 0, and alpha = 0 with beta = 1, return without touching
+ * y. alpha = 0 scales y by beta without reading A or x (zeros when beta = 0);
+ * beta = 0 does not read y. For trans 0 a column whose x entry is +-0 adds
+ * exactly 0 (reference BLAS skips it), so Infinity or NaN in that column of A
+ * does not reach y. dgemv computes in native fp64 (the reference emulates
+ * fp64 with f32 pairs). Queued on the device stream; gpu_ms as for wg_sgemm. */
+wg_status wg_sgemv(wg_device *dev, int trans, int64_t m, int64_t n, float alpha, const wg_buffer *A, int64_t offA,
+                   int64_t lda, const wg_buffer *x, int64_t offx, int64_t incx, float beta, wg_buffer *y,
+                   int64_t offy, int64_t incy, float *gpu_ms);
+wg_status wg_dgemv(wg_device *dev, int trans, int64_t m, int64_t n, double alpha, const wg_buffer *A, int64_t offA,
+                   int64_t lda, const wg_buffer *x, int64_t offx, int64_t incx, double beta, wg_buffer *y,
+                   int64_t offy, int64_t incy, float *gpu_ms);
+/* The same on raw device pointers of the device (no size checks). */
+wg_status wg_sgemv_dev(wg_device *dev, int trans, int64_t m, int64_t n, float alpha, const float *A, int64_t lda,
+                       const float *x, int64_t incx, float beta, float *y, int64_t incy);
+wg_status wg_dgemv_dev(wg_device *dev, int trans, int64_t m, int64_t n, double alpha, const double *A, int64_t lda,
+                       const double *x, int64_t incx, double beta, double *y, int64_t incy);
+
 /* ---- multi-GPU: C sharded by row blocks, B broadcast over NVLink (NCCL) ---- */
 /* The reference drives several GPUs only as independent devices with no data
  * exchange (src/init.mjs:14-29, examples/init-two-gpus/init-two-gpus.js); this

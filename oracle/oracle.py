@@ -385,3 +385,93 @@ def strsm_residual_factor(X, side, uplo, transA, diag, m, n, alpha, A, lda, B, l
     if np.all(zero):
         return 0.0
     return float(np.max(err[~zero] / bound[~zero]))
+
+
+# ---- sgemv / dgemv: the reference's test oracle, restated ---------------------------
+
+def _mat_at(A, lda, layout):
+    """A(i, j) of a matrix stored row- or column-major with leading dimension lda."""
+    return (lambda i, j: A[j * lda + i]) if layout == "column-major" else (lambda i, j: A[i * lda + j])
+
+
+def gemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy, layout="row-major"):
+    """y := alpha*op(A)*x + beta*y as the reference's tests compute it: the
+    published algorithm of @stdlib/blas-base-sgemv@0.1.1 / -dgemv@0.1.1 (npm
+    dependencies not vendored in the reference, called at
+    tests/helpers/stdlib.js:104-122,304-313), which is reference BLAS xGEMV:
+
+    * m = 0, n = 0, or alpha = 0 with beta = 1: y unchanged;
+    * y := beta*y first (zeros when beta = 0, y not read), then nothing more
+      when alpha = 0;
+    * the inner loop runs along A's storage: where op(A)'s rows are contiguous
+      (row-major no-transpose, column-major transpose) each y entry gets
+      temp = sum of A*x in increasing order, then y += alpha*temp; otherwise
+      column by column, temp = alpha*x_j and y += temp*A(:, j), a column whose
+      x entry is 0 skipped (tests/sgemv/src/test.sgemv.js:341-344).
+
+    Every operation rounds to the array's type (f32 for float32 inputs, f64 for
+    float64), as stdlib rounds each f32 step. Returns a new array the size of y;
+    entries outside the strided y keep their values."""
+    y = np.array(y, copy=True)
+    dt = y.dtype.type
+    if m == 0 or n == 0 or (alpha == 0 and beta == 1):
+        return y
+    A = np.asarray(A, dt)
+    x = np.asarray(x, dt)
+    no_t = trans == "no-transpose"
+    xlen, ylen = (n, m) if no_t else (m, n)
+    iy = np.arange(ylen) * incy
+    ix = np.arange(xlen) * incx
+    a, b = dt(alpha), dt(beta)
+    with np.errstate(all="ignore"):
+        if beta != 1:
+            y[iy] = dt(0) if beta == 0 else b * y[iy]
+        if alpha == 0:
+            return y
+        at = _mat_at(A, lda, layout)
+        rows_contiguous = no_t == (layout != "column-major")
+        yv = y[iy]
+        if rows_contiguous:  # dot products: temp over the contraction index, in order
+            temp = np.zeros(ylen, dt)
+            for p in range(xlen):
+                col = at(np.arange(ylen), p) if no_t else at(p, np.arange(ylen))
+                temp = temp + col * x[ix[p]]
+            yv = yv + a * temp
+        else:  # column by column, skipping zero x entries
+            for p in range(xlen):
+                xp = x[ix[p]]
+                if xp == 0:
+                    continue
+                t = a * xp
+                col = at(np.arange(ylen), p) if no_t else at(p, np.arange(ylen))
+                yv = yv + t * col
+        y[iy] = yv
+    return y
+
+
+def gemv_forward_factor(got, ref, trans, m, n, alpha, A, lda, x, incx, beta, y, incy, layout="row-major"):
+    """forwardFactor of tests/sgemv/helpers.js (eps = 2^-23) and tests/dgemv/helpers.js
+    (eps = 2^-48), chosen by y's type: max over outputs of |got - ref| /
+    (eps*((nTerms + 1)|alpha| sum|A||x| + |beta||y_in|)); an output whose bound is 0
+    must match exactly, else the factor is infinite."""
+    y = np.asarray(y)
+    eps = 2.0**-48 if y.dtype == np.float64 else 2.0**-23
+    no_t = trans == "no-transpose"
+    xlen, ylen = (n, m) if no_t else (m, n)
+    if ylen == 0 or xlen == 0:
+        return 0.0
+    at = _mat_at(np.abs(np.asarray(A, np.float64)), lda, layout)
+    xa = np.abs(np.asarray(x, np.float64)[np.arange(xlen) * incx])
+    i = np.arange(ylen)[:, None]
+    p = np.arange(xlen)[None, :]
+    mat = at(i, p) if no_t else at(p, i)
+    dot = mat @ xa
+    iy = np.arange(ylen) * incy
+    err = np.abs(np.asarray(got, np.float64)[iy] - np.asarray(ref, np.float64)[iy])
+    bound = eps * ((xlen + 1) * abs(alpha) * dot + abs(beta) * np.abs(y[iy].astype(np.float64)))
+    zero = bound == 0
+    if np.any(err[zero] != 0):
+        return float("inf")
+    if np.all(zero):
+        return 0.0
+    return float(np.max(err[~zero] / bound[~zero]))

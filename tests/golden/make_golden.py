@@ -33,6 +33,11 @@ strsm_edge_cases.json
     reference checks strsm by its backward residual
     (tests/strsm/helpers.js, factor <= 5 in tests/strsm/src/test.strsm.js), not
     bit for bit; the exact solution pins the restated stdlib oracle.
+gemv_edge_cases.json
+    The cases of tests/{sgemv,dgemv}/edge-cases*.json (inputs copied as data),
+    each with the exact y := alpha*op(A)*x + beta*y (strided gaps of y kept),
+    computed with rationals and checked to be exact in the routine's type; the
+    reference compares these outputs bit for bit (tests/sgemv/src/test.sgemv.js:116-153).
 dd_lanes.json
     The lane cases of tests/shaders/src/test.dekker.js:98-138 (inputs and the
     expected result of twoSum, twoProdBit, ddAdd and ddMul per lane), restated
@@ -41,7 +46,8 @@ dd_lanes.json
     a non-finite hi.
 validation_params.json
     The parameter specs the reference's sgemm/dgemm validation tests load
-    (tests/validation/params/{device,trans,layout,m,n,k,alpha,beta,A,B,C,ld,uplo}.json,
+    (tests/validation/params/{device,trans,layout,m,n,k,alpha,beta,A,B,C,ld,uplo,side,diag,
+    lda,x,incx,y,incy}.json,
     read by tests/sgemm/src/test.sgemm.js:23-56 and tests/sgemmtr/src/test.sgemmtr.js), copied as data: the invalid
     values with their expected error substrings and the edge values that must
     not throw. tests/validation_runner.py replays them.
@@ -276,6 +282,42 @@ def strsm_edge_cases(ref):
     return cases
 
 
+def exact_gemv(case):
+    layout = case.get("layout", "row-major")
+    m, n = case["m"], case["n"]
+    no_t = case["trans"] == "no-transpose"
+    xlen, ylen = (n, m) if no_t else (m, n)
+
+    def a(i, j):
+        return Fraction(_elem(case["A"], case["lda"], layout, i, j))
+
+    out = list(case["y"])
+    for r in range(ylen):
+        acc = sum((a(r, p) if no_t else a(p, r)) * Fraction(case["x"][p * case["incx"]]) for p in range(xlen))
+        val = Fraction(case["alpha"]) * acc + Fraction(case["beta"]) * Fraction(case["y"][r * case["incy"]])
+        fv = float(val)
+        if Fraction(fv) != val or (case["routine"] == "sgemv" and f32(fv) != fv):
+            raise ValueError(f"{case['label']}: result {val} is not exact")
+        out[r * case["incy"]] = fv
+    return out
+
+
+def gemv_edge_cases(ref):
+    keys = ("label", "trans", "m", "n", "alpha", "A", "lda", "x", "incx", "beta", "y", "incy")
+    cases = []
+    for routine in ("sgemv", "dgemv"):
+        for fname in ("edge-cases.json", "edge-cases-column-major.json"):
+            with open(os.path.join(ref, "tests", routine, fname)) as fh:
+                for tc in json.load(fh):
+                    case = {k: tc[k] for k in keys}
+                    case["layout"] = tc.get("layout", "row-major")
+                    case["routine"] = routine
+                    case["source"] = f"tests/{routine}/{fname}"
+                    case["expected"] = exact_gemv(case)
+                    cases.append(case)
+    return cases
+
+
 # ---- double-double lane cases (tests/shaders/src/test.dekker.js:98-138) ----
 
 def dd_lanes():
@@ -354,7 +396,8 @@ def _dump(obj, name):
 
 
 def validation_params(ref):
-    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld", "uplo", "side", "diag"]
+    names = ["device", "trans", "layout", "m", "n", "k", "alpha", "beta", "A", "B", "C", "ld", "uplo", "side", "diag",
+             "lda", "x", "incx", "y", "incy"]
     out = {}
     for name in names:
         with open(os.path.join(ref, "tests", "validation", "params", f"{name}.json")) as fh:
@@ -368,6 +411,7 @@ def main():
     _dump(gemmtr_edge_cases(ref), "gemmtr_edge_cases.json")
     _dump(symm_trmm_edge_cases(ref), "symm_trmm_edge_cases.json")
     _dump(strsm_edge_cases(ref), "strsm_edge_cases.json")
+    _dump(gemv_edge_cases(ref), "gemv_edge_cases.json")
     _dump(dd_lanes(), "dd_lanes.json")
     _dump(validation_params(ref), "validation_params.json")
     seeds = [0, 1, 2, 3, 42, 100, 111, 112, 113, 200, 300]

@@ -53,6 +53,11 @@ def test_reference_flop_and_byte_counts(rl):
     t = {"m": 4096, "n": 64, "aOrder": 4096}
     assert rl.ROUTINES["strsm"].flops(t) == 4096 * 64 * 4096
     assert rl.ROUTINES["strsm"].bytes(t) == (4096 * 4097 / 2 + 2 * 4096 * 64) * 4
+    v = {"m": 4096, "n": 1024, "trans": "transpose"}
+    assert rl.ROUTINES["sgemv"].flops(v) == 2 * 4096 * 1024
+    assert rl.ROUTINES["sgemv"].bytes(v) == (4096 * 1024 + 4096 + 2 * 1024) * 4
+    assert rl.ROUTINES["dgemv"].bytes(dict(v, trans="no-transpose")) == (4096 * 1024 + 1024 + 2 * 4096) * 8
+    assert rl.ROUTINES["sgemv"].level == 2
 
 
 def test_every_row_is_placed_with_its_bound(rl, line):

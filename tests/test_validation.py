@@ -24,7 +24,7 @@ def fake_device(wg):
 
 
 @pytest.mark.parametrize("routine", ["sgemm", "dgemm", "sgemmtr", "dgemmtr", "ssyrk", "dsyrk", "ssyr2k", "dsyr2k",
-                                     "ssymm", "dsymm", "strmm", "dtrmm", "strsm"])
+                                     "ssymm", "dsymm", "strmm", "dtrmm", "strsm", "sgemv", "dgemv"])
 def test_invalid_arguments_raise_reference_messages(wg, fake_device, routine):
     fn = getattr(wg, routine)
     n = 0

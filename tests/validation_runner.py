@@ -1,6 +1,6 @@
 """Replays the reference's spec-driven argument validation for sgemm / dgemm, the
 gemmtr family (sgemmtr, ssyrk, ssyr2k and their d twins), ssymm / strmm (and
-d twins) and strsm.
+d twins), strsm and sgemv / dgemv.
 
 Follows tests/helpers/validation.js (runValidation, :455-560): a baseline
 argument set is built from the specs in tests/golden/validation_params.json
@@ -56,6 +56,20 @@ def build_specs(routine: str) -> dict:
     a_base = copy.deepcopy(P["A"])
     lvl3 = a_base.pop("level-3")
     a_spec = {**a_base, **lvl3}
+    if routine[1:] == "gemv":
+        # tests/sgemv/src/test.sgemv.js:29-51 (tests/dgemv/src/test.dgemv.js the same at f64)
+        n_spec = copy.deepcopy(P["n"])
+        n_spec["edge"] = [e for e in n_spec["edge"] if e.get("value") != -1]
+        n_spec["invalid"] = n_spec["invalid"] + [{"value": -1, "error": "n must be non-negative", "label": "negative"}]
+        a_gemv = copy.deepcopy(P["A"])
+        a_gemv.pop("level-3", None)
+        specs = {"device": P["device"], "trans": P["trans"], "m": P["m"], "n": n_spec, "alpha": P["alpha"],
+                 "beta": P["beta"], "lda": P["lda"], "A": a_gemv, "x": P["x"], "incx": P["incx"], "y": P["y"],
+                 "incy": P["incy"], "layout": P["layout"]}
+        if routine.startswith("d"):
+            for name in ("A", "x", "y"):
+                specs[name] = _derive64(specs[name])
+        return specs
     if routine[1:] in ("symm", "trmm", "trsm"):
         # tests/ssymm/src/test.ssymm.js, tests/strmm/src/test.strmm.js and
         # tests/strsm/src/test.strsm.js:32-63 (strsm's A spec adds a fill of
@@ -111,6 +125,11 @@ def _dtype(spec_type):
 
 def _matrix_len(depends_on, dims):
     """ndArrayLen for a matrix spec (tests/helpers/validation.js:192-253)."""
+    if "incx" in depends_on or "incy" in depends_on:  # a level-2 vector (validation.js ndArrayLen case 2)
+        no_t = dims.get("trans", "no-transpose") == "no-transpose"
+        inc_key = "incx" if "incx" in depends_on else "incy"
+        length = (dims["n"] if no_t else dims["m"]) if inc_key == "incx" else (dims["m"] if no_t else dims["n"])
+        return max(0, (length - 1) * dims[inc_key] + 1)
     ld_key = next(d for d in depends_on if d.startswith("ld"))
     trans_key = next((d for d in depends_on if d.startswith("trans")), None)
     cm = dims.get("layout") == "column-major"
@@ -137,9 +156,17 @@ def baselines(specs, device):
             b[name] = np.array(v, _dtype(spec["type"])) if isinstance(v, list) else v
     b["device"] = device
     for name, spec in specs.items():
-        if spec.get("type") in ("float32array", "float64array") and name not in b:
-            dims = dict(b, lda=specs["lda"]["range"]["max"])
-            b[name] = np.ones(_matrix_len(spec["dependsOn"], dims), _dtype(spec["type"]))
+        if spec.get("type") not in ("float32array", "float64array") or name in b:
+            continue
+        deps = spec["dependsOn"]
+        inc = next((d for d in deps if d.startswith("inc")), None)
+        if inc:
+            # applyTransBaselines + buildArrayBaselines (validation.js:469-511): level-2
+            # vectors long enough for either trans, at the largest stride of the spec.
+            length = (max(b["m"], b["n"]) - 1) * specs[inc]["range"]["max"] + 1
+        else:
+            length = _matrix_len(deps, dict(b, lda=specs["lda"]["range"]["max"]))
+        b[name] = np.ones(length, _dtype(spec["type"]))
     return b
 
 
@@ -177,6 +204,9 @@ def cases(routine, device, kind, make_wrong_dtype_matrix=None):
 
 
 def call(fn, a):
+    if "incx" in a:  # gemv
+        return fn(a["device"], a["trans"], a["m"], a["n"], a["alpha"], a["A"], a["lda"], a["x"], a["incx"], a["beta"],
+                  a["y"], a["incy"], a["layout"])
     if "side" in a:  # symm / trmm
         if "diag" in a:
             return fn(a["device"], a["side"], a["uplo"], a["transA"], a["diag"], a["m"], a["n"], a["alpha"], a["A"],

@@ -142,6 +142,15 @@ WG_DIAG_NON_UNIT, WG_DIAG_UNIT = 0, 1
 _trsm_dims = [c_dev_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _i64, _i64, ct.c_float]
 _sig("wg_strsm", _st, *_trsm_dims, c_buf_p, _i64, _i64, c_buf_p, _i64, _i64, _f32p)
 _sig("wg_strsm_dev", _st, *_trsm_dims, ct.c_void_p, _i64, ct.c_void_p, _i64)
+_gemv_dims = [c_dev_p, ct.c_int, _i64, _i64]
+_sig("wg_sgemv", _st, *_gemv_dims, ct.c_float, c_buf_p, _i64, _i64, c_buf_p, _i64, _i64, ct.c_float, c_buf_p, _i64,
+     _i64, _f32p)
+_sig("wg_dgemv", _st, *_gemv_dims, ct.c_double, c_buf_p, _i64, _i64, c_buf_p, _i64, _i64, ct.c_double, c_buf_p,
+     _i64, _i64, _f32p)
+_sig("wg_sgemv_dev", _st, *_gemv_dims, ct.c_float, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_float, ct.c_void_p,
+     _i64)
+_sig("wg_dgemv_dev", _st, *_gemv_dims, ct.c_double, ct.c_void_p, _i64, ct.c_void_p, _i64, ct.c_double, ct.c_void_p,
+     _i64)
 c_comm_p = ct.c_void_p
 _sig("wg_comm_unique_id", _st, ct.c_char_p, ct.c_size_t)
 _sig("wg_comm_init_rank", _st, c_dev_p, ct.c_int, ct.c_int, ct.c_char_p, ct.c_size_t, ct.c_int, ct.POINTER(c_comm_p))

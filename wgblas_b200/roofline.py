@@ -73,6 +73,15 @@ def _trsm(elt):
             lambda p: (p["aOrder"] * (p["aOrder"] + 1) / 2.0 + 2.0 * p["m"] * p["n"]) * elt)
 
 
+def _gemv(elt):
+    def lens(p):
+        no_t = p.get("trans", "no-transpose") == "no-transpose"
+        return (p["n"], p["m"]) if no_t else (p["m"], p["n"])
+
+    return (lambda p: 2.0 * p["m"] * p["n"],
+            lambda p: (1.0 * p["m"] * p["n"] + lens(p)[0] + 2.0 * lens(p)[1]) * elt)
+
+
 def _routine(level, precision, pair, source):
     return Routine(level, precision, pair[0], pair[1], source)
 
@@ -91,6 +100,9 @@ ROUTINES = {
     "strmm": _routine(3, "fp32", _trmm(4), "benchmarks/strmm/wgblas/strmm.js:51-55"),
     "dtrmm": _routine(3, "fp64", _trmm(8), "benchmarks/dtrmm/wgblas/dtrmm.js:50-54"),
     "strsm": _routine(3, "fp32", _trsm(4), "benchmarks/strsm/wgblas/strsm.js:55-58"),
+    "sgemv": _routine(2, "fp32", _gemv(4), "assets/routines/routine_params.json (flops), "
+                      "benchmarks/sgemv/wgblas/sgemv.js:49 (bytes)"),
+    "dgemv": _routine(2, "fp64", _gemv(8), "benchmarks/dgemv/wgblas/dgemv.js:49"),
 }
 
 
