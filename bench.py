@@ -678,11 +678,6 @@ def main():
         extra["probes"] = {"fp32_ffma_tflops": fp32_peak, "fp64_dfma_tflops": fp64_dfma,
                            "fp64_dmma_tflops": fp64_dmma, "hbm_copy_gbs": hbm,
                            "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
-        for kind in ("hbm_read", "hbm_scale"):  # the other patterns of bandwidth.js
-            try:
-                extra["probes"][f"{kind}_gbs"] = dev.probe_peak(kind)
-            except wg.Error as e:
-                extra["probes"][f"{kind}_error"] = str(e)
         extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
         for name in ("dgemm4096", "sgemm512", "ragged", "sgemmtr4096", "ssyrk4096", "dsyrk4096") if world == 1 else ():
             if name == pick_workload(args, world):
@@ -702,15 +697,6 @@ def main():
                 extra[name] = time_special(wg, dev, name, max(3, args.steps // 2), 3, flush)
             except wg.Error as e:  # a secondary line: report it, keep the headline
                 extra[name] = {"error": str(e)}
-        for routine in ("sgemv", "dgemv"):
-            for trans in ("no-transpose", "transpose"):
-                key = f"{routine}4096_{'N' if trans == 'no-transpose' else 'T'}"
-                try:
-                    extra[key] = time_gemv(wg, dev, routine, trans, max(3, args.steps // 2), 3, flush)
-                    if hbm:
-                        extra[key]["pct_of_hbm_copy"] = 100.0 * extra[key]["gbs"] / hbm
-                except wg.Error as e:
-                    extra[key] = {"error": str(e)}
         for nrhs in (64, 4096):
             try:
                 extra[f"strsm4096_n{nrhs}"] = time_trsm(wg, dev, nrhs, max(3, args.steps // 2), 3, flush)
@@ -776,6 +762,23 @@ def main():
 
     e2e = time_e2e(wg, dev, w, max(3, args.steps // 2), args.warmup) if (rank == 0 and not w.get("sharded")) else None
     cb = None if (args.no_cpu_baseline or rank != 0 or world > 1) else cpu_baseline(w)
+    if not args.no_extra and world == 1 and not w.get("sharded"):
+        # Level-2 lines and the other bandwidth patterns, after every figure the
+        # headline line needs has been taken.
+        for kind in ("hbm_read", "hbm_scale"):  # the other patterns of bandwidth.js
+            try:
+                extra["probes"][f"{kind}_gbs"] = dev.probe_peak(kind)
+            except wg.Error as e:
+                extra["probes"][f"{kind}_error"] = str(e)
+        for routine in ("sgemv", "dgemv"):
+            for trans in ("no-transpose", "transpose"):
+                key = f"{routine}4096_{'N' if trans == 'no-transpose' else 'T'}"
+                try:
+                    extra[key] = time_gemv(wg, dev, routine, trans, max(3, args.steps // 2), 3, flush)
+                    if hbm:
+                        extra[key]["pct_of_hbm_copy"] = 100.0 * extra[key]["gbs"] / hbm
+                except wg.Error as e:
+                    extra[key] = {"error": str(e)}
     barrier(world)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
