@@ -17,8 +17,9 @@
 //   solve(second half, 1)
 //
 // so the m*n*order multiply-adds run almost entirely in a few large GEMMs
-// (the 3xTF32 tensor-core path, the FFMA kernel for small or non-finite
-// operands), and the diagonal blocks in `strsm_leaf`. The reference instead
+// (the 3xTF32 tensor-core path for the deep updates of the upper levels, the
+// FFMA kernel for shallow updates, small shapes and non-finite operands), and
+// the diagonal blocks in `strsm_leaf`. The reference instead
 // walks 64-row blocks one at a time with a k=64 update GEMM after each
 // (strsm.mjs:399-432) and, above eight blocks, applies explicit block inverses
 // (strsv_invert_block.wgsl). Substitution plus GEMM keeps stdlib's IEEE
@@ -39,6 +40,11 @@ namespace {
 constexpr int LEAF = 64;      // rows of a diagonal block
 constexpr int LEAF_RHS = 64;  // right-hand sides per CTA, one per thread
 constexpr int LS = LEAF + 4;  // shared row stride: keeps 16-byte alignment of each column
+// Updates at most this deep (the lower levels of the recursion) run on the FFMA
+// kernel: the tensor-core path costs a split pass plus a fixed time per call in
+// its MMA kernel (68 us for a 512^3 product, measured with per-kernel events)
+// that a k <= 256 update does not amortise.
+constexpr int64_t SIMT_MAX_K = 256;
 
 struct LeafArgs {
   const float *L;  // Lt(0, 0) of the diagonal block
@@ -149,17 +155,30 @@ struct Trsm {
     return WG_OK;
   }
 
+  // C := -op(X) op(Y) + beta C, on the FFMA kernel when k is shallow.
+  wg_status gemm(int tX, int tY, int64_t m, int64_t n, int64_t k, const float *X, int64_t ldx, const float *Y,
+                 int64_t ldy, float beta, float *C, int64_t ldc) const {
+    if (k > SIMT_MAX_K || d->sgemm_path == WG_SGEMM_TF32X3)
+      return wg_gemm_enqueue<float>(d, tX, tY, m, n, k, -1.0f, X, ldx, Y, ldy, beta, C, ldc);
+    if (m == 0 || n == 0) return WG_OK;
+    d->stats.calls++;
+    d->stats.simt_launches++;
+    wg_launch_scope scope(d, "sgemm_simt");
+    WG_CUDA(wg_launch_gemm_simt<float>(d->stream, tX, tY, m, n, k, -1.0f, X, ldx, Y, ldy, beta, C, ldc, d->dwords,
+                                       nullptr));
+    return WG_OK;
+  }
+
   // Bt[R] := beta * Bt[R] - Lt[R, J] * Xt[J], R = [r0, r0 + nr), J = [j0, j0 + nj).
   wg_status update(int64_t r0, int64_t nr, int64_t j0, int64_t nj, float beta) const {
     if (left) {
       // B[R, :] -= op(A)[R, J] * B[J, :]; op(A)[R, J] is A[R, J] or A[J, R]^T.
       const float *ap = trans ? A + j0 + r0 * lda : A + r0 + j0 * lda;
-      return wg_gemm_enqueue<float>(d, trans, 0, nr, other, nj, -1.0f, ap, lda, B + j0, ldb, beta, B + r0, ldb);
+      return gemm(trans, 0, nr, other, nj, ap, lda, B + j0, ldb, beta, B + r0, ldb);
     }
     // B[:, R] -= B[:, J] * op(A)[J, R]; op(A)[J, R] is A[J, R] or A[R, J]^T.
     const float *ap = trans ? A + r0 + j0 * lda : A + j0 + r0 * lda;
-    return wg_gemm_enqueue<float>(d, 0, trans, other, nr, nj, -1.0f, B + j0 * ldb, ldb, ap, lda, beta,
-                                  B + r0 * ldb, ldb);
+    return gemm(0, trans, other, nr, nj, B + j0 * ldb, ldb, ap, lda, beta, B + r0 * ldb, ldb);
   }
 
   wg_status solve(int64_t lo, int64_t hi, float alpha) const {
