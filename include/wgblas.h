@@ -174,6 +174,14 @@ wg_status wg_probe_peak(wg_device *dev, int kind, double *value);
 /* (src/classes/GpuMatrix.mjs:43-207, src/util/buffer.mjs:58-78,134-227)     */
 
 wg_status wg_buffer_alloc(wg_device *dev, size_t bytes, wg_buffer **out);
+/* A temporary for work queued on the device stream: its memory comes from the
+ * handle's stream-ordered pool (no mapping once the pool has grown to the
+ * size), valid for work queued on that stream after this call. Not for host
+ * copies (wg_buffer_upload / download). wg_buffer_free returns it to the pool in
+ * stream order, without waiting; free it before wg_device_close. */
+wg_status wg_buffer_alloc_async(wg_device *dev, size_t bytes, wg_buffer **out);
+/* Frees a buffer: wg_buffer_alloc's after the work queued on the device stream
+ * has finished (it waits), wg_buffer_alloc_async's in stream order. */
 wg_status wg_buffer_free(wg_buffer *buf);
 wg_status wg_buffer_size(const wg_buffer *buf, size_t *bytes);
 wg_status wg_buffer_device_ptr(const wg_buffer *buf, void **ptr);

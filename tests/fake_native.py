@@ -45,6 +45,9 @@ class FakeLib:
         ref._obj.value = self._next
         return 0
 
+    def wg_buffer_alloc_async(self, dev, nbytes, ref):
+        return self.wg_buffer_alloc(dev, nbytes, ref)
+
     def wg_buffer_free(self, b):
         self.bufs.pop(self._key(b), None)
         return 0

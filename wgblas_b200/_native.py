@@ -97,6 +97,7 @@ _sig("wg_device_profile_read", _st, c_dev_p, ct.POINTER(KernelProfile), ct.c_int
 _sig("wg_device_kernel_launches", _st, c_dev_p, ct.POINTER(ct.c_uint64))
 _sig("wg_probe_peak", _st, c_dev_p, ct.c_int, ct.POINTER(ct.c_double))
 _sig("wg_buffer_alloc", _st, c_dev_p, ct.c_size_t, ct.POINTER(c_buf_p))
+_sig("wg_buffer_alloc_async", _st, c_dev_p, ct.c_size_t, ct.POINTER(c_buf_p))
 _sig("wg_buffer_free", _st, c_buf_p)
 _sig("wg_buffer_size", _st, c_buf_p, ct.POINTER(ct.c_size_t))
 _sig("wg_buffer_device_ptr", _st, c_buf_p, ct.POINTER(ct.c_void_p))

@@ -223,26 +223,6 @@ cudaError_t h2d_block(T *dst, const T *src, int64_t ld, Stored s, cudaStream_t s
                            cudaMemcpyHostToDevice, st);
 }
 
-// A memory pool on the device that keeps what it has mapped when its
-// allocations are freed (release threshold = unlimited), so repeated host-array
-// calls reuse device memory instead of mapping and unmapping it every call. It
-// is destroyed, and its memory returned, with the device handle.
-cudaError_t staging_pool(int ordinal, cudaMemPool_t *out) {
-  cudaMemPoolProps props = {};
-  props.allocType = cudaMemAllocationTypePinned;
-  props.location.type = cudaMemLocationTypeDevice;
-  props.location.id = ordinal;
-  cudaError_t e = cudaMemPoolCreate(out, &props);
-  if (e != cudaSuccess) return e;
-  uint64_t keep = UINT64_MAX;
-  e = cudaMemPoolSetAttribute(*out, cudaMemPoolAttrReleaseThreshold, &keep);
-  if (e != cudaSuccess) {
-    cudaMemPoolDestroy(*out);
-    *out = nullptr;
-  }
-  return e;
-}
-
 // Panel width of the host-array path: wide enough that each panel's GEMM is
 // efficient, narrow enough that the upload, the GEMM and the read-back of
 // consecutive panels overlap.
@@ -297,7 +277,8 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   wg_device_guard guard(d->ordinal);
   if (!d->h2d) WG_CUDA(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
   if (!d->d2h) WG_CUDA(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
-  if (!d->staging) WG_CUDA(staging_pool(d->ordinal, &d->staging));
+  st = wg_staging_pool(d);
+  if (st != WG_OK) return st;
   cudaStream_t s = d->stream;
   const Stored sa = stored_a(transA, m, k), sb = stored_b(transB, n, k);
   const size_t na = reads_ab ? (size_t)(sa.rows * sa.cols) : 0;

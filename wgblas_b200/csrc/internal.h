@@ -111,6 +111,7 @@ struct wg_buffer {
   wg_device *dev;
   void *ptr;
   size_t bytes;
+  int pooled;  // memory from the device's stream-ordered pool (wg_buffer_alloc_async)
 };
 
 // Records a message for wg_last_error() on this thread and returns `st`.
@@ -192,6 +193,10 @@ void wg_tc_product_join(wg_tc_product *p);
 
 // Returns at least `bytes` of device scratch owned by the handle (stream-ordered reuse).
 wg_status wg_workspace(wg_device *dev, size_t bytes, void **ptr);
+// The device's stream-ordered memory pool (created on first use, destroyed
+// with the handle). It keeps the memory it has mapped when allocations are
+// freed, so repeated temporaries of the same sizes cost no mapping.
+wg_status wg_staging_pool(wg_device *dev);
 
 // ---- kernel launchers (gemm_simt.cu, sgemm_tf32x3.cu) ----
 

@@ -316,12 +316,58 @@ extern "C" wg_status wg_buffer_alloc(wg_device *d, size_t bytes, wg_buffer **out
   return WG_OK;
 }
 
+wg_status wg_staging_pool(wg_device *d) {
+  if (d->staging) return WG_OK;
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = d->ordinal;
+  cudaMemPool_t pool = nullptr;
+  WG_CUDA(cudaMemPoolCreate(&pool, &props));
+  uint64_t keep = UINT64_MAX;  // release threshold: keep what has been mapped
+  cudaError_t e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  if (e != cudaSuccess) {
+    cudaMemPoolDestroy(pool);
+    return wg_fail(WG_ERR_CUDA, "cudaMemPoolSetAttribute failed: %s", cudaGetErrorString(e));
+  }
+  d->staging = pool;
+  return WG_OK;
+}
+
+extern "C" wg_status wg_buffer_alloc_async(wg_device *d, size_t bytes, wg_buffer **out) {
+  if (!d || !out) return wg_fail(WG_ERR_INVALID_ARGUMENT, "invalid argument");
+  *out = nullptr;
+  wg_device_guard guard(d->ordinal);
+  wg_status st = wg_staging_pool(d);
+  if (st != WG_OK) return st;
+  wg_buffer *b = (wg_buffer *)calloc(1, sizeof(wg_buffer));
+  if (!b) return wg_fail(WG_ERR_OUT_OF_MEMORY, "host allocation failed");
+  b->dev = d;
+  b->bytes = bytes;
+  b->pooled = 1;
+  if (bytes) {
+    cudaError_t e = cudaMallocFromPoolAsync(&b->ptr, bytes, d->staging, d->stream);
+    if (e != cudaSuccess) {
+      free(b);
+      return wg_fail(e == cudaErrorMemoryAllocation ? WG_ERR_OUT_OF_MEMORY : WG_ERR_CUDA,
+                     "cudaMallocFromPoolAsync(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    }
+  }
+  *out = b;
+  return WG_OK;
+}
+
 extern "C" wg_status wg_buffer_free(wg_buffer *b) {
   if (!b) return WG_OK;
   wg_device_guard guard(b->dev->ordinal);
-  // Work queued on the owning stream may still read the buffer.
-  cudaStreamSynchronize(b->dev->stream);
-  if (b->ptr) cudaFree(b->ptr);
+  if (b->pooled) {
+    // Returned to the pool in stream order, after the work queued so far.
+    if (b->ptr) cudaFreeAsync(b->ptr, b->dev->stream);
+  } else {
+    // Work queued on the owning stream may still read the buffer.
+    cudaStreamSynchronize(b->dev->stream);
+    if (b->ptr) cudaFree(b->ptr);
+  }
   free(b);
   return WG_OK;
 }

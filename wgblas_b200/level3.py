@@ -158,8 +158,20 @@ def _validate_special(routine, device, side, uplo, transA, diag, m, n, alpha, A,
     return None
 
 
+def _scratch(device, rows, cols, ld, layout, dtype):
+    """A device temporary for the work this call queues: drawn from the handle's
+    stream-ordered pool (``wg_buffer_alloc_async``) and returned to it in stream
+    order on destroy(), so a call allocates and frees without mapping memory or
+    waiting for the GPU."""
+    outer = rows if layout == "row-major" else cols
+    buf = nat.c_buf_p()
+    nat.check(nat.lib.wg_buffer_alloc_async(device.handle, max(outer * ld, 1) * np.dtype(dtype).itemsize,
+                                            ct.byref(buf)))
+    return GpuMatrix(buf, rows, cols, ld, None, layout, device, dtype)
+
+
 def _dense(device, order, dtype):
-    return GpuMatrix.empty(device, order, order, order, "column-major", dtype)
+    return _scratch(device, order, order, order, "column-major", dtype)
 
 
 def _symm(routine, device, side, uplo, m, n, alpha, A, lda, B, ldb, beta, C, ldc, layout):
@@ -237,7 +249,7 @@ def _trmm(routine, device, side, uplo, transA, diag, m, n, alpha, A, lda, B, ldb
                                            order))
         # alpha*op(A)*B (or alpha*B*op(A)) into scratch with B's layout, then over B.
         outer = m if GB.layout == "row-major" else n
-        T = GpuMatrix.empty(device, m, n, ldb, GB.layout, dt)
+        T = _scratch(device, m, n, ldb, GB.layout, dt)
         scratch.append(T)
         X, Y = (D, GB) if side == "left" else (GB, D)
         r = _execute(f64, device, "no-transpose", "no-transpose", m, n, order, alpha, X, X.lda, Y, Y.lda, 0.0, T,
