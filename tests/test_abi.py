@@ -66,3 +66,26 @@ def test_library_random_matches_oracle_and_golden(wg, oracle):
 def test_unseeded_random_differs(wg):
     a, b = wg.randomFloat32Array(64), wg.randomFloat32Array(64)
     assert not np.array_equal(a, b) and a.min() >= -1 and a.max() < 1
+
+
+def test_every_declared_function_has_a_binding(wg):
+    """_native declares argument and result types for every entry point, so no
+    call goes through ctypes' int defaults."""
+    lib = wg._native.lib
+    unbound = [n for n in _declared() if getattr(lib, n).argtypes is None]
+    assert not unbound, unbound
+
+
+def test_null_device_is_rejected_by_the_level3_and_level2_entry_points(wg):
+    L, N = wg._native.lib, wg._native
+    bad = N.WG_ERR_INVALID_ARGUMENT
+    assert L.wg_strsm(None, 0, 1, 0, 0, 2, 2, 1.0, None, 0, 2, None, 0, 2, None) == bad
+    assert L.wg_strsm_dev(None, 0, 1, 0, 0, 2, 2, 1.0, None, 2, None, 2) == bad
+    assert L.wg_sgemv(None, 0, 2, 2, 1.0, None, 0, 2, None, 0, 1, 0.0, None, 0, 1, None) == bad
+    assert L.wg_dgemv(None, 1, 2, 2, 1.0, None, 0, 2, None, 0, 1, 0.0, None, 0, 1, None) == bad
+    assert L.wg_sgemv_dev(None, 0, 2, 2, 1.0, None, 2, None, 1, 0.0, None, 1) == bad
+    assert L.wg_symmetrize(None, 4, 1, 2, None, 0, 2, None, 0, 2) == bad
+    assert L.wg_triangularize(None, 8, 2, 0, 1, 2, None, 0, 2, None, 0, 2) == bad
+    h = N.c_buf_p()
+    assert L.wg_buffer_alloc_async(None, 64, ct.byref(h)) == bad
+    assert b"NULL" in L.wg_last_error() or b"invalid" in L.wg_last_error()
