@@ -69,6 +69,14 @@ WORKLOADS = {
                       lda=4096, ldb=4096, ldc=4096, alpha=1.0, beta=0.0, data="uniform", uplo=1, syrk=True),
 }
 PANEL_COLS = 0  # B broadcast panels of the sharded workloads: 0 = the library's plan
+# DRAM traffic of one launch of the dominant kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum, bytes) from the ncu capture of the same kernel and
+# workload summarised in profiles/ (tests/test_bench_traffic.py keeps these in
+# step with those files).
+NCU_TRAFFIC = {
+    ("sgemm4096", "sgemm_tf32x3_mma"): (623.8e6, 63.2e6, "profiles/sgemm_tf32x3_4096_TN.md"),
+    ("dgemm4096", "dgemm_dmma"): (1231.7e6, 120.5e6, "profiles/dgemm_dmma_4096_NT.md"),
+}
 
 
 def flops(w):
@@ -755,6 +763,11 @@ def main():
         roof = {"bound": "fp64-simt" if w["routine"] == "dgemm" else "fp32-simt", "achieved": achieved,
                 "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None, "traffic": None,
                 "peak_basis": "FMA-chain probe measured in this run (no FP32/FP64 SIMT figure in MEASURED_PEAKS.json)"}
+    traffic = NCU_TRAFFIC.get((pick_workload(args, world), dom[0]))
+    if traffic:
+        roof["traffic"] = traffic[0] + traffic[1]
+        roof["traffic_unit"] = "bytes per launch (DRAM read + write)"
+        roof["traffic_source"] = f"ncu capture of this kernel and workload, {traffic[2]}"
     roof["kernel"] = dom[0]
     roof["kernel_ms"] = dom_ms
     roof["launches_per_step"] = dom[1][0] / args.steps
