@@ -39,3 +39,24 @@ def test_bounded_wait_rejects_bad_budget(wg, device):
     nat = wg._native
     assert nat.lib.wg_selftest_bounded_wait(device.handle, 0) == nat.WG_ERR_INVALID_ARGUMENT
     assert nat.lib.wg_selftest_bounded_wait(device.handle, 2_000_000) == nat.WG_ERR_INVALID_ARGUMENT
+
+
+def test_a_rank_that_leaves_between_steps(wg):
+    """Two GPUs (skipped with fewer): rank 1 leaves after a sharded product;
+    rank 0 learns of it from the store before its next launch, aborts its
+    communicator without waiting on the departed rank, and keeps computing."""
+    import os
+    import subprocess
+    import sys
+
+    if wg._native.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "180", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29541",
+           os.path.join(root, "tests", "leave_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=260)
+    print(r.stdout[-3000:], r.stderr[-3000:])
+    assert r.returncode == 0
+    assert "rank 1 left" in r.stdout and "device still computes: True" in r.stdout
