@@ -24,6 +24,11 @@ column panels (the library's planned widths for sgemm, one panel for dgemm),
 each panel's GEMM overlapping the next panel's transfer;
 value = total FLOPs / max over ranks of the step time (strong scaling).
 
+At N=1 the line's "extra" also carries the other configs and the next routines
+at the reference's benchmark shapes (gemmtr/syrk, symm/trmm, strsm, gemv), each
+with "routine", "shape" and "ms_per_step" for the roofline report
+(python -m wgblas_b200.roofline), and the roofline probes of the run.
+
 --impl reference times the reference's arithmetic on the host cores instead:
 the CPU oracle's restatement of the reference's fp32 shader arithmetic
 (oracle/, "port"; the reference itself runs only through WebGPU, which has no
