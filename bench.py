@@ -27,7 +27,8 @@ value = total FLOPs / max over ranks of the step time (strong scaling).
 At N=1 the line's "extra" also carries the other configs and the next routines
 at the reference's benchmark shapes (gemmtr/syrk, symm/trmm, strsm, gemv), each
 with "routine", "shape" and "ms_per_step" for the roofline report
-(python -m wgblas_b200.roofline), and the roofline probes of the run.
+(python -m wgblas_b200.roofline), the roofline probes of the run, and a cuBLAS
+column (torch.mm at 4096^3, fp32 with TF32 off and fp64) for comparison.
 
 --impl reference times the reference's arithmetic on the host cores instead:
 the CPU oracle's restatement of the reference's fp32 shader arithmetic
@@ -418,6 +419,42 @@ def time_gemv(wg, dev, routine, trans, steps, warmup, flush):
             "note": "4096x4096 column-major, unit strides; public API on GpuMatrix/GpuVector; L2 flushed"}
 
 
+def time_cublas(dt, steps, warmup, flush, local):
+    """The library-GEMM comparison column of the reference's build plan: torch.mm
+    (cuBLAS) at 4096^3 on the same GPU, fp32 with TF32 off (the FP32 SIMT path,
+    the accuracy class of sgemm) or fp64, L2 flushed between steps. Not part of
+    the product; reported beside it."""
+    import torch
+
+    n = 4096
+    device = torch.device("cuda", local)
+    torch_dt = torch.float64 if dt == "f64" else torch.float32
+    g = torch.Generator(device=device).manual_seed(5)
+    A = torch.rand((n, n), generator=g, device=device, dtype=torch_dt) * 2 - 1
+    B = torch.rand((n, n), generator=g, device=device, dtype=torch_dt) * 2 - 1
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for _ in range(warmup):
+            flush.add_(1.0)
+            C = torch.mm(A, B)
+        torch.cuda.synchronize(device)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        for i in range(steps):
+            flush.add_(1.0)
+            starts[i].record()
+            C = torch.mm(A, B)
+            ends[i].record()
+        torch.cuda.synchronize(device)
+        ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del A, B, C
+    return {"tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+            "note": f"torch.mm (cuBLAS) {n}^3 {'fp64' if dt == 'f64' else 'fp32, TF32 off'}; comparison only"}
+
+
 def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
     """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs)."""
     import torch
@@ -788,6 +825,12 @@ def main():
                 extra["probes"][f"{kind}_gbs"] = dev.probe_peak(kind)
             except wg.Error as e:
                 extra["probes"][f"{kind}_error"] = str(e)
+        for dt in ("f32", "f64"):
+            key = f"cublas_{'d' if dt == 'f64' else 's'}gemm4096"
+            try:
+                extra[key] = time_cublas(dt, max(3, args.steps // 2), 3, flush, local)
+            except RuntimeError as e:
+                extra[key] = {"error": str(e)}
         for routine in ("sgemv", "dgemv"):
             for trans in ("no-transpose", "transpose"):
                 key = f"{routine}4096_{'N' if trans == 'no-transpose' else 'T'}"
