@@ -7,6 +7,7 @@ import os
 import re
 
 import numpy as np
+import pytest
 
 from conftest import ROOT, bits_equal, load_golden
 
@@ -89,3 +90,55 @@ def test_null_device_is_rejected_by_the_level3_and_level2_entry_points(wg):
     h = N.c_buf_p()
     assert L.wg_buffer_alloc_async(None, 64, ct.byref(h)) == bad
     assert b"NULL" in L.wg_last_error() or b"invalid" in L.wg_last_error()
+
+
+def _blank_device():
+    """A zeroed block standing in for a device handle: the argument checks of the
+    entry points below run before any field is read, and a zero compute
+    capability then stops them with WG_ERR_NOT_SUPPORTED, before any CUDA call."""
+    block = (ct.c_char * 65536)()
+    return block, ct.cast(block, ct.c_void_p)
+
+
+@pytest.mark.parametrize("args,status,text", [
+    ((2, 1, 0, 0, 4, 3, 4, 4), "INVALID_ARGUMENT", "side must be"),
+    ((0, 0, 0, 0, 4, 3, 4, 4), "INVALID_ARGUMENT", "uplo must be"),
+    ((0, 1, 2, 0, 4, 3, 4, 4), "INVALID_ARGUMENT", "transA must be"),
+    ((0, 1, 0, 2, 4, 3, 4, 4), "INVALID_ARGUMENT", "diag must be"),
+    ((0, 1, 0, 0, -1, 3, 4, 4), "INVALID_ARGUMENT", "m and n must be non-negative."),
+    ((0, 1, 0, 0, 4, 3, 0, 4), "INVALID_ARGUMENT", "lda and ldb must be positive."),
+    ((0, 1, 0, 0, 4, 3, 3, 4), "INVALID_ARGUMENT", "lda must be >= m."),
+    ((1, 1, 0, 0, 4, 3, 2, 4), "INVALID_ARGUMENT", "lda must be >= n."),
+    ((0, 1, 0, 0, 4, 3, 4, 3), "INVALID_ARGUMENT", "ldb must be >= rows of B as stored."),
+    ((0, 1, 0, 0, 0, 3, 1, 1), "OK", ""),
+    ((0, 2, 1, 1, 4, 3, 4, 4), "NOT_SUPPORTED", "not a Blackwell"),
+])
+def test_strsm_argument_checks(wg, args, status, text):
+    N = wg._native
+    keep, dev = _blank_device()
+    side, uplo, trans, diag, m, n, lda, ldb = args
+    st = N.lib.wg_strsm_dev(dev, side, uplo, trans, diag, m, n, 1.0, None, lda, None, ldb)
+    assert st == getattr(N, "WG_" + status if status == "OK" else "WG_ERR_" + status)
+    if text:
+        assert text in N.lib.wg_last_error().decode()
+
+
+@pytest.mark.parametrize("args,status,text", [
+    ((2, 4, 3, 4, 1, 1), "INVALID_ARGUMENT", "trans must be"),
+    ((0, -1, 3, 4, 1, 1), "INVALID_ARGUMENT", "m and n must be non-negative."),
+    ((0, 4, 3, 4, 0, 1), "INVALID_ARGUMENT", "incx and incy must be positive."),
+    ((1, 4, 3, 4, 1, -2), "INVALID_ARGUMENT", "incx and incy must be positive."),
+    ((0, 4, 3, 0, 1, 1), "INVALID_ARGUMENT", "lda must be positive."),
+    ((0, 4, 3, 3, 1, 1), "INVALID_ARGUMENT", "lda must be >= rows of A as stored."),
+    ((0, 4, 0, 1, 1, 1), "OK", ""),
+    ((1, 4, 3, 5, 2, 3), "NOT_SUPPORTED", "not a Blackwell"),
+])
+def test_gemv_argument_checks(wg, args, status, text):
+    N = wg._native
+    keep, dev = _blank_device()
+    trans, m, n, lda, incx, incy = args
+    for fn in (N.lib.wg_sgemv_dev, N.lib.wg_dgemv_dev):
+        st = fn(dev, trans, m, n, 1.0, None, lda, None, incx, 0.5, None, incy)
+        assert st == getattr(N, "WG_" + status if status == "OK" else "WG_ERR_" + status)
+        if text:
+            assert text in N.lib.wg_last_error().decode()
