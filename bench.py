@@ -216,6 +216,67 @@ def barrier(world):
         dist.barrier()
 
 
+PARITY_COLS = 16  # sampled columns of C checked after the timed region
+
+
+def parity_columns(w, m_rows, A, lda, B, C0, ldc, got, ldg, ncols=PARITY_COLS):
+    """Checks sampled columns of one result against the fp64 truth (numpy only).
+
+    A is this rank's op(A) source (column-major, ``lda``; ``m_rows`` rows of
+    op(A)), B the full stored B (ld = w["ldb"]), C0 the C the checked call
+    started from (column-major, ld ``ldc``) and got the C it left (ld ``ldg``). The bound is
+    the north star's: |got - truth| <= 2*K*2^-24*(|alpha| sum|a||b| + |beta||c|)
+    for sgemm, 4*K*2^-53*(...) for dgemm. The truth is numpy's fp64 product,
+    whose own error (at most K*2^-53 of the same sum) counts against the
+    measured one, so a pass is never looser than the stated bound allows."""
+    k, n = w["k"], w["n"]
+    ta, tb = w["transA"], w["transB"]
+    cols = np.unique(np.linspace(0, n - 1, ncols).astype(np.int64))
+    if ta:
+        opA = A[: m_rows * lda].reshape(m_rows, lda)[:, :k]
+    else:
+        opA = A[: k * lda].reshape(k, lda)[:, :m_rows].T
+    ldb = w["ldb"]
+    if tb:
+        Bs = np.stack([B[j + np.arange(k) * ldb] for j in cols], axis=1)
+    else:
+        Bs = np.stack([B[j * ldb: j * ldb + k] for j in cols], axis=1)
+    Cs = np.stack([C0[j * ldc: j * ldc + m_rows] for j in cols], axis=1).astype(np.float64)
+    Gs = np.stack([got[j * ldg: j * ldg + m_rows] for j in cols], axis=1).astype(np.float64)
+    A64 = opA.astype(np.float64)
+    B64 = Bs.astype(np.float64)
+    alpha, beta = float(w["alpha"]), float(w["beta"])
+    truth = alpha * (A64 @ B64) + beta * Cs
+    np.abs(A64, out=A64)
+    absab = abs(alpha) * (A64 @ np.abs(B64)) + abs(beta) * np.abs(Cs)
+    del A64
+    unit = 2.0 * k * 2.0 ** -24 if w["routine"] == "sgemm" else 4.0 * k * 2.0 ** -53
+    bound = unit * absab
+    err = np.abs(Gs - truth)
+    finite = bool(np.all(np.isfinite(Gs)))
+    ratio = float(np.max(err / np.where(bound > 0, bound, 1.0))) if err.size else 0.0
+    return {"ok": bool(finite and np.all(err <= bound)), "max_err_over_bound": ratio,
+            "cols": int(len(cols)), "rows": int(m_rows),
+            "bound": "2*K*2^-24*(|alpha|sum|a||b|+|beta||c|)" if w["routine"] == "sgemm"
+            else "4*K*2^-53*(|alpha|sum|a||b|+|beta||c|)",
+            "truth": "numpy fp64 product of the sampled columns"}
+
+
+def parity_over_ranks(par, world):
+    """Every rank's parity folded into one record: ok on all ranks, the worst ratio."""
+    if world == 1:
+        return par
+    ok = min_over_ranks(1.0 if par["ok"] else 0.0, world) > 0.5
+    ratio = max_over_ranks(par["max_err_over_bound"], world)
+    out = dict(par, ok=ok, max_err_over_bound=ratio, ranks=world)
+    out["rows"] = int(sum_over_ranks(par["rows"], world))
+    return out
+
+
+def min_over_ranks(x, world):
+    return -max_over_ranks(-float(x), world)
+
+
 def gemm_enqueue(wg, dev, w, GA, GB, GC):
     """One step on resident operands, queued on the device stream (no host sync)."""
     nat = wg._native
@@ -231,9 +292,14 @@ def gemm_enqueue(wg, dev, w, GA, GB, GC):
                  GB._buf, 0, w["ldb"], w["beta"], GC._buf, 0, w["ldc"], None))
 
 
-def time_resident(wg, dev, w, steps, warmup, world, flush):
-    """Device-timed steps on resident operands: returns (ms_per_step list, profile, launches)."""
+def time_resident(wg, dev, w, steps, warmup, world, flush, parity=True):
+    """Device-timed steps on resident operands: returns (ms_per_step list, profile,
+    launches, wall seconds, parity). After the timed region C is restored, one
+    more call runs, and sampled columns of its result are checked against the
+    fp64 truth (parity_columns)."""
     import torch
+
+    from wgblas_b200.classes import _upload
 
     A, B, C = host_inputs(wg, w)
     (ar, ac), (br, bc) = stored(w)
@@ -268,10 +334,21 @@ def time_resident(wg, dev, w, steps, warmup, world, flush):
             prof = dev.profile_read()
             dev.check()
             ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+            par = None
+            if parity:
+                _upload(GC._buf, C[: w["ldc"] * w["n"]])
+                gemm_enqueue(wg, dev, w, GA, GB, GC)
+                dev.synchronize()
+                dev.check()
+                got = GC.read()
+                if w.get("uplo"):
+                    par = None  # the gemmtr lines: parity lives in the tests (triangle semantics)
+                else:
+                    par = parity_columns(w, w["m"], A, w["lda"], B, C, w["ldc"], got, w["m"])
     finally:
         for g in (GA, GB, GC):
             g.destroy()
-    return ms, prof, launches, wall
+    return ms, prof, launches, wall, par
 
 
 def time_special(wg, dev, name, steps, warmup, flush):
@@ -455,21 +532,36 @@ def time_cublas(dt, steps, warmup, flush, local):
             "note": f"torch.mm (cuBLAS) {n}^3 {'fp64' if dt == 'f64' else 'fp32, TF32 off'}; comparison only"}
 
 
-def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
-    """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs)."""
-    import torch
-
-    from wgblas_b200.shard import gemm_sharded, plan_rows
+def sharded_inputs(wg, w, world, rank):
+    """This rank's seeded row blocks of op(A) and C (dense column-major, ld = its
+    rows) and the full B (generated on every rank: the root uploads it, the
+    others use it only to check their result)."""
+    from wgblas_b200.shard import plan_rows
 
     m, n, k = w["m"], w["n"], w["k"]
     offs = plan_rows(m, world)
     mr = offs[rank + 1] - offs[rank]
     dt = np.float64 if w["routine"] == "dgemm" else np.float32
     rnd = wg.randomFloat64Array if dt == np.float64 else wg.randomFloat32Array
-    GA = wg.GpuMatrix.from_(dev, rnd(mr * k, -1, 1, 10 + rank), mr, k, mr, "column-major")
-    GC = wg.GpuMatrix.from_(dev, rnd(mr * n, -1, 1, 30 + rank), mr, n, mr, "column-major")
+    return offs, mr, rnd(mr * k, -1, 1, 10 + rank), rnd(k * n, -1, 1, 2), rnd(mr * n, -1, 1, 30 + rank)
+
+
+def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush, parity=True):
+    """Device-timed steps of the row-sharded GEMM (B broadcast + local GEMMs).
+    After the timed region every rank restores its C rows, one more sharded call
+    runs, and each rank checks sampled columns of its rows against the fp64
+    truth (parity_columns); the record is folded over the ranks."""
+    import torch
+
+    from wgblas_b200.classes import _upload
+    from wgblas_b200.shard import gemm_sharded
+
+    m, n, k = w["m"], w["n"], w["k"]
+    offs, mr, A, B, C0 = sharded_inputs(wg, w, world, rank)
+    GA = wg.GpuMatrix.from_(dev, A, mr, k, mr, "column-major")
+    GC = wg.GpuMatrix.from_(dev, C0, mr, n, mr, "column-major")
     # B lives on the root only; the other ranks receive it into the library's buffer.
-    GB = wg.GpuMatrix.from_(dev, rnd(k * n, -1, 1, 2), k, n, k, "column-major") if rank == 0 else None
+    GB = wg.GpuMatrix.from_(dev, B, k, n, k, "column-major") if rank == 0 else None
     stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
 
     def step():
@@ -505,11 +597,21 @@ def time_sharded(wg, dev, comm, w, steps, warmup, world, rank, flush):
             prof = dev.profile_read()
             dev.check()
             ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+            par = None
+            if parity:
+                _upload(GC._buf, C0)
+                barrier(world)
+                step()
+                dev.synchronize()
+                comm.wait()
+                dev.check()
+                par = parity_columns(w, mr, A, mr, B, C0, mr, GC.read(), mr)
+                par = parity_over_ranks(par, world)
     finally:
         for g in (GA, GB, GC):
             if g is not None:
                 g.destroy()
-    return ms, prof, launches, wall
+    return ms, prof, launches, wall, par
 
 
 def time_e2e(wg, dev, w, steps, warmup):
@@ -536,6 +638,56 @@ def time_e2e(wg, dev, w, steps, warmup):
     sec = statistics.mean(times)
     return {"value": flops(w) / sec / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "ms_per_step": sec * 1e3, "api": f"wgblas_b200.{w['routine']}"}
+
+
+def time_e2e_sharded(wg, dev, comm, w, steps, warmup, world, rank):
+    """The sharded metric end to end through the public host-array call
+    (wgblas_b200.shard.gemm_sharded_host): every step each rank uploads its row
+    blocks of op(A) and C from page-locked host memory, the root uploads B, the
+    product runs sharded, C is gathered on the root and read back into a
+    page-locked array. Timed with CUDA events on each rank's device stream
+    around the whole call; the step time is the max over ranks."""
+    import torch
+
+    from wgblas_b200.shard import gemm_sharded_host
+
+    m, n, k = w["m"], w["n"], w["k"]
+    offs, mr, A, B, C0 = sharded_inputs(wg, w, world, rank)
+    dt = A.dtype
+
+    def pinned(x):
+        p = wg.pinned_empty(x.size, dt)
+        p[:] = x
+        return p
+
+    Ap, Cp = pinned(A), pinned(C0)
+    Bp = pinned(B) if rank == 0 else None
+    del A, B, C0
+    out = wg.pinned_empty(m * n, dt) if rank == 0 else None
+    stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+
+    def call():
+        gemm_sharded_host(comm, w["transA"], w["transB"], mr, n, k, w["alpha"], Ap, Bp, k, w["beta"], Cp, offs,
+                          root=0, panel_cols=PANEL_COLS, out=out)
+
+    for _ in range(max(1, warmup // 2)):
+        call()
+    times = []
+    for _ in range(steps):
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        call()
+        t1.record(stream)
+        t1.synchronize()
+        times.append(t0.elapsed_time(t1))
+    ms = max_over_ranks(statistics.mean(times), world)
+    item = np.dtype(dt).itemsize
+    h2d = (m * k + m * n + k * n) * item
+    return {"value": flops(w) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(m * n * item), "ms_per_step": ms,
+            "api": "wgblas_b200.shard.gemm_sharded_host",
+            "timing": "CUDA events on each rank's device stream around the whole call, max over ranks"}
 
 
 def cpu_baseline(w, target_s=12.0):
@@ -581,23 +733,30 @@ def cpu_baseline(w, target_s=12.0):
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the oracle's restatement of the reference's arithmetic on
+    the host cores (rank 0 only), each step a column slab of the same workload.
+    ms_per_step is the time of the slab actually computed; value is the slab's
+    FLOPs over that time (the sample names the slab). Nothing of wgblas_b200 is
+    imported on this path."""
     if rank != 0:
         return 0
     w = WORKLOADS[pick_workload(args, world)]
-    vals = []
+    vals, secs = [], []
     cb = None
     for i in range(args.warmup + args.steps):
         cb = cpu_baseline(w, target_s=max(2.0, 60.0 / (args.warmup + args.steps)))
         if i >= args.warmup:
             vals.append(cb["value"])
+            secs.append(cb["seconds"])
     value = statistics.mean(vals)
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": flops(w) / (value * 1e12) * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64 (double-double)" if w["routine"] == "dgemm" else "f32",
-            "data": "synthetic (seeded)", "impl": "reference",
-            "config": config_of(w, args.workload),
+            "warmup": args.warmup, "ms_per_step": statistics.mean(secs) * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f64 (double-double)" if w["routine"] == "dgemm" else "f32",
+            "data": "synthetic (seeded mulberry32)", "impl": "reference",
+            "config": config_of(w, args.workload, world),
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
-                             "sample": cb["sample"]},
+                             "sample": cb["sample"] + "; each step computes this slab, ms_per_step is its time"},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
     return 0
@@ -609,18 +768,16 @@ def pick_workload(args, world):
     return args.workload
 
 
-def panel_plan(w, world):
+def panel_plan(wg, w, world):
     """The broadcast panel widths a sharded call uses (its planned widths on the
     3xTF32 path; a dgemm product is one panel)."""
     if w["routine"] == "dgemm" or PANEL_COLS:
         return [w["n"]] if not PANEL_COLS else f"{PANEL_COLS} wide"
     import ctypes as ct
 
-    sys.path.insert(0, ROOT)
-    from wgblas_b200 import _native as nat
-
     import torch
 
+    nat = wg._native
     sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
     m_local = -(-w["m"] // world)
     widths = (ct.c_int64 * 4096)()
@@ -642,10 +799,11 @@ def shape_of(w):
 
 
 def config_of(w, name, world=1):
+    """The workload's description; identical on both arms (it reads nothing of the library)."""
     shard = ""
     if w.get("sharded"):
-        shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 in column panels "
-                 f"{panel_plan(w, world)} (copy-engine chain over NVLink)")
+        shard = (f", C row-block sharded over {world} GPU(s), B broadcast from rank 0 over NVLink in "
+                 "column panels")
     label = f"configs[{w['config_index']}]" if w.get("config_index") is not None else name
     return {"workload": f"{label} {w['routine']} {w['m']}x{w['n']}x{w['k']} "
                         f"{'T' if w['transA'] else 'N'}{'T' if w['transB'] else 'N'} column-major{shard}",
@@ -653,7 +811,10 @@ def config_of(w, name, world=1):
             "m": w["m"], "n": w["n"], "k": w["k"], "lda": w["lda"], "ldb": w["ldb"], "ldc": w["ldc"],
             "alpha": w["alpha"], "beta": w["beta"], "inputs": "N(0,1) seeded" if w["data"] == "normal" else "U[-1,1] seeded",
             "l2": "flushed between steps (512 MB device write outside the step events)",
-            "routine": routine_of(w), "shape": shape_of(w)}
+            "routine": routine_of(w), "shape": shape_of(w),
+            "scaling_note": ("N=1 times configs[1] (4096^3 sgemm); N>1 times configs[4] (16384^3, strong "
+                             "scaling); extra.efficiency_same_config compares each N>1 value with the same "
+                             "configuration on one GPU timed in the same run")}
 
 
 _JSON_OUT = None
@@ -664,6 +825,45 @@ def emit(line: dict) -> None:
     out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
     out.write(json.dumps(line) + "\n")
     out.flush()
+
+
+def secondary(extra, key, fn):
+    """Runs one secondary line; any failure is recorded under its key instead of
+    costing the JSON line."""
+    try:
+        extra[key] = fn()
+    except Exception as e:  # noqa: BLE001 (a secondary line must not cost the JSON line)
+        extra[key] = {"error": f"{type(e).__name__}: {e}"}
+
+
+def resident_line(wg, dev, wx, steps, flush, fp32_peak, fp64_peak):
+    msx, profx, _, _, parx = time_resident(wg, dev, wx, steps, 3, 1, flush)
+    tf = flops(wx) / (statistics.mean(msx) * 1e-3) / 1e12
+    pk = fp64_peak if wx["routine"] == "dgemm" else fp32_peak
+    line = {"tflops": tf, "ms_per_step": statistics.mean(msx), "routine": routine_of(wx), "shape": shape_of(wx),
+            f"pct_of_{'fp64' if wx['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf / pk if pk else None,
+            "kernels": {k: v[1] / max(v[0], 1) for k, v in profx.items()}}
+    if parx is not None:
+        line["parity"] = parx
+    return line
+
+
+def one_gpu_sharded_line(wg, dev, name, flush, fp32_peak, fp64_peak):
+    """configs[4] on one GPU through the same sharded path (a one-rank
+    communicator): the same-config reference point of the multi-GPU runs."""
+    from wgblas_b200.shard import Comm
+
+    ws = WORKLOADS[name]
+    c1 = Comm(dev, 1, 0, Comm.unique_id())
+    try:
+        ms1, prof1, _, _, par1 = time_sharded(wg, dev, c1, ws, 3, 3, 1, 0, flush)
+    finally:
+        c1.destroy()
+    tf1 = flops(ws) / (statistics.mean(ms1) * 1e-3) / 1e12
+    pk = fp64_peak if ws["routine"] == "dgemm" else fp32_peak
+    return {"tflops": tf1, "ms_per_step": statistics.mean(ms1), "routine": ws["routine"], "shape": shape_of(ws),
+            f"pct_of_{'fp64' if ws['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf1 / pk if pk else None,
+            "kernels": {k: v[1] / max(v[0], 1) for k, v in prof1.items()}, "parity": par1}
 
 
 def main():
@@ -694,7 +894,8 @@ def main():
 
     dev = wg.init(device=local)
     torch.cuda.set_device(local)
-    w = WORKLOADS[pick_workload(args, world)]
+    wname = pick_workload(args, world)
+    w = WORKLOADS[wname]
     flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=f"cuda:{local}")  # 512 MB
 
     phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
@@ -706,9 +907,11 @@ def main():
         comm = comm_from_torch(dev) if world > 1 else Comm(dev, 1, 0, Comm.unique_id())
     with Clocks(smi_index) as clk:
         if w.get("sharded"):
-            ms, prof, launches, wall = time_sharded(wg, dev, comm, w, args.steps, args.warmup, world, rank, flush)
+            ms, prof, launches, wall, parity = time_sharded(wg, dev, comm, w, args.steps, args.warmup, world, rank,
+                                                            flush)
         else:
-            ms, prof, launches, wall = time_resident(wg, dev, w, args.steps, args.warmup, world, flush)
+            ms, prof, launches, wall, parity = time_resident(wg, dev, w, args.steps, args.warmup, world, flush)
+            parity = parity_over_ranks(parity, world) if parity else parity
     clocks = clk.summary()
     step_ms = statistics.mean(ms)
     step_ms_max = max_over_ranks(step_ms, world)
@@ -719,6 +922,7 @@ def main():
     peaks, peak_src = measured_peaks()
     extra = {}
     fp32_peak = fp64_peak = hbm = None
+    short = max(3, args.steps // 2)
     if not args.no_extra and rank == 0:
         fp32_peak = dev.probe_peak("fp32")
         fp64_dfma = dev.probe_peak("fp64")
@@ -729,51 +933,46 @@ def main():
                            "fp64_dmma_tflops": fp64_dmma, "hbm_copy_gbs": hbm,
                            "source": "wg_probe_peak (benchmarks/roofline counterpart), this run"}
         extra["pct_of_fp32_peak"] = 100.0 * value / world / fp32_peak if w["routine"] == "sgemm" else None
-        for name in ("dgemm4096", "sgemm512", "ragged", "sgemmtr4096", "ssyrk4096", "dsyrk4096") if world == 1 else ():
-            if name == pick_workload(args, world):
-                continue
-            wx = WORKLOADS[name]
-            msx, profx, _, _ = time_resident(wg, dev, wx, max(3, args.steps // 2), 3, 1, flush)
-            tf = flops(wx) / (statistics.mean(msx) * 1e-3) / 1e12
-            pk = fp64_peak if wx["routine"] == "dgemm" else fp32_peak
-            extra[name] = {"tflops": tf, "ms_per_step": statistics.mean(msx), "routine": routine_of(wx),
-                           "shape": shape_of(wx),
-                           f"pct_of_{'fp64' if wx['routine'] == 'dgemm' else 'fp32'}_peak": 100.0 * tf / pk,
-                           "kernels": {k: v[1] / max(v[0], 1) for k, v in profx.items()}}
+        if world == 1:
+            for name in ("dgemm4096", "sgemm512", "ragged", "sgemmtr4096", "ssyrk4096", "dsyrk4096"):
+                if name != wname:
+                    secondary(extra, name, lambda n=name: resident_line(wg, dev, WORKLOADS[n], short, flush,
+                                                                        fp32_peak, fp64_peak))
 
     if not args.no_extra and world == 1 and not w.get("sharded"):
         for name in ("ssymm4096", "strmm4096"):
-            try:
-                extra[name] = time_special(wg, dev, name, max(3, args.steps // 2), 3, flush)
-            except wg.Error as e:  # a secondary line: report it, keep the headline
-                extra[name] = {"error": str(e)}
+            secondary(extra, name, lambda n=name: time_special(wg, dev, n, short, 3, flush))
         for nrhs in (64, 4096):
-            try:
-                extra[f"strsm4096_n{nrhs}"] = time_trsm(wg, dev, nrhs, max(3, args.steps // 2), 3, flush)
-            except wg.Error as e:
-                extra[f"strsm4096_n{nrhs}"] = {"error": str(e)}
-    if not args.no_extra and world == 1 and not w.get("sharded"):
-        # configs[4] on one GPU through the same sharded path (one rank): the N=1
-        # reference point for the multi-GPU scaling of the sharded workload.
-        from wgblas_b200.shard import Comm
-
-        c1 = Comm(dev, 1, 0, Comm.unique_id())
-        try:
-            ws = WORKLOADS["shard16384"]
-            ms1, prof1, _, _ = time_sharded(wg, dev, c1, ws, 3, 3, 1, 0, flush)
-            tf1 = flops(ws) / (statistics.mean(ms1) * 1e-3) / 1e12
-            extra["shard16384_1gpu"] = {"tflops": tf1, "ms_per_step": statistics.mean(ms1), "routine": "sgemm",
-                                        "shape": shape_of(ws),
-                                        "pct_of_fp32_peak": 100.0 * tf1 / fp32_peak if fp32_peak else None,
-                                        "kernels": {k: v[1] / max(v[0], 1) for k, v in prof1.items()}}
-        finally:
-            c1.destroy()
+            secondary(extra, f"strsm4096_n{nrhs}", lambda r=nrhs: time_trsm(wg, dev, r, short, 3, flush))
+        # configs[4] on one GPU, sgemm and dgemm: the same-config reference points of the scaling runs.
+        for name in ("shard16384", "shard16384d"):
+            secondary(extra, f"{name}_1gpu", lambda n=name: one_gpu_sharded_line(wg, dev, n, flush, fp32_peak,
+                                                                                 fp64_peak))
     if world > 1 and not args.no_extra and w["routine"] == "sgemm":
-        # configs[4] for dgemm on the same ranks
+        # configs[4] for dgemm on the same ranks, with its parity
         wd = WORKLOADS["shard16384d"]
-        msd, _, _, _ = time_sharded(wg, dev, comm, wd, 3, 2, world, rank, flush)
+        msd, _, _, _, pard = time_sharded(wg, dev, comm, wd, 3, 3, world, rank, flush)
         md = max_over_ranks(statistics.mean(msd), world)
-        extra["shard16384d"] = {"tflops": flops(wd) / (md * 1e-3) / 1e12, "ms_per_step": md}
+        extra["shard16384d"] = {"tflops": flops(wd) / (md * 1e-3) / 1e12, "ms_per_step": md, "parity": pard}
+    if world > 1 and not args.no_extra and w.get("sharded"):
+        # The same configuration on one GPU (rank 0, a one-rank communicator) in this
+        # run, so that the scaling efficiency compares one workload with itself.
+        one = {}
+        if rank == 0:
+            for name in (wname, "shard16384d") if w["routine"] == "sgemm" else (wname,):
+                secondary(one, name, lambda n=name: one_gpu_sharded_line(wg, dev, n, flush, fp32_peak, fp64_peak))
+        barrier(world)
+        if rank == 0:
+            eff = {}
+            t1 = one.get(wname, {}).get("tflops")
+            if t1:
+                eff[wname] = value / (world * t1)
+            td = one.get("shard16384d", {}).get("tflops")
+            if td and "shard16384d" in extra:
+                eff["shard16384d"] = extra["shard16384d"]["tflops"] / (world * td)
+            extra["one_gpu_same_config"] = one
+            extra["efficiency_same_config"] = eff
+            extra["panels"] = secondary_value(lambda: panel_plan(wg, w, world))
 
     # Roofline of the dominant kernel, from the per-kernel events of the timed region.
     # Sharded: this rank's share of the product runs as several panel launches per
@@ -805,7 +1004,7 @@ def main():
         roof = {"bound": "fp64-simt" if w["routine"] == "dgemm" else "fp32-simt", "achieved": achieved,
                 "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None, "traffic": None,
                 "peak_basis": "FMA-chain probe measured in this run (no FP32/FP64 SIMT figure in MEASURED_PEAKS.json)"}
-    traffic = NCU_TRAFFIC.get((pick_workload(args, world), dom[0]))
+    traffic = NCU_TRAFFIC.get((wname, dom[0]))
     if traffic:
         roof["traffic"] = traffic[0] + traffic[1]
         roof["traffic_unit"] = "bytes per launch (DRAM read + write)"
@@ -815,7 +1014,12 @@ def main():
     roof["launches_per_step"] = dom[1][0] / args.steps
     roof["kernels"] = {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in prof.items()}
 
-    e2e = time_e2e(wg, dev, w, max(3, args.steps // 2), args.warmup) if (rank == 0 and not w.get("sharded")) else None
+    if w.get("sharded") and world > 1:
+        e2e = time_e2e_sharded(wg, dev, comm, w, short, args.warmup, world, rank)
+    elif rank == 0 and not w.get("sharded"):
+        e2e = time_e2e(wg, dev, w, short, args.warmup)
+    else:
+        e2e = None
     cb = None if (args.no_cpu_baseline or rank != 0 or world > 1) else cpu_baseline(w)
     if not args.no_extra and world == 1 and not w.get("sharded"):
         # Level-2 lines and the other bandwidth patterns, after every figure the
@@ -826,30 +1030,26 @@ def main():
             except Exception as e:  # noqa: BLE001 (a secondary line must not cost the JSON line)
                 extra["probes"][f"{kind}_error"] = str(e)
         for dt in ("f32", "f64"):
-            key = f"cublas_{'d' if dt == 'f64' else 's'}gemm4096"
-            try:
-                extra[key] = time_cublas(dt, max(3, args.steps // 2), 3, flush, local)
-            except Exception as e:  # noqa: BLE001
-                extra[key] = {"error": str(e)}
+            secondary(extra, f"cublas_{'d' if dt == 'f64' else 's'}gemm4096",
+                      lambda d=dt: time_cublas(d, short, 3, flush, local))
         for routine in ("sgemv", "dgemv"):
             for trans in ("no-transpose", "transpose"):
                 key = f"{routine}4096_{'N' if trans == 'no-transpose' else 'T'}"
-                try:
-                    extra[key] = time_gemv(wg, dev, routine, trans, max(3, args.steps // 2), 3, flush)
-                    if hbm:
-                        extra[key]["pct_of_hbm_copy"] = 100.0 * extra[key]["gbs"] / hbm
-                except Exception as e:  # noqa: BLE001 (a secondary line must not cost the JSON line)
-                    extra[key] = {"error": str(e)}
+                secondary(extra, key, lambda r=routine, t=trans: time_gemv(wg, dev, r, t, short, 3, flush))
+                if hbm and "gbs" in extra[key]:
+                    extra[key]["pct_of_hbm_copy"] = 100.0 * extra[key]["gbs"] / hbm
     barrier(world)
     if rank == 0:
+        config = config_of(w, args.workload, world)
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": step_ms_max, "higher_is_better": True,
-                "scaling": "strong" if w.get("sharded") else "weak",
+                "scaling": "strong",
                 "vs_baseline": None, "dtype": "f64" if w["routine"] == "dgemm" else "f32",
-                "data": "synthetic (seeded mulberry32)", "config": config_of(w, args.workload, world),
-                "roofline": roof, "cpu_baseline": cb, "e2e": e2e,
+                "data": "synthetic (seeded mulberry32)", "config": config,
+                "roofline": roof, "cpu_baseline": cb, "e2e": e2e, "parity": parity,
                 "gpu_launches": launches_total,
-                "clocks": clocks, "wall_s_timed_region": wall, "extra": extra}
+                "clocks": clocks, "wall_s_timed_region": wall, "extra": extra,
+                "summary": summary_of(value, parity, extra)}
         emit(line)
     if comm is not None:
         comm.destroy()
@@ -858,6 +1058,27 @@ def main():
 
         dist.destroy_process_group()
     return 0
+
+
+def secondary_value(fn):
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
+def summary_of(value, parity, extra):
+    """Compact figures of the line, last in it so that a truncated tail still holds them."""
+    out = {"value_tflops": round(value, 2), "parity_ok": None if parity is None else parity.get("ok")}
+    for key in ("dgemm4096", "sgemm512", "ragged", "shard16384_1gpu", "shard16384d_1gpu", "shard16384d"):
+        x = extra.get(key)
+        if isinstance(x, dict) and "tflops" in x:
+            out[f"{key}_tflops"] = round(x["tflops"], 3)
+            if isinstance(x.get("parity"), dict):
+                out[f"{key}_parity_ok"] = x["parity"].get("ok")
+    if "efficiency_same_config" in extra:
+        out["efficiency_same_config"] = {k: round(v, 4) for k, v in extra["efficiency_same_config"].items()}
+    return out
 
 
 if __name__ == "__main__":

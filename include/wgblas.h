@@ -236,9 +236,11 @@ wg_status wg_dgemm_dev(wg_device *dev, int transA, int transB, int64_t m, int64_
  * on this handle's device, ordered on its stream. It needs k >= 8 (alpha == 0 or
  * k == 0 only scale C) and rejects, with WG_ERR_INVALID_ARGUMENT, shapes whose
  * scratch 2*(round_up(m,128) + round_up(n,256))*round_up(k,32)*4 bytes exceeds
- * the array. The first call on a device looks up the array's address and should
- * come before any stream capture. All calls on a device share the array: calls
- * that overlap on the GPU race, so order them on one stream. */
+ * the array. The array is reserved on a GPU when a handle to it is opened
+ * (wg_device_open looks up its address, so CUDA's lazy module loading cannot
+ * defer the reservation to the first call): open the handle before your own
+ * allocator takes the device's memory. All calls on a device share the array:
+ * calls that overlap on the GPU race, so order them on one stream. */
 #define WG_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
 wg_status wg_sgemm_noalloc(wg_device *dev, int transA, int transB, int64_t m, int64_t n, int64_t k,
                            float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,

@@ -83,3 +83,43 @@ def test_no_alloc_rejects_oversized_problems(wg, device):
                             4096, 0.0, ct.c_void_p(16), 4096)
     assert st == wg._native.WG_ERR_INVALID_ARGUMENT
     assert b"scratch" in L.wg_last_error()
+
+
+def test_no_alloc_calls_take_no_device_memory(wg, device):
+    """The property the entry point exists for: after a handle is open, its calls
+    reserve no device memory. A fresh handle (empty grow-only workspace) runs a
+    shape whose allocating plan would split tiles along k (so falling back to
+    the workspace path would show), and the GPU's free memory is unchanged
+    across further calls."""
+    import torch
+
+    L = wg._native.lib
+    dev = wg.init(powerPreference="high-performance", benchmark=False, device=device.ordinal)
+    assert dev is not device
+    plan = wg._native.TcPlan()
+    wg._native.check(L.wg_sgemm_tc_plan(dev.props()["sm_count"], 1024, 1024, 2048, ct.byref(plan)))
+    assert plan.split_segments > 1, "pick a shape whose allocating plan splits tiles"
+    m = n = 1024
+    k = 2048
+    A = wg.randomFloat32Array(m * k, -1, 1, 31)
+    B = wg.randomFloat32Array(k * n, -1, 1, 32)
+    bufs = []
+    try:
+        a, pa = _dev_array(wg, dev, A)
+        b, pb = _dev_array(wg, dev, B)
+        c, pc = _dev_array(wg, dev, np.zeros(m * n, np.float32))
+        bufs = [a, b, c]
+        torch.cuda.mem_get_info(dev.ordinal)  # torch's own context first
+        wg._native.check(L.wg_sgemm_noalloc(dev.handle, 0, 0, m, n, k, 1.0, pa, m, pb, k, 0.0, pc, m))
+        dev.synchronize()
+        free0, _ = torch.cuda.mem_get_info(dev.ordinal)
+        for _ in range(2):
+            wg._native.check(L.wg_sgemm_noalloc(dev.handle, 0, 0, m, n, k, 1.0, pa, m, pb, k, 0.5, pc, m))
+        dev.synchronize()
+        dev.check()
+        free1, _ = torch.cuda.mem_get_info(dev.ordinal)
+        assert free1 == free0, f"device memory changed by {free0 - free1} bytes"
+    finally:
+        for buf in bufs:
+            L.wg_buffer_free(buf)
+        wg.cleanup(dev)

@@ -135,15 +135,21 @@ class GpuMatrix:
             raise
         return GpuMatrix(buf, rows, cols, lda, None, layout, device, data.dtype)
 
-    def read(self) -> np.ndarray:
+    def read(self, out: np.ndarray | None = None) -> np.ndarray:
         """The matrix as a dense 1-D array in its own layout, lda padding stripped
-        (src/classes/GpuMatrix.mjs:142-202)."""
+        (src/classes/GpuMatrix.mjs:142-202). ``out`` (an addition) receives the
+        values instead of a new array, e.g. a page-locked one from
+        ``pinned_empty`` for a full-rate copy."""
         self._require_live()
         is_row = self.layout != "column-major"
         outer = self.rows if is_row else self.cols
         inner = self.cols if is_row else self.rows
         item = np.dtype(self.dtype).itemsize
-        out = np.empty(outer * inner, self.dtype)
+        if out is None:
+            out = np.empty(outer * inner, self.dtype)
+        elif (out.dtype != np.dtype(self.dtype) or out.size != outer * inner or out.ndim != 1
+              or not out.flags.c_contiguous):
+            raise Error("out must be a contiguous 1-D array of the matrix's dtype and rows*cols elements.")
         nat.check(nat.lib.wg_buffer_download_2d(self._buf, 0, self.lda * item,
                                                 out.ctypes.data_as(ct.c_void_p), inner * item,
                                                 inner * item, outer))

@@ -228,6 +228,9 @@ size_t wg_tf32x3_workspace_bytes_sk(const wg_device *dev, int64_t m, int64_t n, 
 double wg_tf32x3_cost(int G, int64_t m, int64_t n, int64_t k);
 // True when the 3xTF32 path supports this shape on this device.
 bool wg_tf32x3_supported(const wg_device *dev, int64_t m, int64_t n, int64_t k);
+// Looks up (and so reserves) wg_sgemm_noalloc's fixed scratch on a device; called
+// when a handle is opened. A failure is left for the first wg_sgemm_noalloc call.
+void wg_noalloc_reserve(int ordinal);
 // Splits op(A), op(B) into tf32 hi/lo operands in `ws`, then runs the tcgen05 kernel.
 // Operands outside the split's exact range make the kernel exit and the FFMA
 // kernel (launched right after, gated on the same epoch) compute C instead.

@@ -85,6 +85,7 @@ extern "C" wg_status wg_device_open(int ordinal, unsigned flags, wg_device **out
   d->stream = d->own_stream;
   d->sgemm_path = WG_SGEMM_AUTO;
   d->dgemm_path = WG_DGEMM_AUTO;
+  wg_noalloc_reserve(ordinal);  // wg_sgemm_noalloc's fixed scratch is reserved now, not at its first call
   *out = d;
   return WG_OK;
 }

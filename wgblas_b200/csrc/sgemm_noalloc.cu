@@ -10,11 +10,17 @@
 // device pointers.
 //
 // The array (g_noalloc_scratch, WG_NOALLOC_SCRATCH_BYTES = 64 MiB) is a
-// file-scope __device__ variable: every GPU that loads the library holds it
-// until the process exits. Host code cannot use its name as a device address,
-// so the first call on each device looks the address up with
-// cudaGetSymbolAddress while that device is current, and caches it. That
-// first call should therefore come before any stream capture.
+// file-scope __device__ variable. Under CUDA's lazy module loading (the
+// default since CUDA 12.2) the runtime reserves it on a GPU only when the code
+// object holding it is first used there, which would make the first call the
+// one that allocates. So wg_device_open looks the array's address up
+// (cudaGetSymbolAddress, with the device current) and caches it per device:
+// the array is reserved when the handle is opened and stays reserved until
+// the process exits. Open the handle before the application's own allocator
+// takes the device's memory. Host code cannot use the array's name as a
+// device address; every call passes the cached address to the kernels. If
+// the lookup failed at open, the first call retries it (and then should come
+// before any stream capture).
 //
 // Every call on a device shares the one array, and the array keeps the last
 // call's contents. Each call rewrites every element it reads (the pack pass
@@ -22,6 +28,7 @@
 // clearing. Calls whose work overlaps on the GPU — on different streams or
 // device handles of the same GPU — race on the array: order them on one
 // stream.
+#include <cstdio>
 #include <mutex>
 
 #include "internal.h"
@@ -53,6 +60,13 @@ wg_status scratch_address(int ordinal, void **out) {
 }
 
 }  // namespace
+
+void wg_noalloc_reserve(int ordinal) {
+  char saved[1024];
+  snprintf(saved, sizeof saved, "%s", wg_last_error());
+  void *p = nullptr;
+  if (scratch_address(ordinal, &p) != WG_OK) wg_fail(WG_OK, "%s", saved);  // retried by the first call
+}
 
 extern "C" wg_status wg_sgemm_noalloc(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                                       float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,

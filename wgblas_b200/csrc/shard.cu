@@ -26,6 +26,7 @@
 // surfaces as an error instead of a hang.
 #include <cuda.h>
 #include <dlfcn.h>
+#include <cstdlib>
 #include <nccl.h>
 
 #include <algorithm>
@@ -62,8 +63,15 @@ NcclApi *nccl() {
   static NcclApi api;
   static std::once_flag once;
   std::call_once(once, [] {
-    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    // WGBLAS_NCCL_LIBRARY names a specific NCCL (the Python layer points it at the
+    // copy bundled with torch, so that a later `import torch` binds to the same
+    // library instead of failing on an older system NCCL that took its soname).
+    // Local symbol scope: nothing of NCCL is exported to libraries loaded later.
+    void *h = nullptr;
+    const char *path = getenv("WGBLAS_NCCL_LIBRARY");
+    if (path && *path) h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
     if (!h) return;
 #define LOAD(field, sym) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, sym))
     LOAD(GetUniqueId, "ncclGetUniqueId");

@@ -15,6 +15,7 @@ pure Python/numpy and is what the CPU multi-process tests check.
 from __future__ import annotations
 
 import ctypes as ct
+import os
 
 import numpy as np
 
@@ -66,10 +67,31 @@ def place_rows(C_full: np.ndarray, ldc: int, block: np.ndarray, ld_block: int, r
         C_full[r0 + j * ldc: r1 + j * ldc] = block[j * ld_block: j * ld_block + mr]
 
 
+def _prefer_bundled_nccl() -> None:
+    """Points the library's NCCL loader at the NCCL that ships with torch's CUDA
+    wheels when present (WGBLAS_NCCL_LIBRARY, unless already set). Two NCCLs in
+    one process share the soname libnccl.so.2: whichever loads first serves both
+    this library and torch, and torch's CUDA library needs its own (newer) one."""
+    if os.environ.get("WGBLAS_NCCL_LIBRARY"):
+        return
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        cand = os.path.join(base, "lib", "libnccl.so.2")
+        if os.path.exists(cand):
+            os.environ["WGBLAS_NCCL_LIBRARY"] = cand
+            return
+
+
 class Comm:
     """A communicator joining one device handle to the other ranks' (wg_comm)."""
 
     def __init__(self, device: Device, nranks: int, rank: int, unique_id: bytes, timeout_ms: int = 60000):
+        _prefer_bundled_nccl()
         self.device = device
         self.nranks = nranks
         self.rank = rank
@@ -80,6 +102,7 @@ class Comm:
 
     @staticmethod
     def unique_id() -> bytes:
+        _prefer_bundled_nccl()
         buf = ct.create_string_buffer(128)
         nat.check(nat.lib.wg_comm_unique_id(buf, 128))
         return buf.raw
@@ -136,6 +159,48 @@ def gemm_sharded(comm: Comm, transA: bool, transB: bool, m_local: int, n: int, k
     nat.check(fn(comm.handle, int(bool(transA)), int(bool(transB)), m_local, n, k, al,
                  _ptr(A_local) if m_local else None, A_local.lda, _ptr(B) if B is not None else None, ldb, root, be,
                  _ptr(C_local) if m_local else None, C_local.lda, panel_cols))
+
+
+def gemm_sharded_host(comm: Comm, transA: bool, transB: bool, m_local: int, n: int, k: int, alpha,
+                      A_local: np.ndarray, B: np.ndarray | None, ldb: int, beta, C_local: np.ndarray,
+                      row_offsets: list[int], root: int = 0, panel_cols: int = 0,
+                      out: np.ndarray | None = None) -> np.ndarray | None:
+    """The sharded GEMM on host arrays, the typed-array counterpart of
+    ``gemm_sharded`` (as the reference's sgemm takes typed arrays and returns a
+    new C, src/sgemm/sgemm.mjs:151-262): every rank uploads its row block of
+    op(A) (dense column-major, ``row_block``'s layout: m_local x k, or k x m_local
+    with transA) and of C (m_local x n, ld m_local); the root uploads B (its
+    stored matrix, leading dimension ldb; other ranks pass None). The product
+    runs sharded, the row blocks are gathered on the root, and the root returns
+    the full column-major C (m x n, ld m; into ``out`` when given, e.g. a
+    page-locked array); other ranks return None. Device buffers live for the
+    call only. Collective: every rank must call it."""
+    dev = comm.device
+    dt = np.dtype(C_local.dtype)
+    m = row_offsets[-1]
+    a_rows, a_cols = (k, m_local) if transA else (m_local, k)
+    b_rows, b_cols = (n, k) if transB else (k, n)
+    made = []
+    try:
+        GA = GpuMatrix.from_(dev, A_local, a_rows, a_cols, a_rows, "column-major") if m_local else None
+        made.append(GA)
+        GC = GpuMatrix.from_(dev, C_local, m_local, n, m_local, "column-major") if m_local else None
+        made.append(GC)
+        GB = GpuMatrix.from_(dev, B, b_rows, b_cols, ldb, "column-major") if comm.rank == root else None
+        made.append(GB)
+        GF = GpuMatrix.empty(dev, m, n, m, "column-major", dt) if comm.rank == root else None
+        made.append(GF)
+        gemm_sharded(comm, transA, transB, m_local, n, k, alpha, GA, GB, beta, GC, root=root,
+                     panel_cols=panel_cols, ldb=ldb)
+        gather_rows(comm, GC, m_local, n, row_offsets, root=root, C_full=GF)
+        dev.synchronize()
+        comm.wait()
+        dev.check()
+        return GF.read(out) if GF is not None else None
+    finally:
+        for g in made:
+            if g is not None:
+                g.destroy()
 
 
 def gather_rows(comm: Comm, C_local: GpuMatrix, m_local: int, n: int, row_offsets: list[int], root: int = 0,
