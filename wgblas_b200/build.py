@@ -33,7 +33,7 @@ def _stale(target: str, deps) -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD_DIR, exist_ok=True)
     headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "wgblas.h")]
-    objs = []
+    objs, jobs = [], []
     for src in SOURCES:
         path = os.path.join(CSRC, src)
         obj = os.path.join(BUILD_DIR, src.replace(".cu", ".o"))
@@ -42,7 +42,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
             cmd = [NVCC, *ARCH, *FLAGS, "-c", path, "-o", obj]
             if verbose:
                 cmd.insert(1, "-Xptxas=-v")
-            subprocess.run(cmd, check=True)
+            jobs.append(cmd)
+    # The translation units compile independently: run them side by side.
+    procs = [subprocess.Popen(cmd) for cmd in jobs]
+    failed = [cmd for cmd, proc in zip(jobs, procs) if proc.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     if force or _stale(LIB, objs):
         subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-ldl"], check=True)
     return LIB

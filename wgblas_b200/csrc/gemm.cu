@@ -126,11 +126,7 @@ wg_status gemm_launch<double>(wg_device *d, int transA, int transB, int64_t m, i
   // the DFMA kernel, whose sequential FMA chains match the CPU restatement bit for bit.
   const bool dmma = d->dgemm_path == WG_DGEMM_DMMA ||
                     (d->dgemm_path == WG_DGEMM_AUTO && k >= 16 && (double)m * (double)n >= 128.0 * 128.0);
-  if (dmma) {
-    wg_launch_scope scope(d, "dgemm_dmma");
-    WG_CUDA(wg_launch_dgemm_dmma(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo));
-    return WG_OK;
-  }
+  if (dmma) return wg_dgemm_dmma(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
   wg_launch_scope scope(d, "dgemm_simt");
   WG_CUDA(wg_launch_gemm_simt<double>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C,
                                       ldc, d->dwords, nullptr, uplo));

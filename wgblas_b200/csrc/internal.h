@@ -209,10 +209,21 @@ cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t 
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
                                 const wg_gate *gate, int uplo = 0);
 
-// dgemm on the FP64 tensor-core (DMMA) path, mma.sync.m16n8k8.f64 (dgemm_dmma.cu).
-cudaError_t wg_launch_dgemm_dmma(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
-                                 double alpha, const double *A, int64_t lda, const double *B, int64_t ldb,
-                                 double beta, double *C, int64_t ldc, int uplo = 0);
+// dgemm on the FP64 tensor-core (DMMA) path (dgemm_dmma.cu), on d->stream: the
+// TMA-fed pipelined kernel when the operands' layout allows its tensor maps,
+// the register-staged kernel otherwise.
+wg_status wg_dgemm_dmma(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, double alpha,
+                        const double *A, int64_t lda, const double *B, int64_t ldb, double beta, double *C,
+                        int64_t ldc, int uplo = 0);
+
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point (no
+// link-time dependency on libcuda); NULL when the driver does not provide it.
+#include <cuda.h>
+typedef CUresult (*wg_encode_tiled_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                       const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                       CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                       CUtensorMapFloatOOBfill);
+wg_encode_tiled_fn wg_encode_tiled();
 
 // C = (alpha == 0 ? 0 : alpha*0) + beta*C elementwise — the k == 0 / alpha == 0 cases.
 template <typename T>

@@ -42,6 +42,8 @@
 //  after it, gated on the same words, computes C instead.
 #include <cuda.h>
 
+#include <mutex>
+
 #include "internal.h"
 #include "tcgen05.cuh"
 
@@ -533,25 +535,11 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
 // ---- host side ------------------------------------------------------------
 // ---- host side ------------------------------------------------------------
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
+wg_encode_tiled_fn encode_fn() { return wg_encode_tiled(); }
 
 // Tensor map of a rows x kp row-major fp32 operand, boxes of box_rows x BK.
 bool make_map(CUtensorMap *map, float *ptr, int64_t rows, int64_t kp, int box_rows) {
-  EncodeTiledFn fn = encode_fn();
+  wg_encode_tiled_fn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kp * sizeof(float)};
@@ -771,6 +759,19 @@ extern "C" wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_
 uint32_t wg_next_epoch(wg_device *d) {
   if (++d->epoch == 0) d->epoch = 1;
   return d->epoch;
+}
+
+wg_encode_tiled_fn wg_encode_tiled() {
+  static wg_encode_tiled_fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<wg_encode_tiled_fn>(p);
+  });
+  return fn;
 }
 
 wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
