@@ -1,8 +1,11 @@
-"""Panelled 3xTF32 products on the GPU: op(A) split once, each op(B) panel split
-on a side stream while the previous panel's MMA runs. They back the
-typed-array sgemm above 2 GFLOP and the sharded sgemm. Covers parity with the
-oracle, and the per-panel device fallback: a non-finite value in one op(B)
-panel sends only that panel to the FFMA kernel, one in op(A) sends them all."""
+"""Panelled 3xTF32 products on the GPU. They back the typed-array sgemm above
+2 GFLOP and the sharded sgemm. Two forms: with the fused kernel (each panel one
+launch that splits its own operands) a value outside the split's range sends
+only the 128 x BN tiles it touches to the FFMA kernel; with the split pass
+(op(A) split once, each op(B) panel split on a side stream while the previous
+panel's MMA runs; forced by 'tf32x3_packed', and taken for operands the fused
+kernel's tensor maps cannot describe) one bad op(B) value sends its panel, one
+bad op(A) value sends every panel. Both are checked against the oracle."""
 from __future__ import annotations
 
 import numpy as np
@@ -22,6 +25,20 @@ def host_panels(m, n, k):
     p = -(-n // 4)
     p = -(-p // 256) * 256
     return min(p, n)
+
+
+@pytest.fixture
+def packed(device):
+    device.set_sgemm_path("tf32x3_packed")
+    yield device
+    device.set_sgemm_path("auto")
+
+
+@pytest.fixture
+def fused256(device):
+    device.set_sgemm_path("tf32x3_fused_bn256")
+    yield device
+    device.set_sgemm_path("auto")
 
 
 def _inputs(wg, m, n, k, seed):
@@ -46,7 +63,7 @@ def test_host_array_panels_match_oracle(wg, device, oracle, shape):
     check_sgemm(oracle, got, N, N, m, n, k, 0.75, A, m, B, k, -0.5, C, m, "column-major")
 
 
-def test_bad_b_panel_falls_back_alone(wg, device, oracle):
+def test_bad_b_panel_falls_back_alone(wg, device, oracle, packed):
     m, n, k = 1024, 2048, 1024
     panel = host_panels(m, n, k)
     A, B, C = _inputs(wg, m, n, k, 50)
@@ -66,7 +83,7 @@ def test_bad_b_panel_falls_back_alone(wg, device, oracle):
                     "column-major")
 
 
-def test_bad_a_sends_every_panel_back(wg, device, oracle):
+def test_bad_a_sends_every_panel_back(wg, device, oracle, packed):
     m, n, k = 1024, 1536, 1024
     panels = -(-n // host_panels(m, n, k))
     A, B, C = _inputs(wg, m, n, k, 60)
@@ -78,9 +95,9 @@ def test_bad_a_sends_every_panel_back(wg, device, oracle):
     assert bits_equal(got, want)
 
 
-def test_clean_call_after_flagged_panels(wg, device, oracle):
+def test_clean_call_after_flagged_panels(wg, device, oracle, packed):
     """Flags of one product do not leak into the next."""
-    test_bad_b_panel_falls_back_alone(wg, device, oracle)
+    test_bad_b_panel_falls_back_alone(wg, device, oracle, packed)
     m, n, k = 1024, 1040, 1100
     A, B, C = _inputs(wg, m, n, k, 70)
     before = device.sgemm_stats()
@@ -89,8 +106,12 @@ def test_clean_call_after_flagged_panels(wg, device, oracle):
     check_sgemm(oracle, got, N, N, m, n, k, 1.0, A, m, B, k, 0.5, C, m, "column-major")
 
 
-def test_sharded_single_rank_panels_with_bad_panel(wg, device, oracle):
-    """The sharded sgemm on one rank with explicit panels: the same product path."""
+@pytest.mark.parametrize("kind", ["tf32x3_packed", "tf32x3_fused_bn256"])
+def test_sharded_single_rank_panels_with_bad_panel(wg, device, oracle, kind):
+    """The sharded sgemm on one rank with explicit 256-column panels: the same
+    product path. With either kernel the bad value's 256 columns (its panel, or
+    its 128 x 256 tiles in every row block) fall back."""
+    device.set_sgemm_path(kind)
     from wgblas_b200.shard import Comm, gemm_sharded
 
     m, n, k = 640, 1280, 512
@@ -107,6 +128,7 @@ def test_sharded_single_rank_panels_with_bad_panel(wg, device, oracle):
         got = GC.read()
         after = device.sgemm_stats()
     finally:
+        device.set_sgemm_path("auto")
         comm.destroy()
         for g in (GA, GB, GC):
             g.destroy()
@@ -118,3 +140,45 @@ def test_sharded_single_rank_panels_with_bad_panel(wg, device, oracle):
         sub = slice(j0 * m, j1 * m)
         check_sgemm(oracle, got[sub], N, N, m, j1 - j0, k, 1.0, A, m, B[j0 * k:], k, -1.0, C[sub], m,
                     "column-major")
+
+
+def test_fused_bad_b_tiles_fall_back_alone(wg, device, oracle, fused256):
+    """Fused panels: one Inf in op(B) sends the 128 x 256 tiles of its column block
+    (every row block of one panel's tile column) to the FFMA kernel, bit for bit
+    the FMA restatement there; every other column stays on the tensor cores."""
+    m, n, k = 1024, 2048, 1024
+    panel = host_panels(m, n, k)
+    A, B, C = _inputs(wg, m, n, k, 50)
+    j_bad = panel + 17
+    B[3 + j_bad * k] = np.inf
+    t0 = (j_bad - panel) // 256 * 256 + panel  # first column of its tile
+    before = device.sgemm_stats()
+    got = wg.sgemm(device, N, N, m, n, k, 1.0, A, m, B, k, 1.0, C, m, "column-major")["C"]
+    assert device.sgemm_stats()["fallbacks"] == before["fallbacks"] + 1
+    want = oracle.sgemm(0, 0, m, n, k, 1.0, A, m, B, k, 1.0, C, m, variant=1)
+    assert bits_equal(got[t0 * m:(t0 + 256) * m], want[t0 * m:(t0 + 256) * m])
+    for j0, j1 in ((0, t0), (t0 + 256, n)):
+        sub = slice(j0 * m, j1 * m)
+        check_sgemm(oracle, got[sub], N, N, m, j1 - j0, k, 1.0, A, m, B[j0 * k:], k, 1.0, C[sub], m,
+                    "column-major")
+
+
+def test_fused_bad_a_row_block_in_every_panel(wg, device, oracle, fused256):
+    """Fused panels: one NaN in op(A) row 7 sends tile row 0 of every panel to the
+    FFMA kernel; the other row blocks stay on the tensor cores."""
+    m, n, k = 1024, 1536, 1024
+    panels = -(-n // host_panels(m, n, k))
+    A, B, C = _inputs(wg, m, n, k, 60)
+    A[7 + 100 * m] = np.nan
+    before = device.sgemm_stats()
+    got = wg.sgemm(device, N, N, m, n, k, 1.25, A, m, B, k, 0.0, C, m, "column-major")["C"]
+    assert device.sgemm_stats()["fallbacks"] == before["fallbacks"] + panels
+    want = oracle.sgemm(0, 0, m, n, k, 1.25, A, m, B, k, 0.0, C, m, variant=1)
+    G, W = got.reshape(n, m), want.reshape(n, m)
+    assert bits_equal(np.ascontiguousarray(G[:, :128]), np.ascontiguousarray(W[:, :128]))
+    A2 = A.copy()
+    A2[7 + 100 * m] = 0.0
+    truth, absab = oracle.sgemm_truth(0, 0, m, n, k, 1.25, A2, m, B, k, 0.0, C, m)
+    bound = oracle.sgemm_bound(m, n, k, 1.25, absab, 0.0, C, m)[128:]
+    err = np.abs(oracle.block(got, m, n, m).astype(np.float64) - oracle.dense(truth, m, n))[128:]
+    assert np.all(err <= bound)

@@ -20,6 +20,15 @@ def tc(device):
     device.set_sgemm_path("auto")
 
 
+@pytest.fixture
+def packed(device):
+    """The split pass + MMA kernel, whose fallback covers the whole call (the fused
+    kernel's per-tile fallback is tested in test_sgemm_fused_gpu.py)."""
+    device.set_sgemm_path("tf32x3_packed")
+    yield device
+    device.set_sgemm_path("auto")
+
+
 def _run(wg, dev, ta, tb, m, n, k, alpha, beta, layout="column-major", seed=7, low=-1.0, high=1.0, pad=(0, 0, 0)):
     cm = layout == "column-major"
     aR, aC = (m, k) if ta == N else (k, m)
@@ -65,7 +74,7 @@ def test_tc_same_sign_worst_case(wg, device, oracle, tc):
 
 
 @pytest.mark.parametrize("bad", [np.inf, -np.inf, np.nan, 1e-20, 3e20])
-def test_tc_device_fallback(wg, device, oracle, tc, bad):
+def test_tc_device_fallback(wg, device, oracle, packed, bad):
     """Operands the split cannot carry exactly make the pack pass flag the call on the
     device; the tensor-core kernel then exits and the FFMA kernel computes C."""
     m = n = k = 256
@@ -82,9 +91,9 @@ def test_tc_device_fallback(wg, device, oracle, tc, bad):
         ieee_match(got, want, 0)
 
 
-def test_tc_no_stale_fallback(wg, device, oracle, tc):
+def test_tc_no_stale_fallback(wg, device, oracle, packed):
     """A flagged call does not send the next (clean) call to the fallback."""
-    test_tc_device_fallback(wg, device, oracle, tc, np.inf)
+    test_tc_device_fallback(wg, device, oracle, packed, np.inf)
     before = device.sgemm_stats()
     got, args = _run(wg, device, N, T, 256, 256, 256, 1.0, 0.0)
     assert device.sgemm_stats()["fallbacks"] == before["fallbacks"]

@@ -77,8 +77,15 @@ class Device:
         return {f: int(getattr(s, f)) for f, _ in s._fields_}
 
     def set_sgemm_path(self, path: str) -> None:
-        """'auto' (default), 'simt' (FFMA kernel) or 'tf32x3' (tensor-core kernel)."""
-        code = {"auto": nat.WG_SGEMM_AUTO, "simt": nat.WG_SGEMM_SIMT, "tf32x3": nat.WG_SGEMM_TF32X3}[path]
+        """'auto' (default), 'simt' (FFMA kernel), 'tf32x3' (tensor cores: the fused
+        kernel where the operands allow it, else split pass + MMA kernel),
+        'tf32x3_packed' (split pass + MMA kernel) or 'tf32x3_fused_bn256' / '_bn128' /
+        '_bn64' (the fused kernel with one tile width)."""
+        code = {"auto": nat.WG_SGEMM_AUTO, "simt": nat.WG_SGEMM_SIMT, "tf32x3": nat.WG_SGEMM_TF32X3,
+                "tf32x3_packed": nat.WG_SGEMM_TF32X3_PACKED,
+                "tf32x3_fused_bn256": nat.WG_SGEMM_TF32X3_FUSED_BN256,
+                "tf32x3_fused_bn128": nat.WG_SGEMM_TF32X3_FUSED_BN128,
+                "tf32x3_fused_bn64": nat.WG_SGEMM_TF32X3_FUSED_BN64}[path]
         nat.check(nat.lib.wg_device_set_sgemm_path(self.handle, code))
 
     def set_dgemm_path(self, path: str) -> None:

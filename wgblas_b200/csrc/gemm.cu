@@ -87,13 +87,32 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
   }
   d->stats.calls++;
   bool tc = false;
-  if (d->sgemm_path == WG_SGEMM_TF32X3) {
+  const int path = d->sgemm_path;
+  const bool forced_tc = path >= WG_SGEMM_TF32X3;
+  if (forced_tc) {
     if (!wg_tf32x3_supported(d, m, n, k))
       return wg_fail(WG_ERR_NOT_SUPPORTED, "the 3xTF32 kernel does not support m=%lld n=%lld k=%lld",
                      (long long)m, (long long)n, (long long)k);
     tc = true;
-  } else if (d->sgemm_path == WG_SGEMM_AUTO) {
+  } else if (path == WG_SGEMM_AUTO) {
     tc = wg_tf32x3_supported(d, m, n, k) && k >= 64 && (double)m * (double)n >= 256.0 * 256.0;
+  }
+  const bool fused = tc && path != WG_SGEMM_TF32X3_PACKED &&
+                     (path >= WG_SGEMM_TF32X3_FUSED_BN256 || (double)m * (double)n * (double)k <= WG_FUSED_MAX_WORK) &&
+                     wg_tf32x3_fused_supported(d, transA, transB, m, n, k, A, lda, B, ldb);
+  if (path >= WG_SGEMM_TF32X3_FUSED_BN256 && !fused)
+    return wg_fail(WG_ERR_NOT_SUPPORTED, "the fused 3xTF32 kernel needs 16-byte aligned A and B and lda, ldb "
+                   "multiples of 4");
+  if (fused) {
+    void *ws = nullptr;
+    const size_t bytes = wg_tf32x3_fused_workspace(d, m, n, k);
+    wg_status st = wg_workspace(d, bytes, &ws);
+    if (st != WG_OK) return st;
+    st = wg_sgemm_tf32x3_fused(d, d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws,
+                               bytes, uplo);
+    if (st != WG_OK) return st;
+    d->stats.tf32x3_launches++;
+    return WG_OK;
   }
   if (tc) {
     void *ws = nullptr;
@@ -211,13 +230,17 @@ wg_status gemm_dev(wg_device *d, int transA, int transB, int64_t m, int64_t n, i
 }
 
 // Copies the rows x cols block of a column-major host matrix (leading dimension
-// ld) into a dense device matrix.
+// ld) into a device matrix with leading dimension dst_ld (>= rows).
 template <typename T>
-cudaError_t h2d_block(T *dst, const T *src, int64_t ld, Stored s, cudaStream_t st) {
+cudaError_t h2d_block(T *dst, int64_t dst_ld, const T *src, int64_t ld, Stored s, cudaStream_t st) {
   if (s.rows == 0 || s.cols == 0) return cudaSuccess;
-  return cudaMemcpy2DAsync(dst, s.rows * sizeof(T), src, ld * sizeof(T), s.rows * sizeof(T), s.cols,
+  return cudaMemcpy2DAsync(dst, dst_ld * sizeof(T), src, ld * sizeof(T), s.rows * sizeof(T), s.cols,
                            cudaMemcpyHostToDevice, st);
 }
+
+// Leading dimension of a device copy: rows rounded up to 4 elements, so that
+// every column starts on a 16-byte boundary (the TMA-fed kernels' requirement).
+int64_t device_ld(int64_t rows) { return rows > 0 ? (rows + 3) / 4 * 4 : 4; }
 
 // Panel width of the host-array path: wide enough that each panel's GEMM is
 // efficient, narrow enough that the upload, the GEMM and the read-back of
@@ -277,10 +300,10 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   if (st != WG_OK) return st;
   cudaStream_t s = d->stream;
   const Stored sa = stored_a(transA, m, k), sb = stored_b(transB, n, k);
-  const size_t na = reads_ab ? (size_t)(sa.rows * sa.cols) : 0;
-  const size_t nb = reads_ab ? (size_t)(sb.rows * sb.cols) : 0;
+  const int64_t lda_d = device_ld(sa.rows), ldb_d = device_ld(sb.rows);
+  const size_t na = reads_ab ? (size_t)(lda_d * sa.cols) : 0;
+  const size_t nb = reads_ab ? (size_t)(ldb_d * sb.cols) : 0;
   const size_t nc = (size_t)(m * n);
-  const int64_t lda_d = sa.rows > 0 ? sa.rows : 1, ldb_d = sb.rows > 0 ? sb.rows : 1;
   const int64_t panel = reads_ab && uplo == WG_UPLO_FULL ? host_panel_cols(m, n, k) : n;
   const int64_t panels = (n + panel - 1) / panel;
   // sgemm panels on the tensor cores run as one wg_tc_product, whose op(B)
@@ -308,7 +331,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   // The copy streams start after the allocations (made on the compute stream).
   if (e == cudaSuccess) e = cudaEventRecord(pipe.ev_a, s);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(d->h2d, pipe.ev_a, 0);
-  if (e == cudaSuccess && na) e = h2d_block(dA, A, lda, sa, d->h2d);
+  if (e == cudaSuccess && na) e = h2d_block(dA, lda_d, A, lda, sa, d->h2d);
   if (e == cudaSuccess) e = cudaEventRecord(pipe.ev_a, d->h2d);
   for (int64_t j = 0; e == cudaSuccess && j < panels; j++) {
     const int64_t j0 = j * panel, cols = n - j0 < panel ? n - j0 : panel;
@@ -317,9 +340,10 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
         e = cudaMemcpy2DAsync(dB + j0, ldb_d * sizeof(T), B + j0, ldb * sizeof(T), cols * sizeof(T), k,
                               cudaMemcpyHostToDevice, d->h2d);
       else         // columns j0.. of the k x n stored B
-        e = h2d_block(dB + j0 * ldb_d, B + j0 * ldb, ldb, Stored{k, cols}, d->h2d);
+        e = h2d_block(dB + j0 * ldb_d, ldb_d, B + j0 * ldb, ldb, Stored{k, cols}, d->h2d);
     }
-    if (e == cudaSuccess && reads_c) e = h2d_block(dC + j0 * m, C_in + j0 * ldc, ldc, Stored{m, cols}, d->h2d);
+    if (e == cudaSuccess && reads_c)
+      e = h2d_block(dC + j0 * m, m, C_in + j0 * ldc, ldc, Stored{m, cols}, d->h2d);
     if (e == cudaSuccess) e = cudaEventRecord(pipe.ev_b[j], d->h2d);
   }
   const bool timing = gpu_ms && (d->flags & WG_DEVICE_TIMING);
@@ -327,7 +351,7 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   if (e == cudaSuccess && timing) e = cudaEventRecord(d->ev_start, s);
   if (e == cudaSuccess && tc)
     st = wg_tc_product_begin(&prod, d, transA, transB, m, k, (float)alpha, (const float *)dA, lda_d, (float)beta,
-                             widths, 2, pipe.ev_a);
+                             widths, 2, pipe.ev_a, (const float *)dB, ldb_d);
   for (int64_t j = 0; e == cudaSuccess && st == WG_OK && j < panels; j++) {
     const int64_t j0 = j * panel, cols = n - j0 < panel ? n - j0 : panel;
     const T *bp = dB ? (transB ? dB + j0 : dB + j0 * ldb_d) : nullptr;

@@ -66,6 +66,7 @@ struct Vec4<double> {
 };
 
 constexpr int BM = 128, BN = 128, BK = 8, TM = 8, TN = 8;
+constexpr int64_t GATED_GRID = 148;  // one wave on a B200: a closed gate costs one CTA launch per SM
 constexpr int TX = BM / TM, TY = BN / TN, NT = TX * TY;  // 16 x 16 = 256 threads
 constexpr int LPT_A = BM * BK / NT, LPT_B = BK * BN / NT;  // 4 elements each
 
@@ -82,23 +83,36 @@ template <typename T, int TA, int TB>
 __global__ void __launch_bounds__(NT, 1)
 gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__ A, int64_t lda,
                  const T *__restrict__ B, int64_t ldb, T beta, T *__restrict__ C, int64_t ldc,
-                 unsigned *dwords, wg_gate gate, int gated, int uplo) {
+                 unsigned *dwords, wg_gate gate, int gated, wg_tile_mask mask, int uplo) {
   if (gated) {
     // Device-side fallback of the 3xTF32 path: run only if its operand check failed.
     if (!wg_gate_open(gate)) return;
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicAdd(dwords + WG_DW_FALLBACKS, 1u);
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(dwords + WG_DW_FALLBACKS, 1u);
   }
-  // gemmtr: a tile with no element in the triangle writes nothing (uniform exit, before any barrier).
-  if (wg_tile_outside(uplo, (int64_t)blockIdx.x * BM, BM, (int64_t)blockIdx.y * BN, BN)) return;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T *As = reinterpret_cast<T *>(smem_raw);       // [2][BK][lda_s]
   T *Bs = As + 2 * BK * lda_s<T>();             // [2][BK][ldb_s]
 
   const int tid = threadIdx.x;
   const int tx = tid % TX, ty = tid / TX;
-  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
   const int64_t kk = (alpha == T(0)) ? 0 : k;  // alpha == 0 reads neither A nor B
   const int64_t ntiles = (kk + BK - 1) / BK;
+  const int64_t tiles_m = (m + BM - 1) / BM, tiles = tiles_m * ((n + BN - 1) / BN);
+  // Tiles in column order of C (m fastest); the grid strides over them, so a gated
+  // launch needs only a few CTAs to exit when its gate is closed.
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+  const int64_t m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+  // gemmtr: a tile with no element in the triangle writes nothing (uniform skip).
+  if (wg_tile_outside(uplo, m0, BM, n0, BN)) continue;
+  // Masked (the fallback of a fused 3xTF32 call): only columns of flagged tiles.
+  if (mask.flags) {
+    const int64_t ftm = m0 / BM, last = (n0 + BN < n ? n0 + BN : n) - 1;
+    bool any = false;
+    for (int64_t ftn = n0 / mask.bn; ftn <= last / mask.bn; ftn++)
+      any |= mask.flags[ftm + ftn * mask.tiles_m] == mask.epoch;
+    if (!any) continue;
+  }
+  __syncthreads();  // the previous tile's last reads of shared memory are done
 
   T acc[TM][TN];
 #pragma unroll
@@ -178,6 +192,7 @@ gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__
     for (int r = 0; r < 4; r++) {
       const int64_t gj = n0 + g * (BN / 2) + 4 * ty + r;
       if (gj >= n) continue;
+      if (mask.flags && mask.flags[m0 / BM + (gj / mask.bn) * mask.tiles_m] != mask.epoch) continue;
 #pragma unroll
       for (int h = 0; h < 2; h++) {
         const int64_t gi = m0 + h * (BM / 2) + 4 * tx;
@@ -201,6 +216,7 @@ gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__
         }
       }
     }
+  }
 }
 
 // C = epilogue(0) elementwise: the k == 0 and alpha == 0 cases.
@@ -220,33 +236,46 @@ __global__ void scale_kernel(int64_t m, int64_t n, T alpha, T beta, T *__restric
 template <typename T, int TA, int TB>
 cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, T alpha, const T *A,
                       int64_t lda, const T *B, int64_t ldb, T beta, T *C, int64_t ldc,
-                      unsigned *dwords, const wg_gate *gate, int uplo) {
+                      unsigned *dwords, const wg_gate *gate, const wg_tile_mask *mask, int uplo) {
   auto kern = gemm_simt_kernel<T, TA, TB>;
   // Per-device attribute: set on every launch so each device that runs the kernel has it.
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem_bytes<T>());
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
+  // One CTA per tile; a gated launch (usually a no-op) strides with at most one
+  // CTA per SM of a B200, so its closed-gate exit costs little more than the launch.
+  int64_t grid = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  if (gate && grid > GATED_GRID) grid = GATED_GRID;
   const wg_gate g = gate ? *gate : wg_gate{nullptr, nullptr, 0u, 0u};
-  kern<<<grid, NT, smem_bytes<T>(), s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, g,
-                                          gate ? 1 : 0, uplo);
+  const wg_tile_mask mk = mask ? *mask : wg_tile_mask{nullptr, 1, 1, 0u};
+  kern<<<(unsigned)grid, NT, smem_bytes<T>(), s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, g,
+                                                   gate ? 1 : 0, mk, uplo);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 template <typename T>
+cudaError_t wg_launch_gemm_simt_masked(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                       T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C,
+                                       int64_t ldc, unsigned *dwords, const wg_gate *gate, const wg_tile_mask *mask,
+                                       int uplo) {
+  if (((m + BM - 1) / BM) * ((n + BN - 1) / BN) >= ((int64_t)1 << 31)) return cudaErrorInvalidConfiguration;
+  if (transA) {
+    return transB ? launch_tt<T, 1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, mask, uplo)
+                  : launch_tt<T, 1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, mask, uplo);
+  }
+  return transB ? launch_tt<T, 0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, mask, uplo)
+                : launch_tt<T, 0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, mask, uplo);
+}
+
+template <typename T>
 cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t m, int64_t n,
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
                                 const wg_gate *gate, int uplo) {
-  if ((n + BN - 1) / BN > 65535) return cudaErrorInvalidConfiguration;
-  if (transA) {
-    return transB ? launch_tt<T, 1, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo)
-                  : launch_tt<T, 1, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo);
-  }
-  return transB ? launch_tt<T, 0, 1>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo)
-                : launch_tt<T, 0, 0>(s, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, gate, uplo);
+  return wg_launch_gemm_simt_masked<T>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords,
+                                       gate, nullptr, uplo);
 }
 
 template <typename T>
@@ -265,5 +294,9 @@ template cudaError_t wg_launch_gemm_simt<float>(cudaStream_t, int, int, int64_t,
 template cudaError_t wg_launch_gemm_simt<double>(cudaStream_t, int, int, int64_t, int64_t, int64_t, double,
                                                  const double *, int64_t, const double *, int64_t, double,
                                                  double *, int64_t, unsigned *, const wg_gate *, int);
+template cudaError_t wg_launch_gemm_simt_masked<float>(cudaStream_t, int, int, int64_t, int64_t, int64_t, float,
+                                                       const float *, int64_t, const float *, int64_t, float,
+                                                       float *, int64_t, unsigned *, const wg_gate *,
+                                                       const wg_tile_mask *, int);
 template cudaError_t wg_launch_scale<float>(cudaStream_t, int64_t, int64_t, float, float, float *, int64_t, int);
 template cudaError_t wg_launch_scale<double>(cudaStream_t, int64_t, int64_t, double, double, double *, int64_t, int);

@@ -77,6 +77,7 @@ struct wg_device {
   uint32_t epoch;    // sgemm call counter, tags WG_DW_FALLBACK
   int sgemm_path;
   int dgemm_path;
+  int fused_bn;  // tile width forced on the fused 3xTF32 kernel (0: chosen per call)
   cudaStream_t h2d, d2h;  // copy streams of the host-array path (created on first use)
   cudaMemPool_t staging;  // device copies of host-array operands; keeps its memory between calls
   // panelled 3xTF32 products: the stream their operand splits run on, and events
@@ -174,14 +175,20 @@ struct wg_tc_product {
   int64_t counter_room;
   int64_t panels;
   uint32_t epoch_a;
+  bool fused;       // panels run on the fused kernel (no operand splits, no side stream)
+  size_t ws_bytes;  // the fused panels' scratch
 };
 // Scratch of a product with these panel widths (queried before begin).
 size_t wg_tc_product_workspace(const wg_device *d, int64_t m, int64_t k, const int64_t *widths, size_t count);
-// Splits op(A) (on the side stream, after a_ready when given); every later panel
-// of the product must be one of `widths`.
+// Starts a product; every later panel must be one of `widths`. B0 / ldb: the
+// stored B the panels are cut from (its base and leading dimension). When the
+// fused kernel can read op(A) and every panel of op(B) (16-byte aligned bases,
+// leading dimensions multiples of 4), each panel is one fused launch on
+// d->stream after its b_ready event (a_ready then orders the first one).
+// Otherwise op(A) is split here (on the side stream, after a_ready when given).
 wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int transB, int64_t m, int64_t k,
                               float alpha, const float *A, int64_t lda, float beta, const int64_t *widths,
-                              size_t count, cudaEvent_t a_ready);
+                              size_t count, cudaEvent_t a_ready, const float *B0, int64_t ldb);
 // C (m x cols) = alpha*op(A)*op(B panel) + beta*C once b_ready (when given) has
 // fired: the split on the side stream, the MMA and its gated FFMA fallback on
 // d->stream. B is the panel's first column of op(B) in the caller's layout.
@@ -208,6 +215,37 @@ cudaError_t wg_launch_gemm_simt(cudaStream_t s, int transA, int transB, int64_t 
                                 int64_t k, T alpha, const T *A, int64_t lda, const T *B,
                                 int64_t ldb, T beta, T *C, int64_t ldc, unsigned *dwords,
                                 const wg_gate *gate, int uplo = 0);
+
+// Which columns of a gated FFMA launch to compute: those of the fused 3xTF32
+// kernel's tiles (tiles_m x ..., tile width bn, 128 rows) whose flag holds epoch.
+struct wg_tile_mask {
+  const unsigned *flags;
+  int tiles_m, bn;
+  uint32_t epoch;
+};
+// The gated FFMA launch restricted to the flagged tiles of a fused 3xTF32 call.
+template <typename T>
+cudaError_t wg_launch_gemm_simt_masked(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                       T alpha, const T *A, int64_t lda, const T *B, int64_t ldb, T beta, T *C,
+                                       int64_t ldc, unsigned *dwords, const wg_gate *gate, const wg_tile_mask *mask,
+                                       int uplo = 0);
+
+// The fused 3xTF32 kernel (sgemm_fused.cu): op(A), op(B) read by TMA straight
+// from the caller's matrices and split inside the kernel. Supported when both
+// bases are 16-byte aligned and lda, ldb are multiples of 4. Chosen
+// automatically for products of at most WG_FUSED_MAX_WORK multiply-adds: there
+// it saves the split pass and its launch; on larger ones its in-kernel split
+// competes with the MMAs for shared-memory bandwidth (measured on B200: 0.92
+// ms against 0.61 ms for the split pass + MMA kernel at 4096^3).
+constexpr double WG_FUSED_MAX_WORK = 1.2e9;
+bool wg_tf32x3_fused_supported(const wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                               const float *A, int64_t lda, const float *B, int64_t ldb);
+// Scratch one fused call needs (split-K partial sums, counters, tile flags).
+size_t wg_tf32x3_fused_workspace(const wg_device *d, int64_t m, int64_t n, int64_t k);
+// Queues the fused kernel and its gated FFMA fallback on stream st.
+wg_status wg_sgemm_tf32x3_fused(wg_device *d, cudaStream_t st, int transA, int transB, int64_t m, int64_t n,
+                                int64_t k, float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                                float beta, float *C, int64_t ldc, void *ws, size_t ws_bytes, int uplo = 0);
 
 // dgemm on the FP64 tensor-core (DMMA) path (dgemm_dmma.cu), on d->stream: the
 // TMA-fed pipelined kernel when the operands' layout allows its tensor maps,

@@ -1,0 +1,652 @@
+// 3xTF32 sgemm in one persistent tcgen05 kernel that splits its own operands.
+//
+// Same arithmetic as sgemm_tf32x3.cu (each fp32 operand x as hi = rna_tf32(x),
+// lo = rna_tf32(x - hi); A*B ~= A_lo*B_hi + A_hi*B_lo + A_hi*B_hi accumulated
+// in fp32 in TMEM; the reference's alpha/beta epilogue,
+// src/shaders/sgemm_large.wgsl:299-304), but the split happens inside the MMA
+// kernel instead of in a separate pass over HBM: op(A) and op(B) are read once,
+// straight from the caller's matrices, and no split operands are written.
+//
+// Roles of the 448 threads (one CTA per SM, persistent over 128 x BN tiles):
+//  warp 0     TMA producer: takes units (a whole tile, or one k-segment of a
+//             split tile) from a work counter, hands each to the other roles
+//             through a shared-memory queue, and streams the fp32 k-slices
+//             (128 x 16 of op(A), BN x 16 of op(B)) into an SR-deep raw ring.
+//             K-contiguous operands arrive in the 64-byte-swizzled K-major
+//             layout the tensor core reads; M/N-contiguous ones as plain
+//             [16][rows] slices.
+//  warps 6-13 split: read each raw slice, write its hi and lo parts into an
+//             SC-deep ring of K-major swizzled operand tiles (transposing the
+//             M/N-contiguous ones on the way), and note whether any element is
+//             outside the split's exact range (non-finite, or |x| outside
+//             [2^-50, 2^50]).
+//  warp 1     MMA issuer: three tcgen05.mma.kind::tf32 (M=128, N=BN, K=8) per
+//             8-wide k step into one of two TMEM accumulators.
+//  warps 2-5  epilogue: tcgen05.ld of the other accumulator, 16 columns at a
+//             time, and the fp32 alpha/beta store of C (or the partial sums of
+//             a split tile; the last segment to arrive adds all segments in k
+//             order), overlapping the next unit's MMAs.
+// Tile widths BN = 256, 128 or 64 (narrower tiles give small products more
+// CTAs); the last wave's tiles can be cut into k-segments as in the other
+// kernel. gemmtr calls skip tiles with no element in the triangle.
+//
+// IEEE semantics: a tile whose operands include an element outside the
+// split's exact range is not written; its entry in a per-tile flag array gets
+// the call's epoch (and the device's fallback word too), and the FFMA kernel
+// launched after this one, gated on those words, computes exactly the flagged
+// tiles from the untouched C. Every wait is clock-bounded (a stalled pipeline
+// sets a bit in the device error word, the roles drain, TMEM is freed).
+#include <cuda.h>
+
+#include "internal.h"
+#include "tcgen05.cuh"
+#include "tf32x3_common.cuh"
+
+namespace {
+
+using wg3::BM;
+using wg3::UQ;
+using wg3::WAIT_BUDGET;
+
+constexpr int XF_WARPS = 8;                      // split warps (6 .. 6 + XF_WARPS - 1)
+constexpr int XF_THREADS = 32 * XF_WARPS;
+constexpr int F_THREADS = 32 * (6 + XF_WARPS);
+constexpr int BADQ = 8;  // slots of the per-unit "operands ruled out" word, indexed by unit order
+constexpr int EC = 16;   // epilogue columns per TMEM load
+
+template <int BN_>
+struct FS {
+  static constexpr int BN = BN_, BK = 16;
+  static constexpr int A_TILE = BM * BK * 4, B_TILE = BN * BK * 4;
+  static constexpr int RAW = A_TILE + B_TILE, COMP = 2 * RAW;
+  static constexpr int SR = BN == 256 ? 3 : (BN == 128 ? 4 : 6);
+  static constexpr int SC = BN == 256 ? 3 : (BN == 128 ? 3 : 4);
+  static constexpr int TMEM_COLS = BN;  // per accumulator; two of them
+  static constexpr size_t SMEM = 1024 + (size_t)SR * RAW + (size_t)SC * COMP + 1024;
+  static_assert(B_TILE % 1024 == 0, "tiles keep 1024-byte alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+};
+
+struct FArgs {
+  int64_t m, n, k;
+  float alpha, beta;
+  float *C;
+  int64_t ldc;
+  unsigned *dwords;      // WG_DW_ERROR (wait timeouts), WG_DW_FALLBACK (any tile ruled out)
+  int tiles_m, tiles_n, kt;
+  int dp_tiles, sk_tiles, sk_split;
+  float *partials;       // split tiles: [sk_tiles * sk_split][BN][BM]
+  unsigned *next_unit;   // work counter (zero at launch)
+  unsigned *counters;    // split tiles: arrivals (zero at launch, reset by the finishing segment)
+  unsigned *tile_bad;    // split tiles: a segment saw ruled-out operands (zero at launch)
+  unsigned *tile_flags;  // [tiles_m * tiles_n]: `epoch` where the FFMA kernel computes the tile
+  uint32_t epoch;
+  int units;
+  int uplo;
+};
+
+__device__ __forceinline__ void split4(const float4 x, float4 &h, float4 &l, bool &bad) {
+  bad |= !wg3::split_ok(x.x) | !wg3::split_ok(x.y) | !wg3::split_ok(x.z) | !wg3::split_ok(x.w);
+  h.x = wg3::rna_tf32(x.x);
+  h.y = wg3::rna_tf32(x.y);
+  h.z = wg3::rna_tf32(x.z);
+  h.w = wg3::rna_tf32(x.w);
+  l.x = wg3::rna_tf32(x.x - h.x);
+  l.y = wg3::rna_tf32(x.y - h.y);
+  l.z = wg3::rna_tf32(x.z - h.z);
+  l.w = wg3::rna_tf32(x.w - h.w);
+}
+
+// Splits one raw k-slice of ROWS rows into hi and lo K-major tiles (rows of 64
+// bytes, 16-byte chunk c of row r at chunk position c ^ ((r >> 1) & 3): the
+// 64-byte swizzle TMA writes and the MMA descriptors describe). KMAJ: the raw
+// slice is already in that layout, so chunk o maps to chunk o. Otherwise it is
+// [16 k][ROWS]: four k values of one row are gathered (a warp reads 32
+// consecutive rows per k: conflict-free) and written as one chunk.
+template <int ROWS, bool KMAJ>
+__device__ __forceinline__ bool split_slice(const uint8_t *raw, uint8_t *hi, uint8_t *lo, int xt) {
+  constexpr int STEP = XF_THREADS;
+  bool bad = false;
+  if (KMAJ) {
+    const float4 *src = reinterpret_cast<const float4 *>(raw);
+#pragma unroll
+    for (int i = xt; i < ROWS * 4; i += STEP) {
+      float4 h, l;
+      split4(src[i], h, l, bad);
+      reinterpret_cast<float4 *>(hi)[i] = h;
+      reinterpret_cast<float4 *>(lo)[i] = l;
+    }
+  } else {
+    const float *src = reinterpret_cast<const float *>(raw);
+#pragma unroll
+    for (int i = xt; i < ROWS * 4; i += STEP) {
+      const int r = i % ROWS, c = i / ROWS;
+      const float4 x = make_float4(src[(4 * c) * ROWS + r], src[(4 * c + 1) * ROWS + r], src[(4 * c + 2) * ROWS + r],
+                                   src[(4 * c + 3) * ROWS + r]);
+      float4 h, l;
+      split4(x, h, l, bad);
+      const int off = r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+      *reinterpret_cast<float4 *>(hi + off) = h;
+      *reinterpret_cast<float4 *>(lo + off) = l;
+    }
+  }
+  return bad;
+}
+
+template <class S, int A_K, int B_K>
+__global__ void __launch_bounds__(F_THREADS, 1)
+tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+             const FArgs args) {
+  constexpr int BN = S::BN, BK = S::BK, SR = S::SR, SC = S::SC;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = wgtc::smem_addr(smem_raw);
+  uint8_t *smem = smem_raw + ((1024 - (base & 1023)) & 1023);
+  uint8_t *raw = smem;                         // SR x RAW
+  uint8_t *comp = smem + (size_t)SR * S::RAW;  // SC x COMP: A_hi, A_lo, B_hi, B_lo
+  uint64_t *raw_full = reinterpret_cast<uint64_t *>(comp + (size_t)SC * S::COMP);
+  uint64_t *raw_empty = raw_full + SR;
+  uint64_t *comp_full = raw_empty + SR;
+  uint64_t *comp_empty = comp_full + SC;
+  uint64_t *acc_full = comp_empty + SC;  // [2]
+  uint64_t *acc_empty = acc_full + 2;    // [2]
+  uint64_t *uq_full = acc_empty + 2;     // [UQ]
+  uint64_t *uq_empty = uq_full + UQ;     // [UQ]: MMA issuer, epilogue and split have read the slot
+  uint64_t *unit_done = uq_empty + UQ;   // [BADQ]: the split has seen all of unit n's operands
+  volatile int *uq = reinterpret_cast<volatile int *>(unit_done + BADQ);
+  volatile int *unit_bad = uq + UQ;      // [BADQ]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(const_cast<int *>(unit_bad) + BADQ);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile unsigned *last_flag = reinterpret_cast<volatile unsigned *>(tmem_slot + 2);
+  volatile unsigned *seg_bad = reinterpret_cast<volatile unsigned *>(tmem_slot + 3);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SR; s++) {
+      wgtc::mbar_init(&raw_full[s], 1);
+      wgtc::mbar_init(&raw_empty[s], XF_WARPS);
+    }
+    for (int s = 0; s < SC; s++) {
+      wgtc::mbar_init(&comp_full[s], XF_WARPS);
+      wgtc::mbar_init(&comp_empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      wgtc::mbar_init(&acc_full[b], 1);
+      wgtc::mbar_init(&acc_empty[b], 32 * wg3::EPI_WARPS);
+    }
+    for (int i = 0; i < UQ; i++) {
+      wgtc::mbar_init(&uq_full[i], 1);
+      wgtc::mbar_init(&uq_empty[i], 3);
+    }
+    for (int i = 0; i < BADQ; i++) wgtc::mbar_init(&unit_done[i], 1);
+    *abort_flag = 0;
+    wgtc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    wgtc::prefetch_tensormap(&map_a);
+    wgtc::prefetch_tensormap(&map_b);
+  }
+  if (warp == 1) {
+    wgtc::tmem_alloc(tmem_slot, 2 * S::TMEM_COLS);
+    wgtc::tmem_relinquish();
+  }
+  wgtc::tc_fence_before();
+  __syncthreads();
+  wgtc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      int64_t g = 0;
+      bool ok = true;
+      for (int n = 0; ok; n++) {
+        const int slot = n % UQ;
+        int un = n == 0 ? (int)blockIdx.x : (int)gridDim.x + (int)atomicAdd(args.next_unit, 1u);
+        while (args.uplo != WG_UPLO_FULL && un < args.units) {
+          int tm0, tn0;
+          wg3::raster(args, wg3::decode(args, un).t, tm0, tn0);
+          if (!wg_tile_outside(args.uplo, (int64_t)tm0 * BM, BM, (int64_t)tn0 * BN, BN)) break;
+          un = (int)gridDim.x + (int)atomicAdd(args.next_unit, 1u);
+        }
+        if (un >= args.units) un = -1;  // no work left: tells the other roles to stop
+        if (!wgtc::mbar_wait_bounded(&uq_empty[slot], ((uint32_t)(n / UQ) & 1u) ^ 1u, WAIT_BUDGET) ||
+            *abort_flag) {
+          atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+          *abort_flag = 1;
+          break;
+        }
+        uq[slot] = un;
+        wg3::mbar_arrive(&uq_full[slot]);
+        if (un < 0) break;
+        const wg3::Unit u = wg3::decode(args, un);
+        int tm, tn;
+        wg3::raster(args, u.t, tm, tn);
+        for (int kb = u.kb0; kb < u.kb1; kb++, g++) {
+          const int s = (int)(g % SR);
+          const uint32_t ph = (uint32_t)(g / SR) & 1u;
+          if (!wgtc::mbar_wait_bounded(&raw_empty[s], ph ^ 1u, WAIT_BUDGET) || *abort_flag) {
+            atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t *st = raw + (size_t)s * S::RAW;
+          wgtc::mbar_arrive_expect_tx(&raw_full[s], S::RAW);
+          const int kc = kb * BK;
+          if (A_K)
+            wgtc::tma_load_2d(st, &map_a, &raw_full[s], kc, tm * BM);
+          else
+            wgtc::tma_load_2d(st, &map_a, &raw_full[s], tm * BM, kc);
+          if (B_K)
+            wgtc::tma_load_2d(st + S::A_TILE, &map_b, &raw_full[s], kc, tn * BN);
+          else
+            wgtc::tma_load_2d(st + S::A_TILE, &map_b, &raw_full[s], tn * BN, kc);
+        }
+      }
+      // Every copy issued lands before the CTA can exit.
+      for (int64_t q = g - SR > 0 ? g - SR : 0; q < g; q++)
+        wgtc::mbar_wait_bounded(&raw_full[q % SR], (uint32_t)(q / SR) & 1u, WAIT_BUDGET);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      constexpr uint32_t idesc = wgtc::idesc_tf32(BM, BN);
+      int64_t h = 0;
+      bool ok = true;
+      for (int n = 0; ok; n++) {
+        const int slot = n % UQ;
+        if (!wgtc::mbar_wait_bounded(&uq_full[slot], (uint32_t)(n / UQ) & 1u, WAIT_BUDGET) || *abort_flag) {
+          atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+          *abort_flag = 1;
+          break;
+        }
+        const int un = uq[slot];
+        wg3::mbar_arrive(&uq_empty[slot]);
+        if (un < 0) break;
+        const wg3::Unit u = wg3::decode(args, un);
+        const int b = n & 1;
+        const uint32_t use = (uint32_t)(n >> 1);
+        if (!wgtc::mbar_wait_bounded(&acc_empty[b], (use & 1u) ^ 1u, WAIT_BUDGET) || *abort_flag) {
+          atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+          *abort_flag = 1;
+          break;
+        }
+        wgtc::tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(b * S::TMEM_COLS);
+        for (int kb = u.kb0; kb < u.kb1; kb++, h++) {
+          const int c = (int)(h % SC);
+          if (!wgtc::mbar_wait_bounded(&comp_full[c], (uint32_t)(h / SC) & 1u, WAIT_BUDGET) || *abort_flag) {
+            atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          wgtc::tc_fence_after();
+          const uint32_t st = wgtc::smem_addr(comp + (size_t)c * S::COMP);
+          const uint32_t a_hi = st, a_lo = st + S::A_TILE, b_hi = st + 2 * S::A_TILE, b_lo = b_hi + S::B_TILE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; kk++) {
+            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the 64-byte rows
+            const uint64_t dah = wgtc::smem_desc_kmajor(a_hi + off, 64);
+            const uint64_t dal = wgtc::smem_desc_kmajor(a_lo + off, 64);
+            const uint64_t dbh = wgtc::smem_desc_kmajor(b_hi + off, 64);
+            const uint64_t dbl = wgtc::smem_desc_kmajor(b_lo + off, 64);
+            const uint32_t acc0 = (kb > u.kb0 || kk > 0) ? 1u : 0u;
+            wgtc::mma_tf32(d_tmem, dal, dbh, idesc, acc0);  // small terms first
+            wgtc::mma_tf32(d_tmem, dah, dbl, idesc, 1u);
+            wgtc::mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+          }
+          wgtc::mma_commit(&comp_empty[c]);  // frees the operand stage once these MMAs have read it
+        }
+        wgtc::mma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= 6) {
+    // ---- split: raw fp32 slices -> hi / lo operand tiles ----
+    const int xt = threadIdx.x - 192;
+    int64_t g = 0, h = 0;
+    for (int n = 0;; n++) {
+      const int slot = n % UQ;
+      const bool got = wgtc::mbar_wait_bounded(&uq_full[slot], (uint32_t)(n / UQ) & 1u, WAIT_BUDGET);
+      const int un = got ? uq[slot] : -1;
+      if (!wg3::group_all<3, XF_THREADS>(got && *abort_flag == 0)) {
+        if (!got) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      if (xt == 0) wg3::mbar_arrive(&uq_empty[slot]);
+      if (un < 0) break;
+      const wg3::Unit u = wg3::decode(args, un);
+      bool bad = false, failed = false;
+      for (int kb = u.kb0; kb < u.kb1; kb++, g++, h++) {
+        const int s = (int)(g % SR), c = (int)(h % SC);
+        const bool okr = wgtc::mbar_wait_bounded(&raw_full[s], (uint32_t)(g / SR) & 1u, WAIT_BUDGET);
+        const bool okc = wgtc::mbar_wait_bounded(&comp_empty[c], ((uint32_t)(h / SC) & 1u) ^ 1u, WAIT_BUDGET);
+        if (!wg3::group_all<3, XF_THREADS>(okr && okc && *abort_flag == 0)) {
+          if (!(okr && okc)) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+          *abort_flag = 1;
+          failed = true;
+          break;
+        }
+        const uint8_t *rs = raw + (size_t)s * S::RAW;
+        uint8_t *cs = comp + (size_t)c * S::COMP;
+        bad |= split_slice<BM, A_K != 0>(rs, cs, cs + S::A_TILE, xt);
+        bad |= split_slice<BN, B_K != 0>(rs + S::A_TILE, cs + 2 * S::A_TILE, cs + 2 * S::A_TILE + S::B_TILE, xt);
+        wgtc::fence_proxy_async_smem();  // the MMAs read these tiles through the async proxy
+        __syncwarp();
+        if (lane == 0) {
+          wg3::mbar_arrive(&comp_full[c]);
+          wg3::mbar_arrive(&raw_empty[s]);
+        }
+      }
+      if (failed) break;
+      const bool any_bad = wg3::group_any<3, XF_THREADS>(bad);
+      if (xt == 0) {
+        unit_bad[n % BADQ] = any_bad ? 1 : 0;
+        wg3::mbar_arrive(&unit_done[n % BADQ]);
+      }
+    }
+  } else {
+    // ---- epilogue: TMEM -> registers -> C (or a partial-sum slot) ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    const float alpha = args.alpha, beta = args.beta;
+    for (int n = 0;; n++) {
+      const int slot = n % UQ;
+      const bool got = wgtc::mbar_wait_bounded(&uq_full[slot], (uint32_t)(n / UQ) & 1u, WAIT_BUDGET);
+      const int un = got ? uq[slot] : -1;
+      if (!wg3::epi_all(got && *abort_flag == 0)) {
+        if (!got) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      if (threadIdx.x == 64) wg3::mbar_arrive(&uq_empty[slot]);
+      if (un < 0) break;
+      const wg3::Unit u = wg3::decode(args, un);
+      const int b = n & 1;
+      const uint32_t use = (uint32_t)(n >> 1);
+      const bool ready = wgtc::mbar_wait_bounded(&acc_full[b], use & 1u, WAIT_BUDGET) &&
+                         wgtc::mbar_wait_bounded(&unit_done[n % BADQ], (uint32_t)(n / BADQ) & 1u, WAIT_BUDGET);
+      if (!wg3::epi_all(ready && *abort_flag == 0)) {
+        if (!ready) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      wgtc::tc_fence_after();
+      const bool bad = unit_bad[n % BADQ] != 0;
+      int tm, tn;
+      wg3::raster(args, u.t, tm, tn);
+      const int64_t row = (int64_t)tm * BM + row_in_tile;
+      const int64_t n0 = (int64_t)tn * BN;
+      const uint32_t trow = tmem + (uint32_t)(b * S::TMEM_COLS) + ((uint32_t)(q * 32) << 16);
+      const bool whole = u.seg < 0;
+      bool finish = whole, ruled_out = bad;
+      const int local = u.t - args.dp_tiles;
+      if (!whole) {
+        // Leave this segment's partial sums (unless its operands were ruled out),
+        // then count arrivals on the tile.
+        if (!bad) {
+          float *part = args.partials + ((int64_t)local * args.sk_split + u.seg) * BN * BM + row_in_tile;
+          for (int c = 0; c < BN; c += EC) {
+            uint32_t r[EC];
+            wgtc::tmem_ld_32x32b_x16(trow + (uint32_t)c, r);
+            wgtc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < EC; j++) part[(int64_t)(c + j) * BM] = __uint_as_float(r[j]);
+          }
+        }
+        if (bad && threadIdx.x == 64) atomicOr(args.tile_bad + local, 1u);
+        __threadfence();
+        wg3::epi_bar();
+        if (threadIdx.x == 64) {
+          const unsigned prev = atomicAdd(args.counters + local, 1u);
+          const bool last = prev == (unsigned)(args.sk_split - 1);
+          if (last) {
+            args.counters[local] = 0;  // ready for the next call on this workspace
+            *seg_bad = atomicExch(args.tile_bad + local, 0u);
+          }
+          *last_flag = last ? 1u : 0u;
+          __threadfence();
+        }
+        wg3::epi_bar();
+        finish = *last_flag != 0;
+        if (finish) {
+          __threadfence();  // order the reads of the other segments' partial sums
+          ruled_out = *seg_bad != 0;
+        }
+      }
+      if (finish && ruled_out) {
+        // Leave C untouched: the gated FFMA kernel computes this tile.
+        if (threadIdx.x == 64) {
+          args.tile_flags[tm + (int64_t)tn * args.tiles_m] = args.epoch;
+          atomicExch(args.dwords + WG_DW_FALLBACK, args.epoch);
+        }
+      } else if (finish) {
+        const int nseg = whole ? 1 : args.sk_split;
+        const int own = whole ? 0 : u.seg;
+        const float *part0 = whole ? nullptr : args.partials + (int64_t)local * args.sk_split * BN * BM + row_in_tile;
+        const bool in_rows = row < args.m;
+        for (int c = 0; c < BN; c += EC) {
+          uint32_t r[EC];
+          wgtc::tmem_ld_32x32b_x16(trow + (uint32_t)c, r);
+          wgtc::tmem_ld_wait();
+          float acc[EC];
+#pragma unroll
+          for (int j = 0; j < EC; j++) acc[j] = __uint_as_float(r[j]);
+          if (nseg > 1) {
+            // Segments in k order, two loaded together; this CTA's own comes from TMEM.
+            float sum[EC];
+            for (int g0 = 0; g0 < nseg; g0 += 2) {
+              float v[2][EC];
+#pragma unroll
+              for (int qq = 0; qq < 2; qq++) {
+                const int sgi = g0 + qq;
+                if (sgi < nseg && sgi != own) {
+                  const float *p = part0 + ((int64_t)sgi * BN + c) * BM;
+#pragma unroll
+                  for (int j = 0; j < EC; j++) v[qq][j] = __ldcg(p + (int64_t)j * BM);
+                }
+              }
+#pragma unroll
+              for (int qq = 0; qq < 2; qq++) {
+                const int sgi = g0 + qq;
+                if (sgi < nseg) {
+#pragma unroll
+                  for (int j = 0; j < EC; j++) {
+                    const float x = sgi == own ? acc[j] : v[qq][j];
+                    sum[j] = sgi == 0 ? x : sum[j] + x;
+                  }
+                }
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < EC; j++) acc[j] = sum[j];
+          }
+          if (in_rows) {
+            float old[EC];
+            if (beta != 0.0f) {
+#pragma unroll
+              for (int j = 0; j < EC; j++) {
+                const int64_t col = n0 + c + j;
+                old[j] = col < args.n && wg_in_triangle(args.uplo, row, col) ? args.C[row + col * args.ldc] : 0.0f;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < EC; j++) {
+              const int64_t col = n0 + c + j;
+              if (col < args.n && wg_in_triangle(args.uplo, row, col)) {
+                const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc[j]);
+                args.C[row + col * args.ldc] = (beta != 0.0f) ? __fmaf_rn(beta, old[j], s) : s;
+              }
+            }
+          }
+        }
+      }
+      wgtc::tc_fence_before();
+      wg3::mbar_arrive(&acc_empty[b]);  // accumulator b may be refilled
+    }
+  }
+
+  wgtc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    wgtc::tc_fence_after();
+    wgtc::tmem_dealloc(tmem, 2 * S::TMEM_COLS);
+  }
+}
+
+// ---- host side ------------------------------------------------------------
+
+// Tensor map of op(A) (rows = m) or of op(B) as its N x K operand (rows = n):
+// K-contiguous sources in 64-byte-swizzled boxes of 16 k x box_rows, the others
+// in plain boxes of box_rows x 16 k.
+bool make_fmap(CUtensorMap *map, const float *ptr, bool kcontig, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+  wg_encode_tiled_fn fn = wg_encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[2], strides[1] = {(cuuint64_t)ld * sizeof(float)};
+  cuuint32_t box[2], estr[2] = {1, 1};
+  if (kcontig) {
+    dims[0] = (cuuint64_t)k;
+    dims[1] = (cuuint64_t)rows;
+    box[0] = 16;
+    box[1] = (cuuint32_t)box_rows;
+  } else {
+    dims[0] = (cuuint64_t)rows;
+    dims[1] = (cuuint64_t)k;
+    box[0] = (cuuint32_t)box_rows;
+    box[1] = 16;
+  }
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, kcontig ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct FLayout {
+  int bn;
+  int tiles_m, tiles_n, kt;
+  wg3::Plan plan;
+};
+
+// Modelled time of a plan, in units of one 16-deep k-block of a 128 x 256 tile:
+// whole rounds of kt k-blocks, split rounds of kt/s, the split's overhead, and
+// a k-block of a narrower tile costing its share of the MMA time but no less
+// than about a third (the operand split and the pipeline's fixed steps).
+double plan_time(int G, const wg3::Plan &p, int kt, int bn) {
+  const double unit = bn >= 256 ? 1.0 : (bn == 128 ? 0.55 : 0.35);
+  double rounds;
+  if (p.sk_tiles == 0) {
+    rounds = (double)((p.dp_tiles + G - 1) / G) * kt;
+  } else {
+    const int s = p.sk_split;
+    rounds = (double)(p.dp_tiles / G) * kt + (double)(((int64_t)s * p.sk_tiles + G - 1) / G) * ((double)kt / s) +
+             wg3::split_overhead(kt, s);
+  }
+  return rounds * unit;
+}
+
+FLayout flayout_of(int G, int64_t m, int64_t n, int64_t k, int bn_force, bool allow_split) {
+  FLayout best{0, 0, 0, 0, {0, 0, 0, 1}};
+  double best_t = 0.0;
+  const int kt = (int)((k + 15) / 16);
+  for (int bn : {256, 128, 64}) {
+    if (bn_force && bn != bn_force) continue;
+    FLayout L;
+    L.bn = bn;
+    L.tiles_m = (int)((m + BM - 1) / BM);
+    L.tiles_n = (int)((n + bn - 1) / bn);
+    L.kt = kt;
+    L.plan = wg3::plan_tiles(G, L.tiles_m, L.tiles_n, kt, allow_split);
+    const double t = plan_time(G, L.plan, kt, bn);
+    if (best.bn == 0 || t < best_t * 0.97) {  // prefer the wider tile unless clearly slower
+      best = L;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
+// Scratch of one call: [partials | next_unit | counters | tile_bad | tile_flags];
+// everything from next_unit on is zeroed before the launch.
+struct FScratch {
+  size_t partial_bytes, zero_offset, zero_bytes, total;
+};
+FScratch fscratch_of(const FLayout &L) {
+  FScratch s;
+  s.partial_bytes = (size_t)L.plan.sk_tiles * L.plan.sk_split * BM * L.bn * sizeof(float);
+  s.zero_offset = s.partial_bytes;
+  const size_t tiles = (size_t)L.tiles_m * L.tiles_n;
+  s.zero_bytes = (1 + 2 * (size_t)L.plan.sk_tiles + tiles) * sizeof(unsigned);
+  s.total = s.zero_offset + s.zero_bytes + 256;
+  return s;
+}
+
+template <int BN>
+cudaError_t launch_bn(cudaStream_t st, int grid, bool a_k, bool b_k, const CUtensorMap &ma, const CUtensorMap &mb,
+                      const FArgs &args) {
+  using S = FS<BN>;
+  auto kern = a_k ? (b_k ? tf32x3_fused<S, 1, 1> : tf32x3_fused<S, 1, 0>)
+                  : (b_k ? tf32x3_fused<S, 0, 1> : tf32x3_fused<S, 0, 0>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, F_THREADS, S::SMEM, st>>>(ma, mb, args);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool wg_tf32x3_fused_supported(const wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                               const float *A, int64_t lda, const float *B, int64_t ldb) {
+  if (d->cc_major != 10 || k < 8 || !wg_encode_tiled()) return false;
+  // TMA: 16-byte aligned bases and row strides; coordinates in int range.
+  if (reinterpret_cast<uintptr_t>(A) % 16 || reinterpret_cast<uintptr_t>(B) % 16 || lda % 4 || ldb % 4) return false;
+  if (m >= ((int64_t)1 << 31) - 512 || n >= ((int64_t)1 << 31) - 512 || k >= ((int64_t)1 << 31) - 64) return false;
+  const int64_t tiles = ((m + BM - 1) / BM) * ((n + 63) / 64);
+  return tiles < ((int64_t)1 << 30);
+}
+
+size_t wg_tf32x3_fused_workspace(const wg_device *d, int64_t m, int64_t n, int64_t k) {
+  return fscratch_of(flayout_of(d->sm_count, m, n, k, d->fused_bn, true)).total;
+}
+
+wg_status wg_sgemm_tf32x3_fused(wg_device *d, cudaStream_t st, int transA, int transB, int64_t m, int64_t n,
+                                int64_t k, float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                                float beta, float *C, int64_t ldc, void *ws, size_t ws_bytes, int uplo) {
+  FLayout L = flayout_of(d->sm_count, m, n, k, d->fused_bn, true);
+  FScratch sc = fscratch_of(L);
+  if (sc.total > ws_bytes) {  // no room for the split tiles' partial sums: whole tiles
+    L = flayout_of(d->sm_count, m, n, k, d->fused_bn, false);
+    sc = fscratch_of(L);
+    if (sc.total > ws_bytes) return wg_fail(WG_ERR_INVALID_ARGUMENT, "fused 3xTF32 scratch too small");
+  }
+  const bool a_k = transA != 0, b_k = transB == 0;
+  CUtensorMap maps[2];
+  if (!make_fmap(&maps[0], A, a_k, m, k, lda, BM) || !make_fmap(&maps[1], B, b_k, n, k, ldb, L.bn))
+    return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fused 3xTF32 operands");
+  char *w = static_cast<char *>(ws);
+  unsigned *zero = reinterpret_cast<unsigned *>(w + sc.zero_offset);
+  WG_CUDA(cudaMemsetAsync(zero, 0, sc.zero_bytes, st));
+  const uint32_t epoch = wg_next_epoch(d);
+  const wg3::Plan &p = L.plan;
+  FArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, L.tiles_m, L.tiles_n, L.kt, p.dp_tiles, p.sk_tiles,
+             p.sk_split, p.sk_tiles ? reinterpret_cast<float *>(w) : nullptr, zero, zero + 1,
+             zero + 1 + p.sk_tiles, zero + 1 + 2 * p.sk_tiles, epoch, p.dp_tiles + p.sk_tiles * p.sk_split, uplo};
+  {
+    wg_launch_scope scope(d, "sgemm_tf32x3_fused", st);
+    cudaError_t e = L.bn == 256 ? launch_bn<256>(st, p.grid, a_k, b_k, maps[0], maps[1], args)
+                  : L.bn == 128 ? launch_bn<128>(st, p.grid, a_k, b_k, maps[0], maps[1], args)
+                                : launch_bn<64>(st, p.grid, a_k, b_k, maps[0], maps[1], args);
+    WG_CUDA(e);
+  }
+  {
+    // Computes the tiles the kernel left to it (operands outside the split's
+    // exact range); a closed gate exits at once.
+    wg_launch_scope scope(d, "sgemm_simt_fallback", st);
+    const wg_gate gate{d->dwords + WG_DW_FALLBACK, d->dwords + WG_DW_FALLBACK, epoch, epoch};
+    const wg_tile_mask mask{args.tile_flags, L.tiles_m, L.bn, epoch};
+    WG_CUDA(wg_launch_gemm_simt_masked(st, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, d->dwords,
+                                       &gate, &mask, uplo));
+  }
+  return WG_OK;
+}

@@ -46,13 +46,26 @@
 
 #include "internal.h"
 #include "tcgen05.cuh"
+#include "tf32x3_common.cuh"
 
 namespace {
 
-constexpr int BM = 128;              // UMMA M (cta_group::1), TMEM lanes
-constexpr int EPI_WARPS = 4;
+using wg3::BM;
+using wg3::EPI_WARPS;
+using wg3::WAIT_BUDGET;
+using wg3::GROUP_M;
+using wg3::MAX_SEG;
+using wg3::UQ;
+using wg3::Unit;
+using wg3::rna_tf32;
+using wg3::split_ok;
+using wg3::epi_bar;
+using wg3::epi_all;
+using wg3::mbar_arrive;
+using wg3::Plan;
+using wg3::split_overhead;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr long long WAIT_BUDGET = 4000000000LL;  // SM clocks (~2 s) before a wait gives up
+constexpr int SEG_GROUP = 2;  // partial-sum segments the fixup loads at once
 
 // Kernel shape: BN columns of C per CTA, BK floats of K per pipeline stage
 // (BK * 4 bytes = the swizzle span: 128 -> SWIZZLE_128B, 64 -> SWIZZLE_64B).
@@ -71,21 +84,6 @@ struct Shape {
 };
 
 using Sh = Shape<256, 16, 4>;  // 48 KB stages, four deep
-
-// Round to nearest TF32 (10 explicit mantissa bits), ties away from zero, on
-// the bit pattern of a finite float: add half of the dropped 13-bit field and
-// truncate. Magnitudes here stay far below the overflow boundary.
-__device__ __forceinline__ float rna_tf32(float x) {
-  uint32_t u = __float_as_uint(x);
-  return __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
-}
-
-// An operand the split represents to ~2^-22 relative accuracy with normal
-// lo parts: zero, or a finite value with 2^-50 <= |x| <= 2^50.
-__device__ __forceinline__ bool split_ok(float x) {
-  const float ax = fabsf(x);
-  return x == 0.0f || (ax >= 0x1p-50f && ax <= 0x1p50f);
-}
 
 struct PackArgs {
   const float *src;
@@ -150,10 +148,6 @@ __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64
 }
 
 
-constexpr int GROUP_M = 16;  // tile rows per rasterization group
-constexpr int MAX_SEG = 16;  // most k-segments one tile is split into
-constexpr int SEG_GROUP = 2; // partial-sum segments the fixup loads at once
-
 struct MmaArgs {
   int64_t m, n, k;
   float alpha, beta;
@@ -171,67 +165,6 @@ struct MmaArgs {
   int units;                 // dp_tiles + sk_tiles * sk_split
   int uplo;                  // WG_UPLO_*: tiles with no element in the triangle are skipped
 };
-
-// Tile t -> (tile row, tile column), GROUP_M tile rows at a time.
-__device__ __forceinline__ void raster(const MmaArgs &a, int t, int &tm, int &tn) {
-  const int per_group = GROUP_M * a.tiles_n;
-  const int g = t / per_group, first = g * GROUP_M;
-  const int rows = a.tiles_m - first < GROUP_M ? a.tiles_m - first : GROUP_M;
-  const int r = t % per_group;
-  tm = first + r % rows;
-  tn = r / rows;
-}
-
-// One unit of work: k-blocks [kb0, kb1) of tile t; for a split tile, its
-// segment `seg` of sk_split (tile index within the split region: t - dp_tiles).
-struct Unit {
-  int t, kb0, kb1, seg;
-};
-
-// Units are numbered whole tiles first (0 .. dp_tiles-1, in raster order), then
-// the split units: unit dp_tiles + v is segment v / sk_tiles of split tile
-// v % sk_tiles, so units handed out together cover neighbouring tiles over the
-// same k range.
-__device__ __forceinline__ Unit decode(const MmaArgs &a, int u) {
-  Unit x;
-  if (u < a.dp_tiles) {
-    x.t = u;
-    x.kb0 = 0;
-    x.kb1 = a.kt;
-    x.seg = -1;
-    return x;
-  }
-  const int v = u - a.dp_tiles;
-  x.seg = v / a.sk_tiles;
-  x.t = a.dp_tiles + v % a.sk_tiles;
-  x.kb0 = (int)((int64_t)a.kt * x.seg / a.sk_split);
-  x.kb1 = (int)((int64_t)a.kt * (x.seg + 1) / a.sk_split);
-  return x;
-}
-
-// Depth of the queue through which the producer hands each unit it takes to the
-// MMA issuer and the epilogue.
-constexpr int UQ = 4;
-
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// True on every epilogue thread iff `v` is true on all of them, so a decision to
-// stop is the same for all four warps and no warp is left waiting at epi_bar.
-__device__ __forceinline__ bool epi_all(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 2, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v)
-      : "memory");
-  return r != 0;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(wgtc::smem_addr(bar)) : "memory");
-}
 
 template <class S>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -301,7 +234,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       // gemmtr: tiles with no element in the triangle are not computed at all.
       while (args.uplo != WG_UPLO_FULL && un < args.units) {
         int tm0, tn0;
-        raster(args, decode(args, un).t, tm0, tn0);
+        wg3::raster(args, wg3::decode(args, un).t, tm0, tn0);
         if (!wg_tile_outside(args.uplo, (int64_t)tm0 * BM, BM, (int64_t)tn0 * S::BN, S::BN)) break;
         un = (int)gridDim.x + (int)atomicAdd(args.next_unit, 1u);
       }
@@ -314,9 +247,9 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       uq[slot] = un;
       mbar_arrive(&uq_full[slot]);
       if (un < 0) break;
-      const Unit u = decode(args, un);
+      const Unit u = wg3::decode(args, un);
       int tm, tn;
-      raster(args, u.t, tm, tn);
+      wg3::raster(args, u.t, tm, tn);
       for (int kb = u.kb0; kb < u.kb1; kb++, g++) {
         const int s = (int)(g % S::STAGES);
         const uint32_t ph = (uint32_t)(g / S::STAGES) & 1u;
@@ -353,7 +286,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       const int un = uq[slot];
       mbar_arrive(&uq_empty[slot]);
       if (un < 0) break;
-      const Unit u = decode(args, un);
+      const Unit u = wg3::decode(args, un);
       const int b = n_units & 1;
       const uint32_t use = (uint32_t)(n_units >> 1);
       if (!wgtc::mbar_wait_bounded(&acc_empty[b], (use & 1u) ^ 1u, WAIT_BUDGET) || *abort_flag) {
@@ -411,7 +344,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       }
       if (threadIdx.x == 64) mbar_arrive(&uq_empty[slot]);
       if (un < 0) break;
-      const Unit u = decode(args, un);
+      const Unit u = wg3::decode(args, un);
       const int b = n_units & 1;
       const uint32_t use = (uint32_t)(n_units >> 1);
       const bool ready = wgtc::mbar_wait_bounded(&acc_full[b], use & 1u, WAIT_BUDGET);
@@ -422,7 +355,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       }
       wgtc::tc_fence_after();
       int tm, tn;
-      raster(args, u.t, tm, tn);
+      wg3::raster(args, u.t, tm, tn);
       const int64_t row = (int64_t)tm * BM + row_in_tile;
       const int64_t n0 = (int64_t)tn * S::BN;
       const uint32_t trow = tmem + (uint32_t)(b * S::TMEM_COLS) + ((uint32_t)(q * 32) << 16);
@@ -570,52 +503,8 @@ Layout layout_of(int64_t m, int64_t n, int64_t k) {
   return L;
 }
 
-// How a call's tiles are spread over the persistent grid.
-struct Plan {
-  int grid;      // CTAs (at most one per SM)
-  int dp_tiles;  // tiles taken whole, round-robin
-  int sk_tiles;  // tiles split into sk_split k-segments
-  int sk_split;
-};
-
-// Whole tiles for every full wave; the rem = T mod G leftover tiles are split
-// into s k-segments when that shortens the last wave. In units of one k-block's
-// MMA time (about 0.5 us on B200), the last wave costs ceil(s*rem/G) rounds of
-// kt/s k-blocks, plus the split's overhead: partial-tile writes, the finishing
-// segment's reads of the other s-1 partial tiles at the end of the wave, and the
-// round imbalance, about (s-1)*c + 8. Measured on B200, c is about 28 for deep
-// tiles (kt = 1024: 128 tiles over 148 SMs ran fastest whole) and about 4 for
-// shallow ones (kt <= 64: 512^3 and 1024^3 ran fastest in 4 segments), so c
-// steps from 4 to 28 at kt = 512. s (at most kt/4 and MAX_SEG) minimises the
-// total, and s = 1 keeps the tiles whole.
-double split_overhead(int kt, int s) { return (kt >= 512 ? 28.0 : 4.0) * (s - 1) + 8.0; }
-
 Plan plan_of(int G, const Layout &L, bool allow_split) {
-  const int T = L.tiles_m * L.tiles_n;
-  Plan p;
-  p.grid = T < G ? T : G;
-  p.dp_tiles = T;
-  p.sk_tiles = 0;
-  p.sk_split = 1;
-  const int rem = T % G;
-  if (!allow_split || rem == 0) return p;
-  const int smax = L.kt / 4 < MAX_SEG ? L.kt / 4 : MAX_SEG;
-  int best_s = 1;
-  double best = (double)L.kt;
-  for (int s = 2; s <= smax; s++) {
-    const double cost = (double)((s * rem + G - 1) / G) * ((double)L.kt / s) + split_overhead(L.kt, s);
-    if (cost < best - 1e-9) {
-      best = cost;
-      best_s = s;
-    }
-  }
-  if (best_s == 1) return p;
-  p.dp_tiles = T - rem;
-  p.sk_tiles = rem;
-  p.sk_split = best_s;
-  const int units = rem * best_s;
-  p.grid = T - rem >= G ? G : (units < G ? units : G);
-  return p;
+  return wg3::plan_tiles(G, L.tiles_m, L.tiles_n, L.kt, allow_split);
 }
 
 // Scratch after the split operands: the partial sums of the split tiles, then
@@ -812,7 +701,38 @@ enum { EV_ENTRY = 0, EV_A_READY = 1, EV_PACKED = 2, EV_SLOT0 = 3, EV_SLOT1 = 4 }
 
 wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int transB, int64_t m, int64_t k,
                               float alpha, const float *A, int64_t lda, float beta, const int64_t *widths,
-                              size_t count, cudaEvent_t a_ready) {
+                              size_t count, cudaEvent_t a_ready, const float *B0, int64_t ldb) {
+  int64_t widest = 0;
+  for (size_t i = 0; i < count; i++) widest = widths[i] > widest ? widths[i] : widest;
+  const bool forced = d->sgemm_path >= WG_SGEMM_TF32X3_FUSED_BN256;
+  if (d->sgemm_path != WG_SGEMM_TF32X3_PACKED && widest > 0 &&
+      (forced || (double)m * (double)widest * (double)k <= WG_FUSED_MAX_WORK) &&
+      wg_tf32x3_fused_supported(d, transA, transB, m, widest, k, A, lda, B0, ldb)) {
+    size_t bytes = 0;
+    for (size_t i = 0; i < count; i++) {
+      const size_t b = wg_tf32x3_fused_workspace(d, m, widths[i], k);
+      bytes = b > bytes ? b : bytes;
+    }
+    void *ws = nullptr;
+    wg_status st = wg_workspace(d, bytes, &ws);
+    if (st != WG_OK) return st;
+    *p = wg_tc_product{};
+    p->d = d;
+    p->transA = transA;
+    p->transB = transB;
+    p->m = m;
+    p->k = k;
+    p->alpha = alpha;
+    p->beta = beta;
+    p->A = A;
+    p->lda = lda;
+    p->ws = static_cast<char *>(ws);
+    p->fused = true;
+    p->ws_bytes = bytes;
+    if (a_ready) WG_CUDA(cudaStreamWaitEvent(d->stream, a_ready, 0));
+    d->stats.calls++;
+    return WG_OK;
+  }
   const ProductLayout P = product_layout(d->sm_count, m, k, widths, count);
   void *ws = nullptr;
   wg_status st = wg_workspace(d, P.total, &ws);
@@ -835,6 +755,8 @@ wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int tr
   p->partial_room = P.partial_room;
   p->counter_room = P.counter_room;
   p->panels = 0;
+  p->fused = false;
+  p->ws_bytes = 0;
   // The splits run on the side stream after everything queued so far on the
   // device stream (earlier users of the workspace) and after op(A) is in place.
   WG_CUDA(cudaEventRecord(d->tc_ev[EV_ENTRY], d->stream));
@@ -855,6 +777,15 @@ wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int tr
 wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, int64_t ldb, float *C, int64_t ldc,
                               cudaEvent_t b_ready) {
   wg_device *d = p->d;
+  if (p->fused) {
+    if (b_ready) WG_CUDA(cudaStreamWaitEvent(d->stream, b_ready, 0));
+    wg_status st = wg_sgemm_tf32x3_fused(d, d->stream, p->transA, p->transB, p->m, cols, p->k, p->alpha, p->A, p->lda,
+                                         B, ldb, p->beta, C, ldc, p->ws, p->ws_bytes);
+    if (st != WG_OK) return st;
+    d->stats.tf32x3_launches++;
+    p->panels++;
+    return WG_OK;
+  }
   const int slot = (int)(p->panels & 1);
   const Layout L = layout_of(p->m, cols, p->k);
   float *ahi = reinterpret_cast<float *>(p->ws);
@@ -885,7 +816,7 @@ wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, in
 
 void wg_tc_product_join(wg_tc_product *p) {
   wg_device *d = p->d;
-  if (!d || !d->side) return;
+  if (!d || p->fused || !d->side) return;
   if (cudaEventRecord(d->tc_ev[EV_PACKED], d->side) == cudaSuccess)
     cudaStreamWaitEvent(d->stream, d->tc_ev[EV_PACKED], 0);
 }

@@ -613,7 +613,7 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
   wg_status st = WG_OK;
   if (tc)
     st = wg_tc_product_begin(&prod, d, transA, transB, m_local, k, (float)alpha, (const float *)A, lda, (float)beta,
-                             widths.data(), widths.size(), nullptr);
+                             widths.data(), widths.size(), nullptr, (const float *)Bsrc, ldb);
   int64_t j0 = 0;
   for (size_t j = 0; st == WG_OK && j < widths.size(); j++) {
     const int64_t cols = widths[j];
