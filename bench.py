@@ -10,6 +10,8 @@ counted as the reference counts them, 2*m*n*k + 2*m*n
 Workloads:
   sgemm4096   configs[1]: sgemm 4096^3 column-major TN, alpha=1, beta=0, A,B ~ N(0,1), C=0
               (the default at N=1)
+  sgemm2048   sgemm 2048^3 NN, U[-1,1] (a mid-size shape for profiling single kernels)
+  dgemm2048   the same for dgemm
   dgemm4096   configs[2]: dgemm 4096^3 column-major NT, alpha=-0.75, beta=1.25, U[-1,1]
   sgemm512    configs[0]: sgemm 512^3 NN, alpha=1.5, beta=0.5, U[-1,1]
   ragged      configs[3]: sgemm 1000x1023x777, lda=1024 ldb=800 ldc=1040, NN
@@ -65,6 +67,10 @@ WORKLOADS = {
                        lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
     "shard16384d": dict(routine="dgemm", config_index=4, transA=0, transB=0, m=16384, n=16384, k=16384,
                         lda=16384, ldb=16384, ldc=16384, alpha=1.0, beta=1.0, data="uniform", sharded=True),
+    "sgemm2048": dict(routine="sgemm", config_index=None, transA=0, transB=0, m=2048, n=2048, k=2048,
+                      lda=2048, ldb=2048, ldc=2048, alpha=1.0, beta=0.5, data="uniform"),
+    "dgemm2048": dict(routine="dgemm", config_index=None, transA=0, transB=0, m=2048, n=2048, k=2048,
+                      lda=2048, ldb=2048, ldc=2048, alpha=1.0, beta=0.5, data="uniform"),
     # The gemmtr family at the reference's own benchmark shape (benchmarks/sgemmtr/wgblas/sgemmtr.js,
     # benchmarks/ssyrk/wgblas/ssyrk.js: m = n = k, lower, alpha 1, beta 0), counted as it counts them.
     "sgemmtr4096": dict(routine="sgemm", config_index=None, transA=0, transB=0, m=4096, n=4096, k=4096,
@@ -81,7 +87,7 @@ PANEL_COLS = 0  # B broadcast panels of the sharded workloads: 0 = the library's
 # step with those files).
 NCU_TRAFFIC = {
     ("sgemm4096", "sgemm_tf32x3_mma"): (623.8e6, 63.2e6, "profiles/sgemm_tf32x3_4096_TN.md"),
-    ("dgemm4096", "dgemm_dmma"): (1231.7e6, 120.5e6, "profiles/dgemm_dmma_4096_NT.md"),
+    ("dgemm4096", "dgemm_dmma"): (1233.8e6, 122.7e6, "profiles/dgemm_dmma_4096_NT.md"),
 }
 
 
@@ -881,6 +887,10 @@ def main():
     p.add_argument("--workload", choices=["auto"] + sorted(WORKLOADS), default="auto")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extra", action="store_true", help="skip the secondary workloads and probes")
+    p.add_argument("--sgemm-path", default="auto",
+                   help="force an sgemm kernel (Device.set_sgemm_path: simt, tf32x3, tf32x3_packed, "
+                        "tf32x3_fused_bn256/128/64) for profiling one kernel; the default picks by shape")
+    p.add_argument("--dgemm-path", default="auto", help="force a dgemm kernel (simt or dmma) for profiling")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -893,6 +903,8 @@ def main():
     import wgblas_b200 as wg
 
     dev = wg.init(device=local)
+    dev.set_sgemm_path(args.sgemm_path)
+    dev.set_dgemm_path(args.dgemm_path)
     torch.cuda.set_device(local)
     wname = pick_workload(args, world)
     w = WORKLOADS[wname]

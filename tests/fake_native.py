@@ -31,6 +31,35 @@ class FakeLib:
             return getattr(self._real, name)
         raise AttributeError(f"the fake library has no {name}")
 
+    # ---- devices (init / cleanup / gpuName tests) ----------------------------
+
+    n_devices = 2
+    opened = 0
+    closed = 0
+
+    def wg_device_count(self, ref):
+        ref._obj.value = self.n_devices
+        return 0
+
+    def wg_device_open(self, ordinal, flags, ref):
+        self._next += 16
+        ref._obj.value = self._next
+        self.opened += 1
+        return 0
+
+    def wg_device_close(self, dev):
+        self.closed += 1
+        return 0
+
+    def wg_device_name(self, dev, buf, size):
+        ct.memmove(buf, b"Fake B200\0", 10)
+        return 0
+
+    def wg_device_props_get(self, dev, ref):
+        p = ref._obj
+        p.ordinal, p.sm_count, p.cc_major, p.cc_minor, p.total_mem, p.flags = 0, 148, 10, 0, 183 << 30, 0
+        return 0
+
     # ---- buffers -------------------------------------------------------------
 
     def _key(self, b):

@@ -27,17 +27,35 @@ class Error(Exception):
     """Raised with the reference's error messages (its ``throw new Error(msg)``)."""
 
 
+class Adapter:
+    """What the reference's GPUAdapter stands for here: the CUDA device behind a
+    handle (src/init.mjs:153-168 hands it out through getAdapter). ``info``
+    holds the fields gpuName reads (``description``, ``device``) plus the
+    vendor and architecture; ``limits`` the device's SM count and memory."""
+
+    __slots__ = ("ordinal", "info", "limits")
+
+    def __init__(self, ordinal: int, info: dict, limits: dict):
+        self.ordinal = ordinal
+        self.info = info
+        self.limits = limits
+
+    def __repr__(self):
+        return f"<wgblas Adapter cuda:{self.ordinal} {self.info.get('device', '')}>"
+
+
 class Device:
     """A CUDA device handle: the counterpart of the reference's GPUDevice."""
 
-    __slots__ = ("_handle", "ordinal", "benchmark", "options", "_name", "__weakref__")
+    __slots__ = ("_handle", "ordinal", "benchmark", "options", "_name", "adapter", "__weakref__")
 
-    def __init__(self, handle, ordinal, benchmark, options, name):
+    def __init__(self, handle, ordinal, benchmark, options, name, adapter=None):
         self._handle = handle
         self.ordinal = ordinal
         self.benchmark = benchmark
         self.options = options
         self._name = name
+        self.adapter = adapter
 
     @property
     def handle(self):
@@ -167,7 +185,13 @@ def init(powerPreference: str = "high-performance", benchmark: bool = False,
     nat.check(nat.lib.wg_device_open(ordinal, nat.WG_DEVICE_TIMING if benchmark else 0, ct.byref(h)))
     buf = ct.create_string_buffer(256)
     nat.check(nat.lib.wg_device_name(h, buf, 256))
-    dev = Device(h, ordinal, bool(benchmark), options, buf.value.decode())
+    name = buf.value.decode()
+    p = nat.DeviceProps()
+    nat.check(nat.lib.wg_device_props_get(h, ct.byref(p)))
+    adapter = Adapter(ordinal, {"vendor": "nvidia", "architecture": f"sm_{p.cc_major}{p.cc_minor}",
+                                "device": name, "description": f"cuda:{ordinal}"},
+                      {"smCount": int(p.sm_count), "totalMemory": int(p.total_mem)})
+    dev = Device(h, ordinal, bool(benchmark), options, name, adapter)
     _devices[key] = dev
     if _primary is None:
         _primary = dev
@@ -201,12 +225,18 @@ def _close(d: Device) -> None:
         d._handle = None
 
 
+def _registered(device) -> bool:
+    return isinstance(device, Device) and not device.destroyed and any(v is device for v in _devices.values())
+
+
 def gpuName(device: Device | None = None) -> dict:
-    """``{description, device}`` for a device (src/init.mjs:133-143)."""
+    """``{description, device}`` for a device, from its adapter's info, each
+    "unknown" when empty (src/init.mjs:133-143)."""
     device = _primary if device is None else device
-    if not isinstance(device, Device) or device.destroyed or device not in _devices.values():
+    if not _registered(device):
         raise Error("CUDA device not initialized — call init() first.")
-    return {"description": f"cuda:{device.ordinal}", "device": device._name or "unknown"}
+    info = device.adapter.info if device.adapter is not None else {}
+    return {"description": info.get("description") or "unknown", "device": info.get("device") or "unknown"}
 
 
 def getDevice() -> Device:
@@ -216,9 +246,19 @@ def getDevice() -> Device:
     return _primary
 
 
-def isBenchmarkEnabled(device: Device | None = None) -> bool:
+def getAdapter(device: Device | None = None) -> Adapter:
+    """The adapter behind ``device``, by default the primary one (src/init.mjs:170-182)."""
     device = _primary if device is None else device
-    return bool(device is not None and not device.destroyed and device.benchmark)
+    if not _registered(device) or device.adapter is None:
+        raise Error("CUDA adapter not initialized — call init() first.")
+    return device.adapter
+
+
+def isBenchmarkEnabled(device: Device | None = None) -> bool:
+    """Whether ``device`` (by default the primary one) was created with
+    benchmark=True; False for anything init() did not hand out (src/init.mjs:153-155)."""
+    device = _primary if device is None else device
+    return bool(_registered(device) and device.benchmark)
 
 
 def require_gpu_device(device) -> None:

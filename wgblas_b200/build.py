@@ -50,7 +50,28 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise subprocess.CalledProcessError(1, failed[0])
     if force or _stale(LIB, objs):
         subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-ldl"], check=True)
+    build_napi(force)
     return LIB
+
+
+NAPI_SRC = os.path.join(HERE, "napi", "wgblas_napi.c")
+NAPI_ADDON = os.path.join(HERE, "napi", "wgblas_napi.node")
+CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
+
+
+def napi_command(out: str) -> list[str]:
+    """gcc command line of the Node-API addon (Node resolves its napi_* symbols at load)."""
+    return ["gcc", "-std=c11", "-O2", "-Wall", "-Wextra", "-Werror", "-shared", "-fPIC", "-fvisibility=hidden",
+            "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(CUDA_HOME, "include"), NAPI_SRC,
+            "-L" + HERE, "-lwgblas_b200", "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcudart",
+            "-Wl,-rpath,$ORIGIN/..", "-o", out]
+
+
+def build_napi(force: bool = False) -> str:
+    """Builds wgblas_napi.node next to its source (the JavaScript shim in napi/js loads it)."""
+    if force or _stale(NAPI_ADDON, [NAPI_SRC, LIB, os.path.join(ROOT, "include", "wgblas.h")]):
+        subprocess.run(napi_command(NAPI_ADDON), check=True)
+    return NAPI_ADDON
 
 
 if __name__ == "__main__":
