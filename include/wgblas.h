@@ -138,7 +138,8 @@ wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_t k, wg_tc_
  * kernel that splits its own operands where the operands' alignment allows its
  * tensor maps, else the split pass + MMA kernel); TF32X3_PACKED forces the
  * split pass + MMA kernel; TF32X3_FUSED_BN256/128/64 force the fused kernel
- * with one tile width (it must be supported for the call). */
+ * with one tile width and TF32X3_PAIR its CTA-pair form (they must be
+ * supported for the call). */
 #define WG_SGEMM_AUTO 0
 #define WG_SGEMM_SIMT 1
 #define WG_SGEMM_TF32X3 2
@@ -146,6 +147,7 @@ wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_t k, wg_tc_
 #define WG_SGEMM_TF32X3_FUSED_BN256 4
 #define WG_SGEMM_TF32X3_FUSED_BN128 5
 #define WG_SGEMM_TF32X3_FUSED_BN64 6
+#define WG_SGEMM_TF32X3_PAIR 7  /* the fused kernel over CTA pairs (256 x 256 tiles) */
 wg_status wg_device_set_sgemm_path(wg_device *dev, int path);
 /* dgemm kernel choice: AUTO picks by shape; SIMT forces the DFMA kernel (one
  * sequential FMA chain per element), DMMA the FP64 tensor-core kernel. */

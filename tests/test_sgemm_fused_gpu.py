@@ -14,7 +14,7 @@ from gemm_check import check_sgemm, ieee_match
 
 pytestmark = pytest.mark.gpu
 T, N = "transpose", "no-transpose"
-WIDTHS = ["tf32x3_fused_bn256", "tf32x3_fused_bn128", "tf32x3_fused_bn64"]
+WIDTHS = ["tf32x3_fused_bn256", "tf32x3_fused_bn128", "tf32x3_fused_bn64", "tf32x3_pair"]
 
 
 @pytest.fixture

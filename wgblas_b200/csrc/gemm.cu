@@ -97,12 +97,29 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
   } else if (path == WG_SGEMM_AUTO) {
     tc = wg_tf32x3_supported(d, m, n, k) && k >= 64 && (double)m * (double)n >= 256.0 * 256.0;
   }
-  const bool fused = tc && path != WG_SGEMM_TF32X3_PACKED &&
-                     (path >= WG_SGEMM_TF32X3_FUSED_BN256 || (double)m * (double)n * (double)k <= WG_FUSED_MAX_WORK) &&
-                     wg_tf32x3_fused_supported(d, transA, transB, m, n, k, A, lda, B, ldb);
-  if (path >= WG_SGEMM_TF32X3_FUSED_BN256 && !fused)
+  const bool aligned = tc && path != WG_SGEMM_TF32X3_PACKED &&
+                       wg_tf32x3_fused_supported(d, transA, transB, m, n, k, A, lda, B, ldb);
+  const bool small = (double)m * (double)n * (double)k <= WG_FUSED_MAX_WORK;
+  const bool forced_fused = path >= WG_SGEMM_TF32X3_FUSED_BN256 && path <= WG_SGEMM_TF32X3_FUSED_BN64;
+  // Above WG_FUSED_MAX_WORK the split pass + MMA kernel is the faster path (the
+  // in-kernel split of either fused form is latency-bound there); the pair form
+  // runs only when asked for.
+  const bool pair = aligned && path == WG_SGEMM_TF32X3_PAIR;
+  const bool fused = aligned && !pair && (forced_fused || small);
+  if ((forced_fused || path == WG_SGEMM_TF32X3_PAIR) && !aligned)
     return wg_fail(WG_ERR_NOT_SUPPORTED, "the fused 3xTF32 kernel needs 16-byte aligned A and B and lda, ldb "
                    "multiples of 4");
+  if (pair) {
+    void *ws = nullptr;
+    const size_t bytes = wg_tf32x3_pair_workspace(d, m, n, k);
+    wg_status st = wg_workspace(d, bytes, &ws);
+    if (st != WG_OK) return st;
+    st = wg_sgemm_tf32x3_pair(d, d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ws, bytes,
+                              uplo);
+    if (st != WG_OK) return st;
+    d->stats.tf32x3_launches++;
+    return WG_OK;
+  }
   if (fused) {
     void *ws = nullptr;
     const size_t bytes = wg_tf32x3_fused_workspace(d, m, n, k);

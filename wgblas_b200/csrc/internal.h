@@ -242,6 +242,15 @@ bool wg_tf32x3_fused_supported(const wg_device *d, int transA, int transB, int64
                                const float *A, int64_t lda, const float *B, int64_t ldb);
 // Scratch one fused call needs (split-K partial sums, counters, tile flags).
 size_t wg_tf32x3_fused_workspace(const wg_device *d, int64_t m, int64_t n, int64_t k);
+// The CTA-pair form of the fused kernel (256 x 256 tiles, tcgen05 cta_group::2):
+// its scratch, and the call (the kernel and its gated FFMA fallback on stream
+// st). Same support rule as the fused kernel; runs when WG_SGEMM_TF32X3_PAIR is
+// set (measured on B200 at 4096^3: 1.02 ms, against 0.82 ms for the one-CTA
+// fused kernel and 0.61 ms for the split pass + MMA kernel).
+size_t wg_tf32x3_pair_workspace(const wg_device *d, int64_t m, int64_t n, int64_t k);
+wg_status wg_sgemm_tf32x3_pair(wg_device *d, cudaStream_t st, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                               float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                               float *C, int64_t ldc, void *ws, size_t ws_bytes, int uplo = 0);
 // Queues the fused kernel and its gated FFMA fallback on stream st.
 wg_status wg_sgemm_tf32x3_fused(wg_device *d, cudaStream_t st, int transA, int transB, int64_t m, int64_t n,
                                 int64_t k, float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,

@@ -270,7 +270,7 @@ extern "C" wg_status wg_device_set_dgemm_path(wg_device *d, int path) {
 
 extern "C" wg_status wg_device_set_sgemm_path(wg_device *d, int path) {
   if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
-  if (path < WG_SGEMM_AUTO || path > WG_SGEMM_TF32X3_FUSED_BN64)
+  if (path < WG_SGEMM_AUTO || path > WG_SGEMM_TF32X3_PAIR)
     return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown sgemm path %d", path);
   d->sgemm_path = path;
   d->fused_bn = path == WG_SGEMM_TF32X3_FUSED_BN256 ? 256

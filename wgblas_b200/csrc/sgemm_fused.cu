@@ -85,8 +85,15 @@ struct FArgs {
   int uplo;
 };
 
+// True when x is outside the split's exact range (wg3::split_ok, on the bits:
+// |x| as an integer is 0, or within [2^-50, 2^50]; NaN and Inf are above).
+__device__ __forceinline__ bool ruled_out(float x) {
+  const uint32_t a = __float_as_uint(x) & 0x7FFFFFFFu;
+  return (a != 0u) & (a - 0x26800000u > 0x32000000u);
+}
+
 __device__ __forceinline__ void split4(const float4 x, float4 &h, float4 &l, bool &bad) {
-  bad |= !wg3::split_ok(x.x) | !wg3::split_ok(x.y) | !wg3::split_ok(x.z) | !wg3::split_ok(x.w);
+  bad |= ruled_out(x.x) | ruled_out(x.y) | ruled_out(x.z) | ruled_out(x.w);
   h.x = wg3::rna_tf32(x.x);
   h.y = wg3::rna_tf32(x.y);
   h.z = wg3::rna_tf32(x.z);
@@ -176,9 +183,12 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
     }
     for (int i = 0; i < UQ; i++) {
       wgtc::mbar_init(&uq_full[i], 1);
-      wgtc::mbar_init(&uq_empty[i], 3);
+      wgtc::mbar_init(&uq_empty[i], 2 + XF_WARPS);  // MMA issuer, epilogue, each split warp
     }
-    for (int i = 0; i < BADQ; i++) wgtc::mbar_init(&unit_done[i], 1);
+    for (int i = 0; i < BADQ; i++) {
+      wgtc::mbar_init(&unit_done[i], XF_WARPS);
+      unit_bad[i] = 0;
+    }
     *abort_flag = 0;
     wgtc::fence_barrier_init();
   }
@@ -303,19 +313,22 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
       }
     }
   } else if (warp >= 6) {
-    // ---- split: raw fp32 slices -> hi / lo operand tiles ----
+    // ---- split: raw fp32 slices -> hi / lo operand tiles. Each warp works on
+    // its share of every slice and signals on its own (the barriers count the
+    // warps), so no warp waits for another. ----
     const int xt = threadIdx.x - 192;
     int64_t g = 0, h = 0;
     for (int n = 0;; n++) {
       const int slot = n % UQ;
       const bool got = wgtc::mbar_wait_bounded(&uq_full[slot], (uint32_t)(n / UQ) & 1u, WAIT_BUDGET);
       const int un = got ? uq[slot] : -1;
-      if (!wg3::group_all<3, XF_THREADS>(got && *abort_flag == 0)) {
+      if (!__all_sync(0xffffffffu, got && *abort_flag == 0)) {
         if (!got) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
         *abort_flag = 1;
         break;
       }
-      if (xt == 0) wg3::mbar_arrive(&uq_empty[slot]);
+      __syncwarp();
+      if (lane == 0) wg3::mbar_arrive(&uq_empty[slot]);
       if (un < 0) break;
       const wg3::Unit u = wg3::decode(args, un);
       bool bad = false, failed = false;
@@ -323,7 +336,7 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
         const int s = (int)(g % SR), c = (int)(h % SC);
         const bool okr = wgtc::mbar_wait_bounded(&raw_full[s], (uint32_t)(g / SR) & 1u, WAIT_BUDGET);
         const bool okc = wgtc::mbar_wait_bounded(&comp_empty[c], ((uint32_t)(h / SC) & 1u) ^ 1u, WAIT_BUDGET);
-        if (!wg3::group_all<3, XF_THREADS>(okr && okc && *abort_flag == 0)) {
+        if (!__all_sync(0xffffffffu, okr && okc && *abort_flag == 0)) {
           if (!(okr && okc)) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
           *abort_flag = 1;
           failed = true;
@@ -341,11 +354,9 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
         }
       }
       if (failed) break;
-      const bool any_bad = wg3::group_any<3, XF_THREADS>(bad);
-      if (xt == 0) {
-        unit_bad[n % BADQ] = any_bad ? 1 : 0;
-        wg3::mbar_arrive(&unit_done[n % BADQ]);
-      }
+      if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(const_cast<int *>(&unit_bad[n % BADQ]), 1);
+      __syncwarp();
+      if (lane == 0) wg3::mbar_arrive(&unit_done[n % BADQ]);
     }
   } else {
     // ---- epilogue: TMEM -> registers -> C (or a partial-sum slot) ----
@@ -375,6 +386,8 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
       }
       wgtc::tc_fence_after();
       const bool bad = unit_bad[n % BADQ] != 0;
+      wg3::epi_bar();  // every thread has read the word before it is cleared for unit n + BADQ
+      if (threadIdx.x == 64) unit_bad[n % BADQ] = 0;
       int tm, tn;
       wg3::raster(args, u.t, tm, tn);
       const int64_t row = (int64_t)tm * BM + row_in_tile;
@@ -497,6 +510,384 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
   }
 }
 
+// ---- the CTA-pair form (cta_group::2) ---------------------------------------
+//
+// The same split-in-kernel 3xTF32 product over pairs of CTAs on neighbouring
+// SMs (a cluster of two). A pair owns 256 x 256 tiles of C: each CTA loads and
+// splits its 128 rows of op(A) and 128 of the tile's 256 rows of op(B), and one
+// thread of the first CTA issues tcgen05.mma.cta_group::2 (M = 256, N = 256),
+// which reads the A and B halves of both CTAs and leaves each CTA's 128 rows of
+// the tile in that CTA's TMEM. Per SM and 16-deep k-block that is 16 KB of TMA
+// traffic, 48 KB written by the split and 48 KB read by the MMAs, against 24,
+// 48 and 72 KB for a single CTA holding a 128 x 256 tile: the pair fits the
+// split inside the shared-memory bandwidth the MMAs leave.
+//
+// Work is scheduled statically (unit u of the decode order goes to pair
+// u mod pairs), so both CTAs walk the same units without a queue between them.
+// Synchronisation across the pair: each CTA's split warps arrive on the first
+// CTA's operand-ready barrier (remotely from the second CTA); the MMA commits
+// multicast to both CTAs' operand-free and accumulator-ready barriers; both
+// epilogues arrive on the first CTA's accumulator-free barrier; each split
+// announces per unit whether its operands were ruled out to both CTAs. Every
+// wait is clock-bounded; both CTAs reach the closing cluster barrier on every
+// path.
+
+constexpr int P_BN = 256;                  // tile columns of a pair (128 B rows per CTA)
+constexpr int P_HALF = P_BN / 2;
+constexpr int P_A = BM * 16 * 4;           // 8 KB: one CTA's k-slice of op(A)
+constexpr int P_B = P_HALF * 16 * 4;       // 8 KB: one CTA's k-slice of op(B)
+constexpr int P_RAW = P_A + P_B, P_COMP = 2 * P_RAW;
+constexpr int P_SR = 4, P_SC = 4;
+constexpr size_t P_SMEM = 1024 + (size_t)P_SR * P_RAW + (size_t)P_SC * P_COMP + 1024;
+static_assert(P_SMEM <= 227 * 1024, "shared memory per CTA");
+
+template <int A_K, int B_K>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F_THREADS, 1)
+tf32x3_fused_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                  const FArgs args) {
+  constexpr int BK = 16, SR = P_SR, SC = P_SC;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = wgtc::smem_addr(smem_raw);
+  uint8_t *smem = smem_raw + ((1024 - (base & 1023)) & 1023);
+  uint8_t *raw = smem;
+  uint8_t *comp = smem + (size_t)SR * P_RAW;
+  uint64_t *raw_full = reinterpret_cast<uint64_t *>(comp + (size_t)SC * P_COMP);
+  uint64_t *raw_empty = raw_full + SR;
+  uint64_t *comp_full = raw_empty + SR;   // first CTA: both CTAs' split warps arrive
+  uint64_t *comp_empty = comp_full + SC;  // both CTAs: the MMA's multicast commit
+  uint64_t *acc_full = comp_empty + SC;   // [2], both CTAs: the MMA's multicast commit
+  uint64_t *acc_empty = acc_full + 2;     // [2], first CTA: both CTAs' epilogue threads
+  uint64_t *unit_done = acc_empty + 2;    // [BADQ], both CTAs: both splits arrive
+  volatile unsigned *unit_bad = reinterpret_cast<volatile unsigned *>(unit_done + BADQ);  // [BADQ]
+  uint32_t *tmem_slot = const_cast<uint32_t *>(reinterpret_cast<volatile uint32_t *>(unit_bad + BADQ));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile unsigned *last_flag = reinterpret_cast<volatile unsigned *>(tmem_slot + 2);
+  volatile unsigned *seg_bad = reinterpret_cast<volatile unsigned *>(tmem_slot + 3);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = wgtc::cluster_ctarank();
+  const int pair = (int)(blockIdx.x >> 1), pairs = (int)(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SR; s++) {
+      wgtc::mbar_init(&raw_full[s], 1);
+      wgtc::mbar_init(&raw_empty[s], XF_WARPS);
+    }
+    for (int s = 0; s < SC; s++) {
+      wgtc::mbar_init(&comp_full[s], 2 * XF_WARPS);
+      wgtc::mbar_init(&comp_empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      wgtc::mbar_init(&acc_full[b], 1);
+      wgtc::mbar_init(&acc_empty[b], 2 * 32 * wg3::EPI_WARPS);
+    }
+    for (int i = 0; i < BADQ; i++) {
+      wgtc::mbar_init(&unit_done[i], 2 * XF_WARPS);  // every split warp of both CTAs
+      unit_bad[i] = 0;
+    }
+    *abort_flag = 0;
+    wgtc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    wgtc::prefetch_tensormap(&map_a);
+    wgtc::prefetch_tensormap(&map_b);
+  }
+  if (warp == 1) {
+    wgtc::tmem_alloc_pair(tmem_slot, 2 * P_BN);
+    wgtc::tmem_relinquish_pair();
+  }
+  wgtc::tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  wgtc::cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  wgtc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // The pair's units, in order: u = pair, pair + pairs, ... (gemmtr skips the
+  // tiles with no element in the triangle; both CTAs skip the same ones).
+  auto next_unit = [&](int u) -> int {
+    for (u += pairs; u < args.units; u += pairs) {
+      if (args.uplo == WG_UPLO_FULL) return u;
+      int tm0, tn0;
+      wg3::raster(args, wg3::decode(args, u).t, tm0, tn0);
+      if (!wg_tile_outside(args.uplo, (int64_t)tm0 * 2 * BM, 2 * BM, (int64_t)tn0 * P_BN, P_BN)) return u;
+    }
+    return args.units;
+  };
+  const int first = next_unit(pair - pairs);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer: this CTA's halves of each k-slice ----
+      int64_t g = 0;
+      bool ok = true;
+      for (int un = first; ok && un < args.units; un = next_unit(un)) {
+        const wg3::Unit u = wg3::decode(args, un);
+        int tm, tn;
+        wg3::raster(args, u.t, tm, tn);
+        const int row_a = tm * 2 * BM + (int)rank * BM, row_b = tn * P_BN + (int)rank * P_HALF;
+        for (int kb = u.kb0; kb < u.kb1; kb++, g++) {
+          const int s = (int)(g % SR);
+          if (!wgtc::mbar_wait_bounded(&raw_empty[s], ((uint32_t)(g / SR) & 1u) ^ 1u, WAIT_BUDGET) || *abort_flag) {
+            atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t *st = raw + (size_t)s * P_RAW;
+          wgtc::mbar_arrive_expect_tx(&raw_full[s], P_RAW);
+          const int kc = kb * BK;
+          if (A_K)
+            wgtc::tma_load_2d(st, &map_a, &raw_full[s], kc, row_a);
+          else
+            wgtc::tma_load_2d(st, &map_a, &raw_full[s], row_a, kc);
+          if (B_K)
+            wgtc::tma_load_2d(st + P_A, &map_b, &raw_full[s], kc, row_b);
+          else
+            wgtc::tma_load_2d(st + P_A, &map_b, &raw_full[s], row_b, kc);
+        }
+      }
+      for (int64_t q = g - SR > 0 ? g - SR : 0; q < g; q++)
+        wgtc::mbar_wait_bounded(&raw_full[q % SR], (uint32_t)(q / SR) & 1u, WAIT_BUDGET);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---- MMA issuer of the pair ----
+      constexpr uint32_t idesc = wgtc::idesc_tf32(2 * BM, P_BN);
+      int64_t h = 0;
+      int it = 0;
+      bool ok = true;
+      for (int un = first; ok && un < args.units; un = next_unit(un), it++) {
+        const wg3::Unit u = wg3::decode(args, un);
+        const int b = it & 1;
+        const uint32_t use = (uint32_t)(it >> 1);
+        if (!wgtc::mbar_wait_bounded_cluster(&acc_empty[b], (use & 1u) ^ 1u, WAIT_BUDGET) || *abort_flag) {
+          atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+          *abort_flag = 1;
+          break;
+        }
+        wgtc::tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(b * P_BN);
+        for (int kb = u.kb0; kb < u.kb1; kb++, h++) {
+          const int c = (int)(h % SC);
+          if (!wgtc::mbar_wait_bounded_cluster(&comp_full[c], (uint32_t)(h / SC) & 1u, WAIT_BUDGET) ||
+              *abort_flag) {
+            atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          wgtc::tc_fence_after();
+          const uint32_t st = wgtc::smem_addr(comp + (size_t)c * P_COMP);
+          const uint32_t a_hi = st, a_lo = st + P_A, b_hi = st + 2 * P_A, b_lo = b_hi + P_B;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; kk++) {
+            const uint32_t off = kk * 32;
+            const uint64_t dah = wgtc::smem_desc_kmajor(a_hi + off, 64);
+            const uint64_t dal = wgtc::smem_desc_kmajor(a_lo + off, 64);
+            const uint64_t dbh = wgtc::smem_desc_kmajor(b_hi + off, 64);
+            const uint64_t dbl = wgtc::smem_desc_kmajor(b_lo + off, 64);
+            const uint32_t acc0 = (kb > u.kb0 || kk > 0) ? 1u : 0u;
+            wgtc::mma_tf32_pair(d_tmem, dal, dbh, idesc, acc0);
+            wgtc::mma_tf32_pair(d_tmem, dah, dbl, idesc, 1u);
+            wgtc::mma_tf32_pair(d_tmem, dah, dbh, idesc, 1u);
+          }
+          wgtc::mma_commit_pair(&comp_empty[c], 0x3);  // both CTAs may refill stage c
+        }
+        if (!ok) break;
+        wgtc::mma_commit_pair(&acc_full[b], 0x3);  // both CTAs' rows of the tile are complete
+      }
+    }
+  } else if (warp >= 6) {
+    // ---- split: this CTA's raw halves -> hi / lo operand tiles (each warp on its
+    // own share, signalling on its own) ----
+    const int xt = threadIdx.x - 192;
+    const uint32_t comp_full_first = wgtc::mapa_shared(wgtc::smem_addr(comp_full), 0);
+    const uint32_t peer = rank ^ 1u;
+    int64_t g = 0, h = 0;
+    int it = 0;
+    for (int un = first; un < args.units; un = next_unit(un), it++) {
+      const wg3::Unit u = wg3::decode(args, un);
+      bool bad = false, failed = false;
+      for (int kb = u.kb0; kb < u.kb1; kb++, g++, h++) {
+        const int s = (int)(g % SR), c = (int)(h % SC);
+        const bool okr = wgtc::mbar_wait_bounded(&raw_full[s], (uint32_t)(g / SR) & 1u, WAIT_BUDGET);
+        const bool okc =
+            wgtc::mbar_wait_bounded_cluster(&comp_empty[c], ((uint32_t)(h / SC) & 1u) ^ 1u, WAIT_BUDGET);
+        if (!__all_sync(0xffffffffu, okr && okc && *abort_flag == 0)) {
+          if (!(okr && okc)) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+          *abort_flag = 1;
+          failed = true;
+          break;
+        }
+        const uint8_t *rs = raw + (size_t)s * P_RAW;
+        uint8_t *cs = comp + (size_t)c * P_COMP;
+        bad |= split_slice<BM, A_K != 0>(rs, cs, cs + P_A, xt);
+        bad |= split_slice<P_HALF, B_K != 0>(rs + P_A, cs + 2 * P_A, cs + 2 * P_A + P_B, xt);
+        wgtc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          wgtc::mbar_arrive_cluster(comp_full_first + (uint32_t)(c * 8));
+          wg3::mbar_arrive(&raw_empty[s]);
+        }
+      }
+      if (failed) break;
+      const bool any_bad = __any_sync(0xffffffffu, bad);
+      if (lane == 0) {
+        const int q = it % BADQ;
+        if (any_bad) {
+          atomicOr(const_cast<unsigned *>(&unit_bad[q]), 1u);
+          wgtc::red_or_cluster(wgtc::mapa_shared(wgtc::smem_addr(const_cast<unsigned *>(&unit_bad[q])), peer), 1u);
+        }
+        wgtc::mbar_arrive_cluster(wgtc::mapa_shared(wgtc::smem_addr(&unit_done[q]), 0));
+        wgtc::mbar_arrive_cluster(wgtc::mapa_shared(wgtc::smem_addr(&unit_done[q]), 1));
+      }
+    }
+  } else if (warp >= 2) {
+    // ---- epilogue: this CTA's 128 rows of the pair's tile ----
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    const float alpha = args.alpha, beta = args.beta;
+    const uint32_t acc_empty_first = wgtc::mapa_shared(wgtc::smem_addr(acc_empty), 0);
+    const int tiles_m128 = 2 * args.tiles_m;
+    int it = 0;
+    for (int un = first; un < args.units; un = next_unit(un), it++) {
+      const wg3::Unit u = wg3::decode(args, un);
+      const int b = it & 1;
+      const uint32_t use = (uint32_t)(it >> 1);
+      const bool ready =
+          wgtc::mbar_wait_bounded_cluster(&acc_full[b], use & 1u, WAIT_BUDGET) &&
+          wgtc::mbar_wait_bounded_cluster(&unit_done[it % BADQ], (uint32_t)(it / BADQ) & 1u, WAIT_BUDGET);
+      if (!wg3::epi_all(ready && *abort_flag == 0)) {
+        if (!ready) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_MMA_WAIT);
+        *abort_flag = 1;
+        break;
+      }
+      wgtc::tc_fence_after();
+      const bool bad = unit_bad[it % BADQ] != 0;
+      wg3::epi_bar();  // every thread has read the word before it is cleared for unit it + BADQ
+      if (threadIdx.x == 64) unit_bad[it % BADQ] = 0;
+      int tm, tn;
+      wg3::raster(args, u.t, tm, tn);
+      const int half = tm * 2 + (int)rank;  // this CTA's 128-row block
+      const int64_t row = (int64_t)half * BM + row_in_tile;
+      const int64_t n0 = (int64_t)tn * P_BN;
+      const uint32_t trow = tmem + (uint32_t)(b * P_BN) + ((uint32_t)(q * 32) << 16);
+      const bool whole = u.seg < 0;
+      bool finish = whole, ruled_out = bad;
+      const int local = (u.t - args.dp_tiles) * 2 + (int)rank;  // split tile half
+      if (!whole) {
+        if (!bad) {
+          float *part = args.partials + ((int64_t)local * args.sk_split + u.seg) * P_BN * BM + row_in_tile;
+          for (int c = 0; c < P_BN; c += EC) {
+            uint32_t r[EC];
+            wgtc::tmem_ld_32x32b_x16(trow + (uint32_t)c, r);
+            wgtc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < EC; j++) part[(int64_t)(c + j) * BM] = __uint_as_float(r[j]);
+          }
+        }
+        if (bad && threadIdx.x == 64) atomicOr(args.tile_bad + local, 1u);
+        __threadfence();
+        wg3::epi_bar();
+        if (threadIdx.x == 64) {
+          const unsigned prev = atomicAdd(args.counters + local, 1u);
+          const bool last = prev == (unsigned)(args.sk_split - 1);
+          if (last) {
+            args.counters[local] = 0;
+            *seg_bad = atomicExch(args.tile_bad + local, 0u);
+          }
+          *last_flag = last ? 1u : 0u;
+          __threadfence();
+        }
+        wg3::epi_bar();
+        finish = *last_flag != 0;
+        if (finish) {
+          __threadfence();
+          ruled_out = *seg_bad != 0;
+        }
+      }
+      if (finish && ruled_out) {
+        if (threadIdx.x == 64) {
+          args.tile_flags[half + (int64_t)tn * tiles_m128] = args.epoch;
+          atomicExch(args.dwords + WG_DW_FALLBACK, args.epoch);
+        }
+      } else if (finish) {
+        const int nseg = whole ? 1 : args.sk_split;
+        const int own = whole ? 0 : u.seg;
+        const float *part0 = whole ? nullptr : args.partials + (int64_t)local * args.sk_split * P_BN * BM + row_in_tile;
+        const bool in_rows = row < args.m;
+        for (int c = 0; c < P_BN; c += EC) {
+          uint32_t r[EC];
+          wgtc::tmem_ld_32x32b_x16(trow + (uint32_t)c, r);
+          wgtc::tmem_ld_wait();
+          float acc[EC];
+#pragma unroll
+          for (int j = 0; j < EC; j++) acc[j] = __uint_as_float(r[j]);
+          if (nseg > 1) {
+            float sum[EC];
+            for (int g0 = 0; g0 < nseg; g0 += 2) {
+              float v[2][EC];
+#pragma unroll
+              for (int qq = 0; qq < 2; qq++) {
+                const int sgi = g0 + qq;
+                if (sgi < nseg && sgi != own) {
+                  const float *p = part0 + ((int64_t)sgi * P_BN + c) * BM;
+#pragma unroll
+                  for (int j = 0; j < EC; j++) v[qq][j] = __ldcg(p + (int64_t)j * BM);
+                }
+              }
+#pragma unroll
+              for (int qq = 0; qq < 2; qq++) {
+                const int sgi = g0 + qq;
+                if (sgi < nseg) {
+#pragma unroll
+                  for (int j = 0; j < EC; j++) {
+                    const float x = sgi == own ? acc[j] : v[qq][j];
+                    sum[j] = sgi == 0 ? x : sum[j] + x;
+                  }
+                }
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < EC; j++) acc[j] = sum[j];
+          }
+          if (in_rows) {
+            float old[EC];
+            if (beta != 0.0f) {
+#pragma unroll
+              for (int j = 0; j < EC; j++) {
+                const int64_t col = n0 + c + j;
+                old[j] = col < args.n && wg_in_triangle(args.uplo, row, col) ? args.C[row + col * args.ldc] : 0.0f;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < EC; j++) {
+              const int64_t col = n0 + c + j;
+              if (col < args.n && wg_in_triangle(args.uplo, row, col)) {
+                const float sv = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc[j]);
+                args.C[row + col * args.ldc] = (beta != 0.0f) ? __fmaf_rn(beta, old[j], sv) : sv;
+              }
+            }
+          }
+        }
+      }
+      wgtc::tc_fence_before();
+      wgtc::mbar_arrive_cluster(acc_empty_first + (uint32_t)(b * 8));  // this CTA's rows are drained
+    }
+  }
+
+  wgtc::tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  wgtc::cluster_sync();  // no remote arrival or pair MMA is outstanding past this point
+  if (warp == 1) {
+    __syncwarp();
+    wgtc::tc_fence_after();
+    wgtc::tmem_dealloc_pair(tmem, 2 * P_BN);
+  }
+}
+
 // ---- host side ------------------------------------------------------------
 
 // Tensor map of op(A) (rows = m) or of op(B) as its N x K operand (rows = n):
@@ -594,7 +985,73 @@ cudaError_t launch_bn(cudaStream_t st, int grid, bool a_k, bool b_k, const CUten
   return cudaGetLastError();
 }
 
+// The pair kernel's plan: 256 x 256 tiles over sm_count / 2 pairs.
+FLayout pair_layout_of(int G, int64_t m, int64_t n, int64_t k, bool allow_split) {
+  FLayout L;
+  L.bn = P_BN;
+  L.tiles_m = (int)((m + 2 * BM - 1) / (2 * BM));
+  L.tiles_n = (int)((n + P_BN - 1) / P_BN);
+  L.kt = (int)((k + 15) / 16);
+  L.plan = wg3::plan_tiles(G / 2 > 0 ? G / 2 : 1, L.tiles_m, L.tiles_n, L.kt, allow_split);
+  return L;
+}
+
+// Scratch of a pair call: [partials | next_unit | counters | tile_bad | tile_flags],
+// counters and tile_bad per 128-row half of each split tile, flags per half tile.
+FScratch pair_scratch_of(const FLayout &L) {
+  FScratch s;
+  s.partial_bytes = (size_t)L.plan.sk_tiles * 2 * L.plan.sk_split * BM * P_BN * sizeof(float);
+  s.zero_offset = s.partial_bytes;
+  s.zero_bytes = (1 + 4 * (size_t)L.plan.sk_tiles + 2 * (size_t)L.tiles_m * L.tiles_n) * sizeof(unsigned);
+  s.total = s.zero_offset + s.zero_bytes + 256;
+  return s;
+}
+
 }  // namespace
+
+size_t wg_tf32x3_pair_workspace(const wg_device *d, int64_t m, int64_t n, int64_t k) {
+  return pair_scratch_of(pair_layout_of(d->sm_count, m, n, k, true)).total;
+}
+
+wg_status wg_sgemm_tf32x3_pair(wg_device *d, cudaStream_t st, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                               float alpha, const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                               float *C, int64_t ldc, void *ws, size_t ws_bytes, int uplo) {
+  FLayout L = pair_layout_of(d->sm_count, m, n, k, true);
+  FScratch sc = pair_scratch_of(L);
+  if (sc.total > ws_bytes) {
+    L = pair_layout_of(d->sm_count, m, n, k, false);
+    sc = pair_scratch_of(L);
+    if (sc.total > ws_bytes) return wg_fail(WG_ERR_INVALID_ARGUMENT, "pair 3xTF32 scratch too small");
+  }
+  const bool a_k = transA != 0, b_k = transB == 0;
+  CUtensorMap maps[2];
+  if (!make_fmap(&maps[0], A, a_k, m, k, lda, BM) || !make_fmap(&maps[1], B, b_k, n, k, ldb, P_HALF))
+    return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the pair 3xTF32 operands");
+  char *w = static_cast<char *>(ws);
+  unsigned *zero = reinterpret_cast<unsigned *>(w + sc.zero_offset);
+  WG_CUDA(cudaMemsetAsync(zero, 0, sc.zero_bytes, st));
+  const uint32_t epoch = wg_next_epoch(d);
+  const wg3::Plan &p = L.plan;
+  FArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, L.tiles_m, L.tiles_n, L.kt, p.dp_tiles, p.sk_tiles,
+             p.sk_split, p.sk_tiles ? reinterpret_cast<float *>(w) : nullptr, zero, zero + 1,
+             zero + 1 + 2 * p.sk_tiles, zero + 1 + 4 * p.sk_tiles, epoch, p.dp_tiles + p.sk_tiles * p.sk_split, uplo};
+  {
+    wg_launch_scope scope(d, "sgemm_tf32x3_pair", st);
+    auto kern = a_k ? (b_k ? tf32x3_fused_pair<1, 1> : tf32x3_fused_pair<1, 0>)
+                    : (b_k ? tf32x3_fused_pair<0, 1> : tf32x3_fused_pair<0, 0>);
+    WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM));
+    kern<<<2 * p.grid, F_THREADS, P_SMEM, st>>>(maps[0], maps[1], args);
+    WG_CUDA(cudaGetLastError());
+  }
+  {
+    wg_launch_scope scope(d, "sgemm_simt_fallback", st);
+    const wg_gate gate{d->dwords + WG_DW_FALLBACK, d->dwords + WG_DW_FALLBACK, epoch, epoch};
+    const wg_tile_mask mask{args.tile_flags, 2 * L.tiles_m, P_BN, epoch};
+    WG_CUDA(wg_launch_gemm_simt_masked(st, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, d->dwords,
+                                       &gate, &mask, uplo));
+  }
+  return WG_OK;
+}
 
 bool wg_tf32x3_fused_supported(const wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                                const float *A, int64_t lda, const float *B, int64_t ldb) {

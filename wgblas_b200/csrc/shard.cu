@@ -10,7 +10,7 @@
 // the transfer of panel j+1 overlaps the math of panel j.
 //
 // Transport: on one node with the ranks on distinct GPUs, a copy-engine chain
-// (root -> root+1 -> ...): each rank's DMA engines push 64 MiB chunks into its
+// (root -> root+1 -> ...): each rank's DMA engines push 16 MiB chunks into its
 // successor's landing buffer (an IPC mapping) and raise the successor's
 // arrival counter with a stream memory write, and a one-warp kernel with a
 // clock-bounded spin waits for each chunk. No SM moves data, so the GEMMs keep
@@ -572,7 +572,10 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
   // Root's B reaches the other ranks in their landing buffer (leading dimension
   // ldb): by the copy-engine chain when the ranks set one up, else by
   // ncclBroadcast. The chain moves the stored B (rows_s x cols_s) in chunks of
-  // about 32 MiB cut inside the panels; a panel is ready when its last chunk is.
+  // at most 16 MiB cut inside the panels; a panel is ready when its last chunk
+  // is. A chunk reaches the last of P ranks after P-1 hops, so small chunks keep
+  // the first panel's wait short (7 hops of 16 MiB at about 700 GB/s: 0.17 ms).
+  constexpr int64_t CHUNK_BYTES = (int64_t)16 << 20;
   const bool chain = c->ce.on;
   const int64_t rows_s = transB ? n : k, cols_s = transB ? k : n;
   if (c->nranks > 1) {
@@ -582,7 +585,7 @@ wg_status sharded(wg_comm *c, int transA, int transB, int64_t m_local, int64_t n
   std::vector<Chunk> chunks;
   std::vector<size_t> panel_last;
   if (chain) {
-    const int64_t per = std::max<int64_t>(1, ((int64_t)64 << 20) / (rows_s * (int64_t)sizeof(T)));
+    const int64_t per = std::max<int64_t>(1, CHUNK_BYTES / (rows_s * (int64_t)sizeof(T)));
     int64_t c0 = 0;
     for (size_t j = 0; j < widths.size(); j++) {
       const int64_t w = transB ? cols_s : widths[j];
