@@ -999,9 +999,12 @@ def main():
         rank_share = (offs[rank + 1] - offs[rank]) / w["m"]
     achieved = flops(w) * rank_share / (dom[1][1] / args.steps * 1e-3) / 1e12
     if dom[0].startswith("sgemm_tf32x3"):
-        # A sharded step runs the tensor cores for tens of milliseconds back to back,
-        # long enough to settle under the power cap: it is held to the sustained figure.
-        key = "bf16_tflops_sustained" if w.get("sharded") else "bf16_tflops"
+        # A long sharded step can settle under the power cap: when the SM clock seen
+        # during the timed region sat below its maximum, the step is held to the
+        # sustained figure, else to the burst one.
+        held = (w.get("sharded") and clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
+                and clocks["sm_mhz"] < 0.97 * clocks["sm_max_mhz"])
+        key = "bf16_tflops_sustained" if held else "bf16_tflops"
         peak = peaks.get(key, FALLBACK_PEAKS[key]) * 0.5 / 3.0
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": None,

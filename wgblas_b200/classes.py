@@ -155,6 +155,17 @@ class GpuMatrix:
                                                 inner * item, outer))
         return out
 
+    def write(self, data: np.ndarray) -> None:
+        """Copies ``data`` (the outer*lda elements ``from`` would take, same dtype)
+        into the matrix's buffer (an addition: refills a resident matrix without
+        a new allocation)."""
+        self._require_live()
+        outer = self.rows if self.layout != "column-major" else self.cols
+        data = np.asarray(data)
+        if data.dtype != np.dtype(self.dtype) or data.size < outer * self.lda:
+            raise Error("data must have the matrix's dtype and at least outer*lda elements.")
+        _upload(self._buf, data.reshape(-1)[: outer * self.lda])
+
     def destroy(self) -> None:
         if self._buf is not None:
             nat.lib.wg_buffer_free(self._buf)

@@ -99,6 +99,14 @@ class Comm:
         nat.check(nat.lib.wg_comm_init_rank(device.handle, nranks, rank, unique_id, len(unique_id), timeout_ms,
                                             ct.byref(h)))
         self._h = h
+        self._host_buffers = None  # gemm_sharded_host's device buffers
+
+    def _free_host_buffers(self) -> None:
+        if self._host_buffers is not None:
+            for g in self._host_buffers[1:]:
+                if g is not None:
+                    g.destroy()
+            self._host_buffers = None
 
     @staticmethod
     def unique_id() -> bytes:
@@ -122,6 +130,7 @@ class Comm:
 
     def destroy(self) -> None:
         if self._h is not None:
+            self._free_host_buffers()
             nat.lib.wg_comm_destroy(self._h)
             self._h = None
 
@@ -173,34 +182,38 @@ def gemm_sharded_host(comm: Comm, transA: bool, transB: bool, m_local: int, n: i
     stored matrix, leading dimension ldb; other ranks pass None). The product
     runs sharded, the row blocks are gathered on the root, and the root returns
     the full column-major C (m x n, ld m; into ``out`` when given, e.g. a
-    page-locked array); other ranks return None. Device buffers live for the
-    call only. Collective: every rank must call it."""
+    page-locked array); other ranks return None. The device buffers of the last
+    shape stay on the communicator for the next call (Comm.destroy frees them).
+    Collective: every rank must call it."""
     dev = comm.device
     dt = np.dtype(C_local.dtype)
     m = row_offsets[-1]
     a_rows, a_cols = (k, m_local) if transA else (m_local, k)
     b_rows, b_cols = (n, k) if transB else (k, n)
-    made = []
-    try:
-        GA = GpuMatrix.from_(dev, A_local, a_rows, a_cols, a_rows, "column-major") if m_local else None
-        made.append(GA)
-        GC = GpuMatrix.from_(dev, C_local, m_local, n, m_local, "column-major") if m_local else None
-        made.append(GC)
-        GB = GpuMatrix.from_(dev, B, b_rows, b_cols, ldb, "column-major") if comm.rank == root else None
-        made.append(GB)
+    # Device buffers of the last shape are kept on the communicator (freed by
+    # destroy()): allocating and freeing a few GiB per call would dominate it.
+    key = (dt.str, a_rows, a_cols, m_local, n, b_rows, b_cols, ldb, m, comm.rank == root)
+    cached = comm._host_buffers
+    if cached is None or cached[0] != key:
+        comm._free_host_buffers()
+        GA = GpuMatrix.empty(dev, a_rows, a_cols, a_rows, "column-major", dt) if m_local else None
+        GC = GpuMatrix.empty(dev, m_local, n, m_local, "column-major", dt) if m_local else None
+        GB = GpuMatrix.empty(dev, b_rows, b_cols, ldb, "column-major", dt) if comm.rank == root else None
         GF = GpuMatrix.empty(dev, m, n, m, "column-major", dt) if comm.rank == root else None
-        made.append(GF)
-        gemm_sharded(comm, transA, transB, m_local, n, k, alpha, GA, GB, beta, GC, root=root,
-                     panel_cols=panel_cols, ldb=ldb)
-        gather_rows(comm, GC, m_local, n, row_offsets, root=root, C_full=GF)
-        dev.synchronize()
-        comm.wait()
-        dev.check()
-        return GF.read(out) if GF is not None else None
-    finally:
-        for g in made:
-            if g is not None:
-                g.destroy()
+        comm._host_buffers = cached = (key, GA, GC, GB, GF)
+    _, GA, GC, GB, GF = cached
+    if GA is not None:
+        GA.write(A_local)
+        GC.write(C_local)
+    if GB is not None:
+        GB.write(B)
+    gemm_sharded(comm, transA, transB, m_local, n, k, alpha, GA, GB, beta, GC, root=root,
+                 panel_cols=panel_cols, ldb=ldb)
+    gather_rows(comm, GC, m_local, n, row_offsets, root=root, C_full=GF)
+    dev.synchronize()
+    comm.wait()
+    dev.check()
+    return GF.read(out) if GF is not None else None
 
 
 def gather_rows(comm: Comm, C_local: GpuMatrix, m_local: int, n: int, row_offsets: list[int], root: int = 0,
