@@ -121,6 +121,26 @@ def host_inputs(wg, w, pinned=False):
     return out
 
 
+class L2Flush:
+    """Evicts the operands from the 126 MB L2 between timed steps: ``add_`` writes a
+    512 MB buffer (the flush the timing rule names), then reads a 256 MB one, so
+    that the dirty lines the write leaves in L2 go back to HBM here, outside the
+    timed region, instead of inside the next step (where an HBM-bound kernel
+    would pay for them)."""
+
+    def __init__(self, device):
+        import torch
+
+        self.w = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=device)
+        self.r = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=device)
+
+    def add_(self, value):
+        import torch
+
+        self.w.add_(value)
+        torch.sum(self.r)
+
+
 class Clocks:
     """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
 
@@ -329,7 +349,7 @@ def time_resident(wg, dev, w, steps, warmup, world, flush, parity=True):
             launches0 = dev.kernel_launches()
             t0 = time.perf_counter()
             for i in range(steps):
-                flush.add_(1.0)  # writes 512 MB: evicts the operands from the 126 MB L2
+                flush.add_(1.0)  # evicts the operands from the 126 MB L2 (L2Flush)
                 starts[i].record(stream)
                 gemm_enqueue(wg, dev, w, GA, GB, GC)
                 ends[i].record(stream)
@@ -463,43 +483,85 @@ def time_trsm(wg, dev, nrhs, steps, warmup, flush):
 
 def time_gemv(wg, dev, routine, trans, steps, warmup, flush):
     """sgemv / dgemv at 4096 x 4096, column-major A, unit strides (the layout of
-    the reference's base sweep, benchmarks/sgemv/wgblas/sgemv.js), through the
-    public API on a GpuMatrix and GpuVectors. A (64 / 128 MiB) is evicted from L2
-    before every step. Bytes: A once, x once, y read and written (the reference's
+    the reference's base sweep, benchmarks/sgemv/wgblas/sgemv.js) on GpuMatrix
+    and GpuVector operands: the public API once, then each timed step queues the
+    C-ABI call it makes (wg_sgemv / wg_dgemv) without the host wait the public
+    call adds after it.
+
+    L2: inputs larger than L2. Four copies of A (256 / 512 MiB together) are
+    used in turn, so the A a step reads was evicted by the three read since;
+    the steps run back to back between one pair of events (the rate of a stream
+    of calls; events between the steps add their own gaps). A second pass
+    flushes L2 (the bench's write-then-read flush) before every step instead and
+    is reported beside it: there the step also pays the launch and first-touch
+    latency that back-to-back calls overlap (an empty kernel measures about 6 us
+    in that setting). Bytes: A once, x once, y read and written (the reference's
     count); the HBM roof is the run's bandwidth probe."""
     import torch
 
     n = 4096
     dt = np.float64 if routine == "dgemv" else np.float32
     rnd = wg.randomFloat64Array if dt == np.float64 else wg.randomFloat32Array
-    GA = wg.GpuMatrix.from_(dev, rnd(n * n, -1, 1, 1), n, n, n, "column-major")
+    host_a = rnd(n * n, -1, 1, 1)
+    GAs = [wg.GpuMatrix.from_(dev, host_a, n, n, n, "column-major") for _ in range(4)]
     gx = wg.GpuVector.from_(dev, rnd(n, -1, 1, 2))
     gy = wg.GpuVector.from_(dev, rnd(n, -1, 1, 3))
     fn = getattr(wg, routine)
+    nat = wg._native
+    cfn = nat.lib.wg_dgemv if dt == np.float64 else nat.lib.wg_sgemv
+    t = 0 if trans == "no-transpose" else 1  # the column-major frame of this call (A column-major)
+
+    def enqueue(i):  # the public call's C-ABI step, queued without a host wait
+        nat.check(cfn(dev.handle, t, n, n, 1.0, GAs[i % 4]._buf, 0, n, gx._buf, 0, 1, 0.5, gy._buf, 0, 1, None))
+
+    steps = max(steps, 20)
     stream = torch.cuda.ExternalStream(dev.stream(), device=torch.device("cuda", dev.ordinal))
+
+    def events():
+        return [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+
     try:
         with torch.cuda.stream(stream):
-            for _ in range(warmup):
-                flush.add_(1.0)
-                fn(dev, trans, n, n, 1.0, GA, n, gx, 1, 0.5, gy, 1)
+            fn(dev, trans, n, n, 1.0, GAs[0], n, gx, 1, 0.5, gy, 1)  # the public API once (validation, result)
+            for i in range(max(warmup, 4)):
+                enqueue(i)
             dev.synchronize()
-            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-            for i in range(steps):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for i in range(steps):  # back to back over the four copies
+                enqueue(i)
+            end.record(stream)
+            dev.synchronize()
+            ms = start.elapsed_time(end) / steps
+            starts, ends = events(), events()
+            for i in range(steps):  # flushed before every step
                 flush.add_(1.0)
                 starts[i].record(stream)
-                fn(dev, trans, n, n, 1.0, GA, n, gx, 1, 0.5, gy, 1)
+                enqueue(i)
                 ends[i].record(stream)
             dev.synchronize()
-            ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+            ms_flushed = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
+            dev.profile_read()
+            dev.set_profiling(True)  # per-kernel events, in a pass of its own
+            for i in range(steps):
+                enqueue(i)
+            dev.synchronize()
+            dev.set_profiling(False)
+            prof = dev.profile_read()
     finally:
-        for g in (GA, gx, gy):
+        for g in (*GAs, gx, gy):
             g.destroy()
     item = np.dtype(dt).itemsize
     nbytes = (n * n + 3 * n) * item
+    kernels = {k: v[1] / max(v[0], 1) for k, v in prof.items()}
     return {"gbs": nbytes / (ms * 1e-3) / 1e9, "tflops": 2.0 * n * n / (ms * 1e-3) / 1e12, "ms_per_step": ms,
-            "routine": routine, "shape": {"m": n, "n": n, "trans": trans},
-            "note": "4096x4096 column-major, unit strides; public API on GpuMatrix/GpuVector; L2 flushed"}
+            "routine": routine, "shape": {"m": n, "n": n, "trans": trans}, "kernels": kernels,
+            "kernel_gbs": nbytes / (sum(kernels.values()) * 1e-3) / 1e9 if kernels else None,
+            "flushed": {"ms_per_step": ms_flushed, "gbs": nbytes / (ms_flushed * 1e-3) / 1e9},
+            "l2": "inputs larger than L2 (4 copies of A used in turn, K steps back to back between one event "
+                  "pair); 'flushed' = L2 flushed before each step, events around each step",
+            "note": "4096x4096 column-major A, unit strides; GpuMatrix/GpuVector operands: the public API once, "
+                    "then the same C-ABI call queued per step without a host wait"}
 
 
 def time_cublas(dt, steps, warmup, flush, local):
@@ -816,7 +878,8 @@ def config_of(w, name, world=1):
             "parallelism": f"row-sharded x{world}" if w.get("sharded") else "single GPU",
             "m": w["m"], "n": w["n"], "k": w["k"], "lda": w["lda"], "ldb": w["ldb"], "ldc": w["ldc"],
             "alpha": w["alpha"], "beta": w["beta"], "inputs": "N(0,1) seeded" if w["data"] == "normal" else "U[-1,1] seeded",
-            "l2": "flushed between steps (512 MB device write outside the step events)",
+            "l2": "flushed between steps outside the step events (a 512 MB device write, then a 256 MB read "
+                  "that writes the dirty lines back)",
             "routine": routine_of(w), "shape": shape_of(w),
             "scaling_note": ("N=1 times configs[1] (4096^3 sgemm); N>1 times configs[4] (16384^3, strong "
                              "scaling); extra.efficiency_same_config compares each N>1 value with the same "
@@ -908,7 +971,7 @@ def main():
     torch.cuda.set_device(local)
     wname = pick_workload(args, world)
     w = WORKLOADS[wname]
-    flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=f"cuda:{local}")  # 512 MB
+    flush = L2Flush(f"cuda:{local}")
 
     phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     smi_index = phys[local] if len(phys) > local and phys[local].strip() else str(local)

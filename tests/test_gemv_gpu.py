@@ -254,3 +254,32 @@ def test_full_size(wg, device, oracle, routine, trans):
     """4096 x 4096, column-major (the reference's base sweep layout): both kernels."""
     a = random_case(dtype_of(routine), trans, "column-major", 4096, 4096, 1, 1, 51)
     check_factor(oracle, routine, call(wg, device, routine, a)["y"], a)
+
+
+@pytest.mark.parametrize("routine", ["sgemv", "dgemv"])
+@pytest.mark.parametrize("m,n,pad", [(2371, 37, 1), (4099, 130, 1), (9000, 20, 0), (30001, 9, 3)])
+@pytest.mark.parametrize("beta,inc", [(0.0, 1), (0.75, 1), (0.75, 3)])
+def test_row_blocks(wg, device, oracle, routine, m, n, pad, beta, inc):
+    """Column-major no-transpose with enough rows for one CTA per row block over
+    every column: a ragged last block, a last vector that crosses row m (read
+    one element at a time, the host copy ends at row m of the last column),
+    padded lda, segments of 4, 8 and 32 lanes, unit and strided x and y."""
+    a = random_case(dtype_of(routine), "no-transpose", "column-major", m, n, inc, inc, m + n, beta=beta, pad=pad)
+    check_factor(oracle, routine, call(wg, device, routine, a)["y"], a)
+
+
+@pytest.mark.parametrize("routine", ["sgemv", "dgemv"])
+def test_row_blocks_zero_x_skips_its_column(wg, device, oracle, routine):
+    """The row-block kernel loads every column but adds nothing for a zero x
+    entry, so Infinity and NaN there never reach y; elsewhere they do."""
+    m, n = 4099, 64
+    a = list(random_case(dtype_of(routine), "no-transpose", "column-major", m, n, 1, 1, 5, beta=0.0, pad=1))
+    A, lda, x, y = a[4], a[5], a[6], a[9]
+    for j in (0, 17, 63):
+        x[j] = 0
+        A[j * lda:j * lda + m:5] = np.nan
+        A[j * lda + m - 1] = np.inf
+    A[3 * lda + 100] = -np.inf
+    A[40 * lda + m - 2] = np.nan
+    y[7] = np.nan  # beta = 0: y is not read
+    assert_ieee_match(call(wg, device, routine, tuple(a))["y"], oracle.gemv(*a), 1e-4)
