@@ -6,8 +6,8 @@ The B200 counterpart of the reference's maintainer tooling: scripts/roofline.mjs
 benchmarks count them (benchmarks/<routine>/wgblas/<routine>.js, cited per
 routine below).
 
-Input: JSON lines as ``bench.py`` prints them (the round's BENCH files hold one
-such line per run). The headline's ``config`` and every secondary row in
+Input: JSON lines as ``bench.py`` prints them (one line per run; a file may hold
+several). The headline's ``config`` and every secondary row in
 ``extra`` carry ``routine``, ``shape`` and ``ms_per_step``; rows without them
 are listed as not placed, as the reference lists rows it cannot place.
 
