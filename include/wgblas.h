@@ -155,6 +155,15 @@ wg_status wg_device_set_sgemm_path(wg_device *dev, int path);
 #define WG_DGEMM_SIMT 1
 #define WG_DGEMM_DMMA 2
 wg_status wg_device_set_dgemm_path(wg_device *dev, int path);
+/* strsm algorithm: AUTO picks by shape; RECURSIVE halves the triangle and runs
+ * the off-diagonal updates as GEMMs (one launch per update and per 64-row
+ * diagonal block); FLOW runs the whole solve in one cooperative launch per
+ * group of 64-column right-hand-side chunks: each CTA owns 64-row blocks,
+ * updates them as earlier blocks are published and solves them in turn. */
+#define WG_STRSM_AUTO 0
+#define WG_STRSM_RECURSIVE 1
+#define WG_STRSM_FLOW 2
+wg_status wg_device_set_strsm_path(wg_device *dev, int path);
 
 /* Per-kernel device time of this handle's own launches, for benchmarks and
  * roofline reports. While profiling is on, every kernel the library launches

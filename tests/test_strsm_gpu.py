@@ -34,6 +34,15 @@ def padding_mask(m, n, ld, layout, size):
     return pad
 
 
+@pytest.fixture(params=["recursive", "flow"])
+def strsm_path(request, device):
+    """Runs a test on both solve forms: GEMM updates with a launch per block, and
+    the cooperative flow kernel."""
+    device.set_strsm_path(request.param)
+    yield request.param
+    device.set_strsm_path("auto")
+
+
 def check(oracle, got, a, pad_check=True):
     factor = oracle.strsm_residual_factor(got, *a)
     assert factor <= THRESHOLD, factor
@@ -97,7 +106,7 @@ def reference_system(wg, N, other, pad, side, layout, seed_a, seed_b):
 @pytest.mark.parametrize("side", ["left", "right"])
 @pytest.mark.parametrize("uplo", ["lower", "upper"])
 @pytest.mark.parametrize("transA", ["no-transpose", "transpose"])
-def test_single_block(wg, device, oracle, N, other, layout, side, uplo, transA):
+def test_single_block(wg, device, oracle, strsm_path, N, other, layout, side, uplo, transA):
     m, n, A, B, ld = reference_system(wg, N, other, 3, side, layout, 121, 122)
     diag = "unit" if uplo == "upper" else "non-unit"
     a = (side, uplo, transA, diag, m, n, 1.5, A, N, B, ld, layout)
@@ -109,7 +118,7 @@ def test_single_block(wg, device, oracle, N, other, layout, side, uplo, transA):
 @pytest.mark.parametrize("side", ["left", "right"])
 @pytest.mark.parametrize("uplo", ["lower", "upper"])
 @pytest.mark.parametrize("transA", ["no-transpose", "transpose"])
-def test_many_blocks_in_place(wg, device, oracle, N, other, pad, layout, side, uplo, transA):
+def test_many_blocks_in_place(wg, device, oracle, strsm_path, N, other, pad, layout, side, uplo, transA):
     m, n, A, B, ld = reference_system(wg, N, other, pad, side, layout, 101, 102)
     diag = "unit" if transA == "transpose" else "non-unit"
     a = (side, uplo, transA, diag, m, n, 1.5, A, N, B, ld, layout)
@@ -117,7 +126,7 @@ def test_many_blocks_in_place(wg, device, oracle, N, other, pad, layout, side, u
 
 
 @pytest.mark.parametrize("side,uplo", [("left", "lower"), ("left", "upper"), ("right", "lower")])
-def test_two_blocks(wg, device, oracle, side, uplo):
+def test_two_blocks(wg, device, oracle, strsm_path, side, uplo):
     order, other = 70, 5
     m, n = (order, other) if side == "left" else (other, order)
     rng = np.random.default_rng(7)
@@ -146,7 +155,7 @@ def assert_ieee_match(got, want, tol=1e-4):
 @pytest.mark.parametrize("transA", ["no-transpose", "transpose"])
 @pytest.mark.parametrize("m", [7, 600])
 @pytest.mark.parametrize("label", ["inf early in B", "inf mid B", "-inf late in B", "inf in A"])
-def test_ieee_special_values(wg, device, oracle, uplo, transA, m, label):
+def test_ieee_special_values(wg, device, oracle, strsm_path, uplo, transA, m, label):
     """tests/strsm/src/test.strsm.js:498-578: Infinity in B or in A's referenced
     triangle lands where substitution puts it; NaN in the other triangle is never read."""
     n = 5
@@ -172,7 +181,7 @@ def test_ieee_special_values(wg, device, oracle, uplo, transA, m, label):
 
 @pytest.mark.parametrize("a_layout,b_layout", [("column-major", "column-major"), ("row-major", "column-major"),
                                                ("column-major", "row-major")])
-def test_gpumatrix_in_place(wg, device, oracle, a_layout, b_layout):
+def test_gpumatrix_in_place(wg, device, oracle, strsm_path, a_layout, b_layout):
     """GpuMatrix operands are solved in place; A and B may carry different layouts."""
     order, other = 300, 130
     rng = np.random.default_rng(11)
@@ -200,7 +209,8 @@ def test_gpumatrix_in_place(wg, device, oracle, a_layout, b_layout):
 @pytest.mark.parametrize("side,uplo,transA", [("left", "lower", "no-transpose"), ("right", "upper", "transpose"),
                                               ("left", "upper", "transpose")])
 def test_tensor_core_updates(wg, device, oracle, side, uplo, transA):
-    """Orders 1000+ put the updates between diagonal blocks on the 3xTF32 GEMM."""
+    """Orders 1000+ put the updates between diagonal blocks of the recursive form
+    on the 3xTF32 GEMM."""
     order, other = (1024, 512) if side == "left" else (777, 900)
     m, n = (order, other) if side == "left" else (other, order)
     rng = np.random.default_rng(12)
@@ -209,6 +219,34 @@ def test_tensor_core_updates(wg, device, oracle, side, uplo, transA):
     B = (rng.random(m * n) * 2 - 1).astype(np.float32)
     before = device.sgemm_stats()["tf32x3_launches"]
     a = (side, uplo, transA, "non-unit", m, n, -0.5, A, order, B, m, "column-major")
-    got = run(wg, device, a)
+    device.set_strsm_path("recursive")
+    try:
+        got = run(wg, device, a)
+    finally:
+        device.set_strsm_path("auto")
     assert device.sgemm_stats()["tf32x3_launches"] > before
+    check(oracle, got, a)
+
+
+@pytest.mark.parametrize("side,uplo,transA,order,other", [
+    ("left", "lower", "no-transpose", 200, 70),      # ragged last block and chunk
+    ("right", "lower", "transpose", 1000, 513),      # one launch, several chunks
+    ("left", "upper", "no-transpose", 130, 10000),   # more chunks than fit at once: several launches
+    ("right", "upper", "no-transpose", 4096, 64),    # the bench's shape, one chunk of 64 blocks
+])
+def test_flow_shapes(wg, device, oracle, side, uplo, transA, order, other):
+    """The flow form at shapes that exercise its partition: ragged blocks and
+    right-hand-side chunks, several CTAs per chunk, and more chunks than one
+    cooperative launch holds."""
+    m, n = (order, other) if side == "left" else (other, order)
+    rng = np.random.default_rng(order + other)
+    A = ((rng.random(order * order) * 2 - 1) / order).astype(np.float32)
+    A[np.arange(order) * (order + 1)] = (1.5 + rng.random(order)).astype(np.float32)
+    B = (rng.random(m * n) * 2 - 1).astype(np.float32)
+    a = (side, uplo, transA, "non-unit", m, n, 0.75, A, order, B, m, "column-major")
+    device.set_strsm_path("flow")
+    try:
+        got = run(wg, device, a)
+    finally:
+        device.set_strsm_path("auto")
     check(oracle, got, a)

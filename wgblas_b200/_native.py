@@ -33,6 +33,7 @@ WG_SGEMM_AUTO, WG_SGEMM_SIMT, WG_SGEMM_TF32X3 = 0, 1, 2
 WG_SGEMM_TF32X3_PACKED, WG_SGEMM_TF32X3_FUSED_BN256, WG_SGEMM_TF32X3_FUSED_BN128, WG_SGEMM_TF32X3_FUSED_BN64 = 3, 4, 5, 6
 WG_SGEMM_TF32X3_PAIR = 7
 WG_DGEMM_AUTO, WG_DGEMM_SIMT, WG_DGEMM_DMMA = 0, 1, 2
+WG_STRSM_AUTO, WG_STRSM_RECURSIVE, WG_STRSM_FLOW = 0, 1, 2
 
 c_dev_p = ct.c_void_p
 c_buf_p = ct.c_void_p
@@ -73,6 +74,7 @@ _sig("wg_device_check", _st, c_dev_p)
 _sig("wg_device_sgemm_stats", _st, c_dev_p, ct.POINTER(SgemmStats))
 _sig("wg_device_set_sgemm_path", _st, c_dev_p, ct.c_int)
 _sig("wg_device_set_dgemm_path", _st, c_dev_p, ct.c_int)
+_sig("wg_device_set_strsm_path", _st, c_dev_p, ct.c_int)
 class KernelProfile(ct.Structure):
     _fields_ = [("name", ct.c_char * 48), ("launches", ct.c_uint64), ("total_ms", ct.c_double)]
 

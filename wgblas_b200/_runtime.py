@@ -112,6 +112,12 @@ class Device:
         code = {"auto": nat.WG_DGEMM_AUTO, "simt": nat.WG_DGEMM_SIMT, "dmma": nat.WG_DGEMM_DMMA}[path]
         nat.check(nat.lib.wg_device_set_dgemm_path(self.handle, code))
 
+    def set_strsm_path(self, path: str) -> None:
+        """'auto' (default), 'recursive' (GEMM updates, a launch per block) or 'flow'
+        (the whole solve in cooperative launches)."""
+        code = {"auto": nat.WG_STRSM_AUTO, "recursive": nat.WG_STRSM_RECURSIVE, "flow": nat.WG_STRSM_FLOW}[path]
+        nat.check(nat.lib.wg_device_set_strsm_path(self.handle, code))
+
     def set_profiling(self, on: bool) -> None:
         nat.check(nat.lib.wg_device_set_profiling(self.handle, int(bool(on))))
 

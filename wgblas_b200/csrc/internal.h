@@ -58,7 +58,8 @@ enum {
   WG_DERR_TMA_WAIT = 1u,  // producer or consumer gave up waiting on a pipeline stage
   WG_DERR_MMA_WAIT = 2u,  // the epilogue gave up waiting for the accumulator
   WG_DERR_TMEM = 4u,      // TMEM allocation returned an unusable address
-  WG_DERR_SELFTEST = 8u   // wg_selftest_bounded_wait's wait ran out, as it is meant to
+  WG_DERR_SELFTEST = 8u,  // wg_selftest_bounded_wait's wait ran out, as it is meant to
+  WG_DERR_FLOW_WAIT = 16u  // a strsm flow CTA gave up waiting for an earlier block
 };
 
 struct wg_device {
@@ -78,6 +79,12 @@ struct wg_device {
   int sgemm_path;
   int dgemm_path;
   int fused_bn;  // tile width forced on the fused 3xTF32 kernel (0: chosen per call)
+  int strsm_path;
+  // strsm flow: per (right-hand-side chunk, 64-row block) "solved" words,
+  // written only by the flow kernel with the call's epoch (zero when allocated)
+  unsigned *flow_flags;
+  size_t flow_flags_n;
+  uint32_t flow_epoch;
   cudaStream_t h2d, d2h;  // copy streams of the host-array path (created on first use)
   cudaMemPool_t staging;  // device copies of host-array operands; keeps its memory between calls
   // panelled 3xTF32 products: the stream their operand splits run on, and events

@@ -85,6 +85,7 @@ extern "C" wg_status wg_device_open(int ordinal, unsigned flags, wg_device **out
   d->stream = d->own_stream;
   d->sgemm_path = WG_SGEMM_AUTO;
   d->dgemm_path = WG_DGEMM_AUTO;
+  d->strsm_path = WG_STRSM_AUTO;
   wg_noalloc_reserve(ordinal);  // wg_sgemm_noalloc's fixed scratch is reserved now, not at its first call
   *out = d;
   return WG_OK;
@@ -95,6 +96,7 @@ extern "C" wg_status wg_device_close(wg_device *d) {
   wg_device_guard guard(d->ordinal);
   cudaStreamSynchronize(d->stream);
   if (d->ws) cudaFree(d->ws);
+  if (d->flow_flags) cudaFree(d->flow_flags);
   if (d->dwords) cudaFree(d->dwords);
   cudaEventDestroy(d->ev_start);
   cudaEventDestroy(d->ev_stop);
@@ -163,7 +165,7 @@ extern "C" wg_status wg_device_check(wg_device *d) {
     WG_CUDA(cudaMemsetAsync(d->dwords + WG_DW_ERROR, 0, sizeof(unsigned), d->stream));
     WG_CUDA(cudaStreamSynchronize(d->stream));
     return wg_fail(WG_ERR_KERNEL_TIMEOUT,
-                   "a GEMM kernel's bounded wait gave up (device error word 0x%x); its output "
+                   "a kernel's bounded wait gave up (device error word 0x%x); its output "
                    "is incomplete", word);
   }
   return WG_OK;
@@ -265,6 +267,14 @@ extern "C" wg_status wg_device_set_dgemm_path(wg_device *d, int path) {
   if (path != WG_DGEMM_AUTO && path != WG_DGEMM_SIMT && path != WG_DGEMM_DMMA)
     return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown dgemm path %d", path);
   d->dgemm_path = path;
+  return WG_OK;
+}
+
+extern "C" wg_status wg_device_set_strsm_path(wg_device *d, int path) {
+  if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
+  if (path != WG_STRSM_AUTO && path != WG_STRSM_RECURSIVE && path != WG_STRSM_FLOW)
+    return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown strsm path %d", path);
+  d->strsm_path = path;
   return WG_OK;
 }
 

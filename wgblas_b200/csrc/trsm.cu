@@ -45,6 +45,8 @@ constexpr int LS = LEAF + 4;  // shared row stride: keeps 16-byte alignment of e
 // its MMA kernel (68 us for a 512^3 product, measured with per-kernel events)
 // that a k <= 256 update does not amortise.
 constexpr int64_t SIMT_MAX_K = 256;
+// Right-hand sides up to which `auto` takes the flow form.
+constexpr int64_t FLOW_AUTO_MAX_RHS = 1024;
 
 struct LeafArgs {
   const float *L;  // Lt(0, 0) of the diagonal block
@@ -116,6 +118,248 @@ __global__ void __launch_bounds__(LEAF_RHS) strsm_leaf(LeafArgs a) {
     if (i < nb) xp[i * a.x_rs] = x[i];
 }
 
+// ---- the flow form: one cooperative launch -----------------------------------
+//
+// The same substitution-plus-update arithmetic without a launch per block.
+// The right-hand sides are cut into chunks of 64; CTA q of a chunk's P owns the
+// 64-row blocks p = q, q + P, ... (in solve order) and takes them in turn:
+//
+//   acc = alpha * Bt[p]                                  (this CTA's block)
+//   for each earlier block j:  wait until block j is published,
+//                              acc -= Lt[p, j] * Xt[j]   (64 x 64 x 64 FFMA)
+//   Xt[p] = substitution on Lt[p, p] over acc; publish block p
+//
+// Only the owner writes a block, and a block waits only on blocks before it in
+// solve order, so with every CTA resident (a cooperative launch) the chain
+// always advances. Publishing is a per-(chunk, block) word set to the call's
+// epoch after the block's stores (release); a waiter reads it with acquire and
+// the block's values bypass L1. Lt[p, j] is loaded before the wait, so only the
+// block's own update, its substitution and the publish are on the chain.
+// Every element is still alpha*b minus a sum of products times the reciprocal
+// of the diagonal, so Infinity and NaN land where substitution puts them.
+// Waits are clock-bounded: one that runs out sets WG_DERR_FLOW_WAIT and the CTA
+// stops (the blocks it owns stay unsolved; wg_device_check reports it).
+constexpr int FLOW_THREADS = 256;
+constexpr int FLOW_LD = LEAF + 4;  // shared row stride of the 64 x 64 tiles (16-byte aligned rows)
+constexpr long long FLOW_BUDGET = 4000000000LL;  // clock cycles a wait may take (about 2 s)
+
+struct FlowArgs {
+  const float *L;  // Lt(r, c) = L[r * l_rs + c * l_cs]
+  int64_t l_rs, l_cs;
+  float *X;  // Bt(r, o) = X[r * x_rs + o * x_cs]
+  int64_t x_rs, x_cs;
+  int64_t order, nrhs;
+  int nb;      // 64-row blocks
+  int chunk0;  // first right-hand-side chunk of this launch
+  int P;       // CTAs per chunk
+  int unit;
+  float alpha;
+  unsigned *flags;  // [chunk][nb]
+  unsigned epoch;
+  unsigned *dwords;
+};
+
+// Rows [r0, r0 + len) of block p (solve order).
+template <bool FORWARD>
+__device__ __forceinline__ void flow_rows(const FlowArgs &a, int p, int64_t &r0, int &len) {
+  if (FORWARD) {
+    r0 = (int64_t)p * LEAF;
+    const int64_t e = r0 + LEAF < a.order ? r0 + LEAF : a.order;
+    len = (int)(e - r0);
+  } else {
+    const int64_t hi = a.order - (int64_t)p * LEAF;
+    r0 = hi > LEAF ? hi - LEAF : 0;
+    len = (int)(hi - r0);
+  }
+}
+
+__device__ __forceinline__ unsigned flow_load_acquire(const unsigned *f) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void flow_store_release(unsigned *f, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+// T[k][i] = Lt(ri + i, rk + k) for i < ni, k < nk (0 elsewhere), in registers
+// first (16 per thread) so the loads can be in flight across a wait.
+__device__ __forceinline__ void flow_load_l(const FlowArgs &a, int64_t ri, int ni, int64_t rk, int nk, float (&v)[16]) {
+#pragma unroll
+  for (int t = 0; t < 16; t++) {
+    const int e = (int)threadIdx.x + t * FLOW_THREADS;
+    int i, k;
+    if (a.l_rs == 1) {  // consecutive threads: consecutive rows
+      i = e % LEAF;
+      k = e / LEAF;
+    } else {
+      k = e % LEAF;
+      i = e / LEAF;
+    }
+    v[t] = (i < ni && k < nk) ? a.L[(ri + i) * a.l_rs + (rk + k) * a.l_cs] : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void flow_store_l(const FlowArgs &a, const float (&v)[16], float (*T)[FLOW_LD]) {
+#pragma unroll
+  for (int t = 0; t < 16; t++) {
+    const int e = (int)threadIdx.x + t * FLOW_THREADS;
+    const int i = a.l_rs == 1 ? e % LEAF : e / LEAF, k = a.l_rs == 1 ? e / LEAF : e % LEAF;
+    T[k][i] = v[t];
+  }
+}
+
+// T[k][o] = Bt(r + k, o0 + o) for k < n, o < w (0 elsewhere); L1 bypassed.
+__device__ __forceinline__ void flow_load_x(const FlowArgs &a, int64_t r, int n, int64_t o0, int w,
+                                            float (*T)[FLOW_LD]) {
+#pragma unroll
+  for (int t = 0; t < 16; t++) {
+    const int e = (int)threadIdx.x + t * FLOW_THREADS;
+    int k, o;
+    if (a.x_rs == 1) {
+      k = e % LEAF;
+      o = e / LEAF;
+    } else {
+      o = e % LEAF;
+      k = e / LEAF;
+    }
+    T[k][o] = (k < n && o < w) ? __ldcg(a.X + (r + k) * a.x_rs + (o0 + o) * a.x_cs) : 0.0f;
+  }
+}
+
+template <bool FORWARD>
+__global__ void __launch_bounds__(FLOW_THREADS) strsm_flow(FlowArgs a) {
+  __shared__ __align__(16) float Ls[LEAF][FLOW_LD];  // update: Ls[k][i] = Lt(p row i, j row k); solve: the diagonal block
+  __shared__ __align__(16) float Xs[LEAF][FLOW_LD];  // update: Xs[k][o] = Xt(j row k, o); solve: Xs[o][i]
+  __shared__ float rd[LEAF];
+  __shared__ int stop;
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const int q = (int)blockIdx.x % a.P;
+  const int c = a.chunk0 + (int)blockIdx.x / a.P;
+  const int64_t o0 = (int64_t)c * LEAF;
+  const int w = (int)(a.nrhs - o0 < LEAF ? a.nrhs - o0 : LEAF);
+  unsigned *flags = a.flags + (int64_t)c * a.nb;
+  if (tid == 0) stop = 0;
+  for (int p = q; p < a.nb; p += a.P) {
+    int64_t r0;
+    int len;
+    flow_rows<FORWARD>(a, p, r0, len);
+    // acc = alpha * Bt[p] (this thread's 4 x 4: rows 4ty.., right-hand sides 4tx..)
+    __syncthreads();
+    flow_load_x(a, r0, len, o0, w, Xs);
+    __syncthreads();
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[i][j] = a.alpha * Xs[4 * ty + i][4 * tx + j];
+    for (int jb = 0; jb < p; jb++) {
+      int64_t rj;
+      int lj;
+      flow_rows<FORWARD>(a, jb, rj, lj);
+      float lv[16];
+      flow_load_l(a, r0, len, rj, lj, lv);  // independent of block jb's values: in flight across the wait
+      if (tid == 0) {
+        const long long t0 = clock64();
+        while (flow_load_acquire(flags + jb) != a.epoch) {
+          if (clock64() - t0 > FLOW_BUDGET) {
+            atomicOr(a.dwords + WG_DW_ERROR, WG_DERR_FLOW_WAIT);
+            stop = 1;
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      __syncthreads();  // also: the previous update's reads of Ls / Xs are done
+      if (stop) return;  // uniform: every thread read the same word after the barrier
+      flow_store_l(a, lv, Ls);
+      flow_load_x(a, rj, lj, o0, w, Xs);
+      __syncthreads();
+#pragma unroll 8
+      for (int k = 0; k < LEAF; k++) {
+        const float4 l = *reinterpret_cast<const float4 *>(&Ls[k][4 * ty]);
+        const float4 x = *reinterpret_cast<const float4 *>(&Xs[k][4 * tx]);
+        const float lr[4] = {l.x, l.y, l.z, l.w}, xr[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int j = 0; j < 4; j++) acc[i][j] = fmaf(-lr[i], xr[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+    // Substitution on the diagonal block: Ls[k][i] = Lt(r0 + i, r0 + k) on the
+    // referenced side of the diagonal only, rd[k] its reciprocal diagonal.
+#pragma unroll
+    for (int t = 0; t < 16; t++) {
+      const int e = tid + t * FLOW_THREADS;
+      int i, k;
+      if (a.l_rs == 1) {
+        i = e % LEAF;
+        k = e / LEAF;
+      } else {
+        k = e % LEAF;
+        i = e / LEAF;
+      }
+      const bool below = FORWARD ? i > k : i < k;
+      Ls[k][i] = (i < len && k < len && below) ? a.L[(r0 + i) * a.l_rs + (r0 + k) * a.l_cs] : 0.0f;
+    }
+    if (tid < LEAF) rd[tid] = (tid < len && !a.unit) ? 1.0f / a.L[(r0 + tid) * (a.l_rs + a.l_cs)] : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) Xs[4 * tx + j][4 * ty + i] = acc[i][j];  // Xs[o][i]
+    __syncthreads();
+    if (tid < w) {
+      float x[LEAF];
+#pragma unroll
+      for (int i = 0; i < LEAF; i++) x[i] = Xs[tid][i];
+      if (FORWARD) {
+#pragma unroll
+        for (int k = 0; k < LEAF; k++) {
+          if (k < len) {
+            const float xk = x[k] * rd[k];
+            x[k] = xk;
+#pragma unroll
+            for (int i = k + 1; i < LEAF; i++) x[i] = fmaf(-Ls[k][i], xk, x[i]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = LEAF - 1; k >= 0; k--) {
+          if (k < len) {
+            const float xk = x[k] * rd[k];
+            x[k] = xk;
+#pragma unroll
+            for (int i = 0; i < k; i++) x[i] = fmaf(-Ls[k][i], xk, x[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < LEAF; i++) Xs[tid][i] = x[i];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 16; t++) {
+      const int e = tid + t * FLOW_THREADS;
+      int i, o;
+      if (a.x_rs == 1) {
+        i = e % LEAF;
+        o = e / LEAF;
+      } else {
+        o = e % LEAF;
+        i = e / LEAF;
+      }
+      if (i < len && o < w) a.X[(r0 + i) * a.x_rs + (o0 + o) * a.x_cs] = Xs[o][i];
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      flow_store_release(flags + p, a.epoch);
+    }
+  }
+}
+
 // The problem in the solve frame, with every pointer already at its offset.
 struct Trsm {
   wg_device *d;
@@ -181,6 +425,60 @@ struct Trsm {
     return gemm(0, trans, other, nr, nj, B + j0 * ldb, ldb, ap, lda, beta, B + r0 * ldb, ldb);
   }
 
+  // The whole solve in cooperative launches of strsm_flow (one per group of
+  // right-hand-side chunks that fits on the GPU at once).
+  wg_status flow(float alpha) const {
+    const int64_t nb = (order + LEAF - 1) / LEAF, chunks = (other + LEAF - 1) / LEAF;
+    const size_t need = (size_t)nb * (size_t)chunks;
+    if (need > d->flow_flags_n) {
+      if (d->flow_flags) {
+        WG_CUDA(cudaStreamSynchronize(d->stream));  // queued flow launches may still read them
+        WG_CUDA(cudaFree(d->flow_flags));
+        d->flow_flags = nullptr;
+        d->flow_flags_n = 0;
+      }
+      WG_CUDA(cudaMalloc(&d->flow_flags, need * sizeof(unsigned)));
+      WG_CUDA(cudaMemsetAsync(d->flow_flags, 0, need * sizeof(unsigned), d->stream));
+      d->flow_flags_n = need;
+    }
+    if (++d->flow_epoch == 0) ++d->flow_epoch;  // 0 is the allocation's value
+    const void *fn = forward ? reinterpret_cast<const void *>(&strsm_flow<true>)
+                             : reinterpret_cast<const void *>(&strsm_flow<false>);
+    int per_sm = 0;
+    WG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, FLOW_THREADS, 0));
+    const int64_t resident = (int64_t)per_sm * d->sm_count;
+    if (resident < 1) return wg_fail(WG_ERR_CUDA, "strsm flow kernel cannot be resident");
+    // CTAs per chunk: enough to spread the updates, no more than there are blocks.
+    int64_t P = resident / chunks;
+    if (P > nb) P = nb;
+    if (P < 1) P = 1;
+    const int64_t group = resident / P;  // chunks per launch
+    FlowArgs fa;
+    fa.L = A;
+    fa.l_rs = l_rs();
+    fa.l_cs = l_cs();
+    fa.X = B;
+    fa.x_rs = b_rs();
+    fa.x_cs = b_cs();
+    fa.order = order;
+    fa.nrhs = other;
+    fa.nb = (int)nb;
+    fa.P = (int)P;
+    fa.unit = unit;
+    fa.alpha = alpha;
+    fa.flags = d->flow_flags;
+    fa.epoch = d->flow_epoch;
+    fa.dwords = d->dwords;
+    for (int64_t c0 = 0; c0 < chunks; c0 += group) {
+      fa.chunk0 = (int)c0;
+      const int64_t g = chunks - c0 < group ? chunks - c0 : group;
+      void *args[] = {&fa};
+      wg_launch_scope scope(d, "strsm_flow");
+      WG_CUDA(cudaLaunchCooperativeKernel(fn, dim3((unsigned)(g * P)), dim3(FLOW_THREADS), args, 0, d->stream));
+    }
+    return WG_OK;
+  }
+
   wg_status solve(int64_t lo, int64_t hi, float alpha) const {
     const int64_t len = hi - lo;
     if (len <= LEAF) return leaf(lo, len, alpha);
@@ -219,6 +517,14 @@ wg_status check_args(wg_device *d, int side, int uplo, int transA, int diag, int
   return WG_OK;
 }
 
+// AUTO: the flow form when the solve has more than one block and few
+// right-hand sides, where the recursive form's many small launches dominate.
+bool use_flow(const wg_device *d, int64_t order, int64_t other) {
+  if (d->strsm_path == WG_STRSM_FLOW) return true;
+  if (d->strsm_path == WG_STRSM_RECURSIVE) return false;
+  return order > LEAF && other <= FLOW_AUTO_MAX_RHS;
+}
+
 bool fits(const wg_buffer *b, int64_t off, int64_t rows, int64_t cols, int64_t ld) {
   if (!b || off < 0) return false;
   const __int128 last = (__int128)off + (__int128)(cols - 1) * ld + rows;
@@ -240,13 +546,17 @@ wg_status strsm_enqueue(wg_device *d, int side, int uplo, int transA, int diag, 
     const int op_lower = (transA == 0) == (uplo == WG_UPLO_LOWER);
     Trsm t{d, left, transA, left ? op_lower : !op_lower, diag == WG_DIAG_UNIT, left ? m : n, left ? n : m,
            A, lda, B, ldb};
-    if (t.order > LEAF && wg_tf32x3_supported(d, t.order, t.other, t.order)) {
+    if (use_flow(d, t.order, t.other)) {
+      st = t.flow(alpha);
+    } else if (t.order > LEAF && wg_tf32x3_supported(d, t.order, t.other, t.order)) {
       // Size the GEMM scratch for the largest update up front: growing it
       // later would wait for the queued solve.
       void *ws = nullptr;
       st = wg_workspace(d, wg_tf32x3_workspace_bytes_sk(d, t.order, t.other, t.order), &ws);
+      if (st == WG_OK) st = t.solve(0, t.order, alpha);
+    } else {
+      st = t.solve(0, t.order, alpha);
     }
-    if (st == WG_OK) st = t.solve(0, t.order, alpha);
   }
   if (st != WG_OK) return st;
   if (timing) {
