@@ -53,6 +53,7 @@ constexpr int XF_THREADS = 32 * XF_WARPS;
 constexpr int F_THREADS = 32 * (6 + XF_WARPS);
 constexpr int BADQ = 8;  // slots of the per-unit "operands ruled out" word, indexed by unit order
 constexpr int EC = 16;   // epilogue columns per TMEM load
+constexpr int FG = 2;    // other segments' partial sums loaded together when a split tile is finished
 
 template <int BN_>
 struct FS {
@@ -448,30 +449,38 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < EC; j++) acc[j] = __uint_as_float(r[j]);
           if (nseg > 1) {
-            // Segments in k order, two loaded together; this CTA's own comes from TMEM.
+            // Segments in k order; the partial sums of up to FG other segments
+            // are loaded together (one memory round trip per group), this CTA's
+            // own comes from TMEM. Group [s, e) holds FG others and, where it
+            // falls among them, this CTA's own segment.
             float sum[EC];
-            for (int g0 = 0; g0 < nseg; g0 += 2) {
-              float v[2][EC];
+            for (int s = 0; s < nseg;) {
+              const bool own_near = own >= s && own <= s + FG;
+              const int e = s + FG + (own_near ? 1 : 0) < nseg ? s + FG + (own_near ? 1 : 0) : nseg;
+              const bool own_in = own >= s && own < e;
+              float v[FG][EC];
 #pragma unroll
-              for (int qq = 0; qq < 2; qq++) {
-                const int sgi = g0 + qq;
-                if (sgi < nseg && sgi != own) {
+              for (int qq = 0; qq < FG; qq++) {
+                const int sgi = s + qq + ((own_in && s + qq >= own) ? 1 : 0);  // the qq-th other segment
+                if (sgi < e) {
                   const float *p = part0 + ((int64_t)sgi * BN + c) * BM;
 #pragma unroll
                   for (int j = 0; j < EC; j++) v[qq][j] = __ldcg(p + (int64_t)j * BM);
                 }
               }
 #pragma unroll
-              for (int qq = 0; qq < 2; qq++) {
-                const int sgi = g0 + qq;
-                if (sgi < nseg) {
+              for (int idx = 0; idx <= FG; idx++) {
+                const int t = s + idx;
+                if (t < e) {
+                  const int vi = idx - ((own_in && t > own) ? 1 : 0);
 #pragma unroll
                   for (int j = 0; j < EC; j++) {
-                    const float x = sgi == own ? acc[j] : v[qq][j];
-                    sum[j] = sgi == 0 ? x : sum[j] + x;
+                    const float x = t == own ? acc[j] : (vi == 0 ? v[0][j] : v[1][j]);
+                    sum[j] = t == 0 ? x : sum[j] + x;
                   }
                 }
               }
+              s = e;
             }
 #pragma unroll
             for (int j = 0; j < EC; j++) acc[j] = sum[j];
