@@ -141,6 +141,47 @@ __device__ __forceinline__ bool split_slice(const uint8_t *raw, uint8_t *hi, uin
   return bad;
 }
 
+// The same split in two phases, so that the split warps can load the raw values
+// of two k-slices before any of their stores (loads in flight together): this
+// thread's share of one slice of ROWS rows is T = ROWS * 4 / XF_THREADS
+// 16-byte chunks.
+template <int ROWS>
+struct SliceShare {
+  static constexpr int T = ROWS * 4 / XF_THREADS;
+  float4 x[T];
+};
+
+template <int ROWS, bool KMAJ>
+__device__ __forceinline__ void slice_load(const uint8_t *raw, int xt, SliceShare<ROWS> &sh) {
+#pragma unroll
+  for (int t = 0; t < SliceShare<ROWS>::T; t++) {
+    const int i = xt + t * XF_THREADS;
+    if (KMAJ) {
+      sh.x[t] = reinterpret_cast<const float4 *>(raw)[i];
+    } else {
+      const float *src = reinterpret_cast<const float *>(raw);
+      const int r = i % ROWS, c = i / ROWS;
+      sh.x[t] = make_float4(src[(4 * c) * ROWS + r], src[(4 * c + 1) * ROWS + r], src[(4 * c + 2) * ROWS + r],
+                            src[(4 * c + 3) * ROWS + r]);
+    }
+  }
+}
+
+template <int ROWS, bool KMAJ>
+__device__ __forceinline__ bool slice_store(const SliceShare<ROWS> &sh, uint8_t *hi, uint8_t *lo, int xt) {
+  bool bad = false;
+#pragma unroll
+  for (int t = 0; t < SliceShare<ROWS>::T; t++) {
+    const int i = xt + t * XF_THREADS;
+    float4 h, l;
+    split4(sh.x[t], h, l, bad);
+    const int off = KMAJ ? i * 16 : (i % ROWS) * 64 + (((i / ROWS) ^ (((i % ROWS) >> 1) & 3)) << 4);
+    *reinterpret_cast<float4 *>(hi + off) = h;
+    *reinterpret_cast<float4 *>(lo + off) = l;
+  }
+  return bad;
+}
+
 template <class S, int A_K, int B_K>
 __global__ void __launch_bounds__(F_THREADS, 1)
 tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -333,26 +374,53 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
       if (un < 0) break;
       const wg3::Unit u = wg3::decode(args, un);
       bool bad = false, failed = false;
-      for (int kb = u.kb0; kb < u.kb1; kb++, g++, h++) {
-        const int s = (int)(g % SR), c = (int)(h % SC);
-        const bool okr = wgtc::mbar_wait_bounded(&raw_full[s], (uint32_t)(g / SR) & 1u, WAIT_BUDGET);
-        const bool okc = wgtc::mbar_wait_bounded(&comp_empty[c], ((uint32_t)(h / SC) & 1u) ^ 1u, WAIT_BUDGET);
-        if (!__all_sync(0xffffffffu, okr && okc && *abort_flag == 0)) {
-          if (!(okr && okc)) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
+      // Two k-slices per step where the unit has them: their raw values are all
+      // loaded before any split value is stored, and the fence and the
+      // signalling are paid once per pair.
+      for (int kb = u.kb0; kb < u.kb1;) {
+        const int nk = kb + 1 < u.kb1 ? 2 : 1;
+        const int s0 = (int)(g % SR), c0 = (int)(h % SC);
+        const int s1 = (int)((g + 1) % SR), c1 = (int)((h + 1) % SC);
+        bool ok = wgtc::mbar_wait_bounded(&raw_full[s0], (uint32_t)(g / SR) & 1u, WAIT_BUDGET) &&
+                  wgtc::mbar_wait_bounded(&comp_empty[c0], ((uint32_t)(h / SC) & 1u) ^ 1u, WAIT_BUDGET);
+        if (ok && nk == 2)
+          ok = wgtc::mbar_wait_bounded(&raw_full[s1], (uint32_t)((g + 1) / SR) & 1u, WAIT_BUDGET) &&
+               wgtc::mbar_wait_bounded(&comp_empty[c1], ((uint32_t)((h + 1) / SC) & 1u) ^ 1u, WAIT_BUDGET);
+        if (!__all_sync(0xffffffffu, ok && *abort_flag == 0)) {
+          if (!ok) atomicOr(args.dwords + WG_DW_ERROR, WG_DERR_TMA_WAIT);
           *abort_flag = 1;
           failed = true;
           break;
         }
-        const uint8_t *rs = raw + (size_t)s * S::RAW;
-        uint8_t *cs = comp + (size_t)c * S::COMP;
-        bad |= split_slice<BM, A_K != 0>(rs, cs, cs + S::A_TILE, xt);
-        bad |= split_slice<BN, B_K != 0>(rs + S::A_TILE, cs + 2 * S::A_TILE, cs + 2 * S::A_TILE + S::B_TILE, xt);
+        const uint8_t *rs0 = raw + (size_t)s0 * S::RAW, *rs1 = raw + (size_t)s1 * S::RAW;
+        uint8_t *cs0 = comp + (size_t)c0 * S::COMP, *cs1 = comp + (size_t)c1 * S::COMP;
+        SliceShare<BM> a0, a1;
+        SliceShare<BN> b0, b1;
+        slice_load<BM, A_K != 0>(rs0, xt, a0);
+        slice_load<BN, B_K != 0>(rs0 + S::A_TILE, xt, b0);
+        if (nk == 2) {
+          slice_load<BM, A_K != 0>(rs1, xt, a1);
+          slice_load<BN, B_K != 0>(rs1 + S::A_TILE, xt, b1);
+        }
+        bad |= slice_store<BM, A_K != 0>(a0, cs0, cs0 + S::A_TILE, xt);
+        bad |= slice_store<BN, B_K != 0>(b0, cs0 + 2 * S::A_TILE, cs0 + 2 * S::A_TILE + S::B_TILE, xt);
+        if (nk == 2) {
+          bad |= slice_store<BM, A_K != 0>(a1, cs1, cs1 + S::A_TILE, xt);
+          bad |= slice_store<BN, B_K != 0>(b1, cs1 + 2 * S::A_TILE, cs1 + 2 * S::A_TILE + S::B_TILE, xt);
+        }
         wgtc::fence_proxy_async_smem();  // the MMAs read these tiles through the async proxy
         __syncwarp();
         if (lane == 0) {
-          wg3::mbar_arrive(&comp_full[c]);
-          wg3::mbar_arrive(&raw_empty[s]);
+          wg3::mbar_arrive(&comp_full[c0]);
+          wg3::mbar_arrive(&raw_empty[s0]);
+          if (nk == 2) {
+            wg3::mbar_arrive(&comp_full[c1]);
+            wg3::mbar_arrive(&raw_empty[s1]);
+          }
         }
+        kb += nk;
+        g += nk;
+        h += nk;
       }
       if (failed) break;
       if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(const_cast<int *>(&unit_bad[n % BADQ]), 1);
