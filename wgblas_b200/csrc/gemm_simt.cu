@@ -241,6 +241,10 @@ cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, T alpha, 
   // Per-device attribute: set on every launch so each device that runs the kernel has it.
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem_bytes<T>());
+  // The same shared-memory carveout as the tensor-core kernels it follows, so an
+  // SM need not reconfigure between them.
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
   // One CTA per tile; a gated launch (usually a no-op) strides with at most one
   // CTA per SM of a B200, so its closed-gate exit costs little more than the launch.

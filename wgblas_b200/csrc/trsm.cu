@@ -228,6 +228,27 @@ __device__ __forceinline__ void flow_load_x(const FlowArgs &a, int64_t r, int n,
   }
 }
 
+// The diagonal block's referenced side, v[t] = Lt(r0 + i, r0 + k) for
+// (i, k) below (FORWARD) or above the diagonal and inside the block, in the
+// layout flow_store_l writes.
+template <bool FORWARD>
+__device__ __forceinline__ void flow_load_diag(const FlowArgs &a, int64_t r0, int len, float (&v)[16]) {
+#pragma unroll
+  for (int t = 0; t < 16; t++) {
+    const int e = (int)threadIdx.x + t * FLOW_THREADS;
+    int i, k;
+    if (a.l_rs == 1) {
+      i = e % LEAF;
+      k = e / LEAF;
+    } else {
+      k = e % LEAF;
+      i = e / LEAF;
+    }
+    const bool side = FORWARD ? i > k : i < k;
+    v[t] = (i < len && k < len && side) ? a.L[(r0 + i) * a.l_rs + (r0 + k) * a.l_cs] : 0.0f;
+  }
+}
+
 template <bool FORWARD>
 __global__ void __launch_bounds__(FLOW_THREADS) strsm_flow(FlowArgs a) {
   __shared__ __align__(16) float Ls[LEAF][FLOW_LD];  // update: Ls[k][i] = Lt(p row i, j row k); solve: the diagonal block
@@ -254,6 +275,11 @@ __global__ void __launch_bounds__(FLOW_THREADS) strsm_flow(FlowArgs a) {
     for (int i = 0; i < 4; i++)
 #pragma unroll
       for (int j = 0; j < 4; j++) acc[i][j] = a.alpha * Xs[4 * ty + i][4 * tx + j];
+    // The diagonal block and its reciprocals, loaded now so that their loads are
+    // off the chain.
+    float dv[16];
+    flow_load_diag<FORWARD>(a, r0, len, dv);
+    const float rdv = (tid < len && !a.unit) ? 1.0f / a.L[(r0 + tid) * (a.l_rs + a.l_cs)] : 1.0f;
     for (int jb = 0; jb < p; jb++) {
       int64_t rj;
       int lj;
@@ -288,23 +314,11 @@ __global__ void __launch_bounds__(FLOW_THREADS) strsm_flow(FlowArgs a) {
       }
       __syncthreads();
     }
-    // Substitution on the diagonal block: Ls[k][i] = Lt(r0 + i, r0 + k) on the
-    // referenced side of the diagonal only, rd[k] its reciprocal diagonal.
-#pragma unroll
-    for (int t = 0; t < 16; t++) {
-      const int e = tid + t * FLOW_THREADS;
-      int i, k;
-      if (a.l_rs == 1) {
-        i = e % LEAF;
-        k = e / LEAF;
-      } else {
-        k = e % LEAF;
-        i = e / LEAF;
-      }
-      const bool below = FORWARD ? i > k : i < k;
-      Ls[k][i] = (i < len && k < len && below) ? a.L[(r0 + i) * a.l_rs + (r0 + k) * a.l_cs] : 0.0f;
-    }
-    if (tid < LEAF) rd[tid] = (tid < len && !a.unit) ? 1.0f / a.L[(r0 + tid) * (a.l_rs + a.l_cs)] : 1.0f;
+    // Substitution on the diagonal block (Ls[k][i] = Lt(r0 + i, r0 + k) on the
+    // referenced side of the diagonal only, rd[k] its reciprocal diagonal), as in
+    // strsm_leaf: one thread per right-hand side.
+    flow_store_l(a, dv, Ls);
+    if (tid < LEAF) rd[tid] = rdv;
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
