@@ -431,24 +431,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 32; j++) acc[j] = sum[j];
           }
-          if (in_rows) {
-            float old[32];
-            if (beta != 0.0f) {
-#pragma unroll
-              for (int j = 0; j < 32; j++) {
-                const int64_t col = n0 + c + j;
-                old[j] = col < args.n && wg_in_triangle(args.uplo, row, col) ? args.C[row + col * args.ldc] : 0.0f;
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-              const int64_t col = n0 + c + j;
-              if (col < args.n && wg_in_triangle(args.uplo, row, col)) {
-                const float s = (alpha == 0.0f) ? 0.0f : __fmul_rn(alpha, acc[j]);
-                args.C[row + col * args.ldc] = (beta != 0.0f) ? __fmaf_rn(beta, old[j], s) : s;
-              }
-            }
-          }
+          if (in_rows) wg3::store_c_row<32>(args.C, args.ldc, row, n0 + c, args.n, args.uplo, alpha, beta, acc);
         }
       }
       wgtc::tc_fence_before();
