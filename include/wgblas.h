@@ -148,6 +148,7 @@ wg_status wg_sgemm_tc_plan(int sm_count, int64_t m, int64_t n, int64_t k, wg_tc_
 #define WG_SGEMM_TF32X3_FUSED_BN128 5
 #define WG_SGEMM_TF32X3_FUSED_BN64 6
 #define WG_SGEMM_TF32X3_PAIR 7  /* the fused kernel over CTA pairs (256 x 256 tiles) */
+#define WG_SGEMM_SIMT_SMALL 8  /* the FFMA arithmetic of SIMT on 32 x 64 tiles (small products) */
 wg_status wg_device_set_sgemm_path(wg_device *dev, int path);
 /* dgemm kernel choice: AUTO picks by shape; SIMT forces the DFMA kernel (one
  * sequential FMA chain per element), DMMA the FP64 tensor-core kernel. */

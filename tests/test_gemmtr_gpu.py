@@ -129,9 +129,10 @@ def check_against(oracle, case, got, exact):
 @pytest.mark.parametrize("routine", ROUTINES)
 @pytest.mark.parametrize("uplo", ["lower", "upper"])
 @pytest.mark.parametrize("layout", ["column-major", "row-major"])
-def test_simt_paths_bit_exact(wg, device, oracle, routine, uplo, layout):
+@pytest.mark.parametrize("spath", ["simt", "simt_small"])
+def test_simt_paths_bit_exact(wg, device, oracle, routine, uplo, layout, spath):
     """Small products run the FFMA / DFMA kernels: bit for bit the FMA restatement."""
-    device.set_sgemm_path("simt")
+    device.set_sgemm_path(spath)
     device.set_dgemm_path("simt")
     try:
         seed = ROUTINES.index(routine) * 4 + (uplo == "upper") * 2 + (layout == "row-major")
@@ -151,7 +152,11 @@ def test_tensor_core_paths(wg, device, oracle, routine, uplo, trans):
     triangle are skipped, diagonal tiles masked, the rest within the bound."""
     before = device.sgemm_stats()
     case = random_case(routine, uplo, "column-major", n=600, k=300, m=700, trans=trans, seed=7)
-    got = call(wg, device, case, case["A"], case["B"], case["C"])["C"]
+    device.set_sgemm_path("tf32x3")  # auto sends a product this small to the FFMA kernel
+    try:
+        got = call(wg, device, case, case["A"], case["B"], case["C"])["C"]
+    finally:
+        device.set_sgemm_path("auto")
     if routine.startswith("s"):
         passes = len(as_gemmtr_passes(case))
         assert device.sgemm_stats()["tf32x3_launches"] - before["tf32x3_launches"] == passes

@@ -26,9 +26,11 @@ def _check(oracle, got, a, exact=False):
                        exact=exact)
 
 
-@pytest.fixture
-def simt(device):
-    device.set_sgemm_path("simt")
+@pytest.fixture(params=["simt", "simt_small"])
+def simt(device, request):
+    """Both FFMA kernels (128 x 128 and 32 x 64 tiles) run the same per-element
+    arithmetic, so both match the FMA restatement bit for bit."""
+    device.set_sgemm_path(request.param)
     yield device
     device.set_sgemm_path("auto")
 
@@ -165,7 +167,7 @@ def test_alpha0_reads_neither_a_nor_b(wg, device, oracle, n, beta):
 
 # ---- IEEE specials with alpha != 0 (the dgemm test's cases, applied to sgemm) -------------
 
-@pytest.mark.parametrize("path", ["auto", "simt"])
+@pytest.mark.parametrize("path", ["auto", "simt", "simt_small"])
 @pytest.mark.parametrize("n", [7, 150, 300])
 def test_ieee_specials(wg, device, oracle, n, path):
     device.set_sgemm_path(path)
@@ -191,10 +193,10 @@ def test_config1_512_cubed(wg, device, oracle):
     a = dict(transA=N, transB=N, m=n, n=n, k=n, alpha=1.5, A=wg.randomFloat32Array(n * n, -1, 1, 1), lda=n,
              B=wg.randomFloat32Array(n * n, -1, 1, 2), ldb=n, beta=0.5, C=wg.randomFloat32Array(n * n, -1, 1, 3),
              ldc=n, layout="column-major")
-    for path in ("auto", "simt"):
+    for path in ("auto", "simt", "simt_small"):
         device.set_sgemm_path(path)
         try:
-            _check(oracle, _call(wg, device, a)["C"], a, exact=(path == "simt"))
+            _check(oracle, _call(wg, device, a)["C"], a, exact=path.startswith("simt"))
         finally:
             device.set_sgemm_path("auto")
 
@@ -208,10 +210,10 @@ def test_config4_ragged_padded(wg, device, oracle, ta):
     a = dict(transA=ta, transB=N, m=m, n=n, k=k, alpha=0.3, A=wg.randomFloat32Array(1024 * cols_a, -1, 1, 41),
              lda=1024, B=wg.randomFloat32Array(800 * n, -1, 1, 42), ldb=800, beta=-2.0,
              C=wg.randomFloat32Array(1040 * n, -1, 1, 43), ldc=1040, layout="column-major")
-    for path in ("auto", "simt"):
+    for path in ("auto", "simt", "simt_small"):
         device.set_sgemm_path(path)
         try:
-            _check(oracle, _call(wg, device, a)["C"], a, exact=(path == "simt"))
+            _check(oracle, _call(wg, device, a)["C"], a, exact=path.startswith("simt"))
         finally:
             device.set_sgemm_path("auto")
 

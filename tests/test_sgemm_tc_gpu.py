@@ -119,6 +119,27 @@ def test_tc_gpumatrix_and_workspace_growth(wg, device, oracle, tc):
 
 def test_auto_picks_tc_for_large_k(wg, device, oracle):
     before = device.sgemm_stats()
-    got, args = _run(wg, device, T, N, 512, 512, 512, 1.0, 0.0)
-    assert device.sgemm_stats()["tf32x3_launches"] == before["tf32x3_launches"] + 1
+    got, args = _run(wg, device, T, N, 1024, 1024, 1024, 1.0, 0.0)
+    after = device.sgemm_stats()
+    # host arrays this size arrive in column panels: one tensor-core launch per panel
+    assert after["tf32x3_launches"] > before["tf32x3_launches"]
+    assert after["simt_launches"] == before["simt_launches"]
     check_sgemm(oracle, got, *args)
+
+
+def test_auto_picks_small_ffma_for_small_products(wg, device, oracle):
+    """512^3 (128 tiles of 32 x 64, one per SM, 32 k-tiles deep): the small-tile
+    FFMA kernel, bit for bit the FMA restatement."""
+    before = device.sgemm_stats()
+    device.profile_read()
+    device.set_profiling(True)
+    try:
+        got, args = _run(wg, device, N, N, 512, 512, 512, 1.5, 0.5)
+    finally:
+        device.set_profiling(False)
+    after = device.sgemm_stats()
+    assert after["tf32x3_launches"] == before["tf32x3_launches"]
+    assert after["simt_launches"] == before["simt_launches"] + 1
+    assert device.profile_read().get("sgemm_simt_small", (0,))[0] == 1
+    rep = check_sgemm(oracle, got, *args, exact=True)
+    assert rep is not None

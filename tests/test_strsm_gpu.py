@@ -220,10 +220,12 @@ def test_tensor_core_updates(wg, device, oracle, side, uplo, transA):
     before = device.sgemm_stats()["tf32x3_launches"]
     a = (side, uplo, transA, "non-unit", m, n, -0.5, A, order, B, m, "column-major")
     device.set_strsm_path("recursive")
+    device.set_sgemm_path("tf32x3")  # auto sends updates this small to the FFMA kernel
     try:
         got = run(wg, device, a)
     finally:
         device.set_strsm_path("auto")
+        device.set_sgemm_path("auto")
     assert device.sgemm_stats()["tf32x3_launches"] > before
     check(oracle, got, a)
 

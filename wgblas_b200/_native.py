@@ -32,6 +32,7 @@ WG_DEVICE_TIMING = 1
 WG_SGEMM_AUTO, WG_SGEMM_SIMT, WG_SGEMM_TF32X3 = 0, 1, 2
 WG_SGEMM_TF32X3_PACKED, WG_SGEMM_TF32X3_FUSED_BN256, WG_SGEMM_TF32X3_FUSED_BN128, WG_SGEMM_TF32X3_FUSED_BN64 = 3, 4, 5, 6
 WG_SGEMM_TF32X3_PAIR = 7
+WG_SGEMM_SIMT_SMALL = 8
 WG_DGEMM_AUTO, WG_DGEMM_SIMT, WG_DGEMM_DMMA = 0, 1, 2
 WG_STRSM_AUTO, WG_STRSM_RECURSIVE, WG_STRSM_FLOW = 0, 1, 2
 

@@ -183,7 +183,7 @@ template <int TA, int TB>
 cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, double alpha, const double *A, int64_t lda,
                       const double *B, int64_t ldb, double beta, double *C, int64_t ldc, int uplo) {
   auto kern = dgemm_regs_kernel<TA, TB>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+  cudaError_t e = wg_kernel_smem(kern, SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
   kern<<<grid, NT, SMEM, s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo);
@@ -450,7 +450,7 @@ bool make_dmap(CUtensorMap *map, const double *ptr, bool kcontig, int64_t rows, 
 template <int AK, int BKC>
 cudaError_t launch_tma(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const TmaArgs &args) {
   auto kern = dgemm_tma_kernel<AK, BKC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk::SMEM);
+  cudaError_t e = wg_kernel_smem(kern, tk::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)((args.m + tk::BM - 1) / tk::BM), (unsigned)((args.n + tk::BN - 1) / tk::BN));
   kern<<<grid, tk::THREADS, tk::SMEM, s>>>(ma, mb, args);

@@ -71,10 +71,29 @@ wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64
 
 namespace {
 
+// Small products on the FFMA pipe: the 32 x 64-tile kernel beats the 3xTF32
+// kernels while each SM runs at most 80 of its 16-deep k-tiles (one CTA per
+// SM per wave). Measured per call on B200 with L2 flushed between calls:
+// 256^3 22 vs 38 us, 512^3 28 vs 41 us, 640^3 43 vs 45 us; 768^3 51 vs 47 us
+// and 256 x 256 x 4096 127 vs 57 us go to the tensor cores.
+bool small_ffma_wins(const wg_device *d, int64_t m, int64_t n, int64_t k) {
+  const int64_t tiles = ((m + 31) / 32) * ((n + 63) / 64), sm = d->sm_count > 0 ? d->sm_count : 1;
+  return (tiles + sm - 1) / sm * ((k + 15) / 16) <= 80;
+}
+
+// FFMA work (no tensor cores) goes to the 32 x 64-tile kernel when asked, when
+// it is a small product (above), or when the 128 x 128-tile kernel would not
+// have a tile for every SM.
+bool simt_small_tiles(const wg_device *d, int path, int64_t m, int64_t n, int64_t k) {
+  if (path == WG_SGEMM_SIMT_SMALL) return true;
+  return path == WG_SGEMM_AUTO &&
+         (small_ffma_wins(d, m, n, k) || ((m + 127) / 128) * ((n + 127) / 128) < d->sm_count);
+}
+
 // sgemm kernel choice. The 3xTF32 tensor-core kernel needs enough k to amortise
-// its split pass and gives no benefit on tiny grids; everything else, and any
-// call whose operands fail the split's range check on the device, runs the
-// FFMA kernel.
+// its split pass and gives no benefit on tiny grids or small products (above);
+// everything else, and any call whose operands fail the split's range check on
+// the device, runs an FFMA kernel.
 template <>
 wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k,
                              float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
@@ -88,14 +107,15 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
   d->stats.calls++;
   bool tc = false;
   const int path = d->sgemm_path;
-  const bool forced_tc = path >= WG_SGEMM_TF32X3;
+  const bool forced_tc = path >= WG_SGEMM_TF32X3 && path <= WG_SGEMM_TF32X3_PAIR;
   if (forced_tc) {
     if (!wg_tf32x3_supported(d, m, n, k))
       return wg_fail(WG_ERR_NOT_SUPPORTED, "the 3xTF32 kernel does not support m=%lld n=%lld k=%lld",
                      (long long)m, (long long)n, (long long)k);
     tc = true;
   } else if (path == WG_SGEMM_AUTO) {
-    tc = wg_tf32x3_supported(d, m, n, k) && k >= 64 && (double)m * (double)n >= 256.0 * 256.0;
+    tc = wg_tf32x3_supported(d, m, n, k) && k >= 64 && (double)m * (double)n >= 256.0 * 256.0 &&
+         !small_ffma_wins(d, m, n, k);
   }
   const bool aligned = tc && path != WG_SGEMM_TF32X3_PACKED &&
                        wg_tf32x3_fused_supported(d, transA, transB, m, n, k, A, lda, B, ldb);
@@ -142,6 +162,11 @@ wg_status gemm_launch<float>(wg_device *d, int transA, int transB, int64_t m, in
     return WG_OK;
   }
   d->stats.simt_launches++;
+  if (simt_small_tiles(d, path, m, n, k)) {
+    wg_launch_scope scope(d, "sgemm_simt_small");
+    WG_CUDA(wg_launch_gemm_simt_small(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, uplo));
+    return WG_OK;
+  }
   wg_launch_scope scope(d, "sgemm_simt");
   WG_CUDA(wg_launch_gemm_simt<float>(s, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
                                      d->dwords, nullptr, uplo));
@@ -325,7 +350,9 @@ wg_status gemm_host(wg_device *d, int transA, int transB, int64_t m, int64_t n, 
   const int64_t panels = (n + panel - 1) / panel;
   // sgemm panels on the tensor cores run as one wg_tc_product, whose op(B)
   // splits overlap the previous panel's MMA.
-  const bool tc = panels > 1 && std::is_same<T, float>::value && wg_sgemm_panel_on_tc(d, (float)alpha, m, panel, k);
+  // A small product as a whole (small_ffma_wins) keeps its panels on the FFMA kernel.
+  const bool tc = panels > 1 && std::is_same<T, float>::value && wg_sgemm_panel_on_tc(d, (float)alpha, m, panel, k) &&
+                  !(d->sgemm_path == WG_SGEMM_AUTO && small_ffma_wins(d, m, n, k));
   const int64_t widths[2] = {panel, n - (panels - 1) * panel};
   wg_tc_product prod{};
   HostPipe pipe;
@@ -415,7 +442,8 @@ wg_status wg_gemm_panel(wg_device *d, int transA, int transB, int64_t m, int64_t
 }
 
 bool wg_sgemm_panel_on_tc(const wg_device *d, float alpha, int64_t m, int64_t cols, int64_t k) {
-  return d->sgemm_path != WG_SGEMM_SIMT && alpha != 0.0f && k >= 64 && m > 0 && cols > 0 &&
+  return d->sgemm_path != WG_SGEMM_SIMT && d->sgemm_path != WG_SGEMM_SIMT_SMALL && alpha != 0.0f && k >= 64 &&
+         m > 0 && cols > 0 &&
          wg_tf32x3_supported(d, m, cols, k);
 }
 

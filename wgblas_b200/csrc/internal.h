@@ -133,6 +133,17 @@ wg_status wg_fail(wg_status st, const char *fmt, ...);
                      "%s failed: %s", #call, cudaGetErrorString(e_));                   \
   } while (0)
 
+// Raises kernel `fn`'s dynamic shared-memory limit to `bytes` (and, when asked,
+// its preferred carveout to the maximum) on the current device, once per
+// (kernel, device, bytes): the attributes last for the context, and setting
+// them again on every launch put host time between the caller's stream
+// operations. (runtime.cu)
+cudaError_t wg_kernel_smem_raw(const void *fn, size_t bytes, bool max_carveout);
+template <class F>
+cudaError_t wg_kernel_smem(F *fn, size_t bytes, bool max_carveout = false) {
+  return wg_kernel_smem_raw(reinterpret_cast<const void *>(fn), bytes, max_carveout);
+}
+
 // Makes `ordinal` current for the lifetime of the guard.
 struct wg_device_guard {
   int prev;
@@ -214,6 +225,10 @@ wg_status wg_staging_pool(wg_device *dev);
 
 // ---- kernel launchers (gemm_simt.cu, sgemm_tf32x3.cu) ----
 
+// The same FFMA arithmetic on 32 x 64 tiles (small products: every SM gets a tile).
+cudaError_t wg_launch_gemm_simt_small(cudaStream_t s, int transA, int transB, int64_t m, int64_t n, int64_t k,
+                                      float alpha, const float *A, int64_t lda, const float *B, int64_t ldb,
+                                      float beta, float *C, int64_t ldc, int uplo);
 // C = alpha*op(A)op(B) + beta*C on the FFMA / DFMA pipes, sequential k per element.
 // With a gate, every CTA first checks it and exits unless it is open (the
 // device-side fallback of the 3xTF32 path), counting runs in dwords[WG_DW_FALLBACKS].

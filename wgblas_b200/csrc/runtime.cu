@@ -11,7 +11,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
+#include <set>
+#include <tuple>
 
 #include "internal.h"
 
@@ -26,6 +29,22 @@ wg_status wg_fail(wg_status st, const char *fmt, ...) {
 }
 
 extern "C" const char *wg_last_error(void) { return g_last_error; }
+
+cudaError_t wg_kernel_smem_raw(const void *fn, size_t bytes, bool max_carveout) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void *, int, size_t, bool>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_tuple(fn, dev, bytes, max_carveout);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && max_carveout)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
 extern "C" int wg_abi_version(void) { return WG_ABI_VERSION; }
 
 // ---------------------------------------------------------------------------
@@ -280,7 +299,7 @@ extern "C" wg_status wg_device_set_strsm_path(wg_device *d, int path) {
 
 extern "C" wg_status wg_device_set_sgemm_path(wg_device *d, int path) {
   if (!d) return wg_fail(WG_ERR_INVALID_ARGUMENT, "device is NULL");
-  if (path < WG_SGEMM_AUTO || path > WG_SGEMM_TF32X3_PAIR)
+  if (path < WG_SGEMM_AUTO || path > WG_SGEMM_SIMT_SMALL)
     return wg_fail(WG_ERR_INVALID_ARGUMENT, "unknown sgemm path %d", path);
   d->sgemm_path = path;
   d->fused_bn = path == WG_SGEMM_TF32X3_FUSED_BN256 ? 256

@@ -1022,7 +1022,7 @@ cudaError_t launch_bn(cudaStream_t st, int grid, bool a_k, bool b_k, const CUten
   using S = FS<BN>;
   auto kern = a_k ? (b_k ? tf32x3_fused<S, 1, 1> : tf32x3_fused<S, 1, 0>)
                   : (b_k ? tf32x3_fused<S, 0, 1> : tf32x3_fused<S, 0, 0>);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+  cudaError_t e = wg_kernel_smem(kern, S::SMEM);
   if (e != cudaSuccess) return e;
   kern<<<grid, F_THREADS, S::SMEM, st>>>(ma, mb, args);
   return cudaGetLastError();
@@ -1082,7 +1082,7 @@ wg_status wg_sgemm_tf32x3_pair(wg_device *d, cudaStream_t st, int transA, int tr
     wg_launch_scope scope(d, "sgemm_tf32x3_pair", st);
     auto kern = a_k ? (b_k ? tf32x3_fused_pair<1, 1> : tf32x3_fused_pair<1, 0>)
                     : (b_k ? tf32x3_fused_pair<0, 1> : tf32x3_fused_pair<0, 0>);
-    WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM));
+    WG_CUDA(wg_kernel_smem(kern, P_SMEM));
     kern<<<2 * p.grid, F_THREADS, P_SMEM, st>>>(maps[0], maps[1], args);
     WG_CUDA(cudaGetLastError());
   }

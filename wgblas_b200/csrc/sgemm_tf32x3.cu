@@ -531,7 +531,7 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
                plan.sk_tiles, plan.sk_split, partials, counters, next_unit,
                plan.dp_tiles + plan.sk_tiles * plan.sk_split, uplo};
   auto kern = tf32x3_mma<Sh>;
-  WG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sh::SMEM));
+  WG_CUDA(wg_kernel_smem(kern, Sh::SMEM));
   {
     wg_launch_scope scope(d, "sgemm_tf32x3_mma");
     kern<<<plan.grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
@@ -687,7 +687,7 @@ wg_status wg_tc_product_begin(wg_tc_product *p, wg_device *d, int transA, int tr
                               size_t count, cudaEvent_t a_ready, const float *B0, int64_t ldb) {
   int64_t widest = 0;
   for (size_t i = 0; i < count; i++) widest = widths[i] > widest ? widths[i] : widest;
-  const bool forced = d->sgemm_path >= WG_SGEMM_TF32X3_FUSED_BN256;
+  const bool forced = d->sgemm_path >= WG_SGEMM_TF32X3_FUSED_BN256 && d->sgemm_path <= WG_SGEMM_TF32X3_PAIR;
   if (d->sgemm_path != WG_SGEMM_TF32X3_PACKED && widest > 0 &&
       (forced || (double)m * (double)widest * (double)k <= WG_FUSED_MAX_WORK) &&
       wg_tf32x3_fused_supported(d, transA, transB, m, widest, k, A, lda, B0, ldb)) {
