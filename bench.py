@@ -951,11 +951,23 @@ def main():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extra", action="store_true", help="skip the secondary workloads and probes")
     p.add_argument("--sgemm-path", default="auto",
-                   help="force an sgemm kernel (Device.set_sgemm_path: simt, tf32x3, tf32x3_packed, "
-                        "tf32x3_fused_bn256/128/64) for profiling one kernel; the default picks by shape")
+                   help="force an sgemm kernel (Device.set_sgemm_path: simt, simt_small, tf32x3, tf32x3_packed, "
+                        "tf32x3_fused_bn256/128/64, tf32x3_pair) for profiling one kernel; the default picks by "
+                        "shape")
     p.add_argument("--dgemm-path", default="auto", help="force a dgemm kernel (simt or dmma) for profiling")
+    p.add_argument("--shape", default=None, metavar="M,N,K[,TA,TB]",
+                   help="time one sgemm of this shape instead of a named workload (column-major, tight leading "
+                        "dimensions, alpha 1.5, beta 0.5, U[-1,1] seeded; TA/TB 1 = transposed)")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.shape:
+        dims = [int(x) for x in args.shape.split(",")]
+        m, n, k = dims[:3]
+        ta, tb = (dims[3], dims[4]) if len(dims) == 5 else (0, 0)
+        WORKLOADS["shape"] = dict(routine="sgemm", config_index=None, transA=ta, transB=tb, m=m, n=n, k=k,
+                                  lda=k if ta else m, ldb=n if tb else k, ldc=m, alpha=1.5, beta=0.5,
+                                  data="uniform")
+        args.workload = "shape"
     world, rank, local = dist_setup()
     if args.impl == "reference":
         return run_reference(args, world, rank)
