@@ -15,7 +15,7 @@ LIB = os.path.join(HERE, "libwgblas_b200.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 
 SOURCES = ["runtime.cu", "gemm.cu", "gemm_simt.cu", "sgemm_tf32x3.cu", "sgemm_fused.cu", "probe.cu", "sgemm_noalloc.cu", "dgemm_dmma.cu", "shard.cu", "level3_aux.cu", "trsm.cu", "gemv.cu"]
-HEADERS = ["internal.h", "tcgen05.cuh", "tf32x3_common.cuh"]
+HEADERS = ["internal.h", "tcgen05.cuh", "tf32x3_common.cuh", "simt_tile.cuh"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

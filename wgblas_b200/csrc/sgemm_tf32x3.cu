@@ -38,13 +38,16 @@
 //     gemmtr calls skip the units whose tile has no element in the triangle
 //     and mask the diagonal tiles' stores.
 //  When the pack flagged the operands (the gate: a flag word holding the
-//  call's epoch) the MMA kernel exits at once and the FFMA kernel launched
-//  after it, gated on the same words, computes C instead.
+//  call's epoch) the MMA kernel computes C itself on the FFMA pipe instead,
+//  with all eight warps running the SIMT GEMM's tile (simt_tile.cuh), so the
+//  result has the reference's IEEE semantics and the FFMA kernel's bits. An
+//  unflagged call launches nothing else.
 #include <cuda.h>
 
 #include <mutex>
 
 #include "internal.h"
+#include "simt_tile.cuh"
 #include "tcgen05.cuh"
 #include "tf32x3_common.cuh"
 
@@ -64,7 +67,11 @@ using wg3::epi_all;
 using wg3::mbar_arrive;
 using wg3::Plan;
 using wg3::split_overhead;
-constexpr int THREADS = 32 * (2 + EPI_WARPS);
+// Producer, MMA issuer, EPI_WARPS epilogue warps and two more that only the
+// FFMA fallback uses (its tile needs 256 threads; one CTA per SM either way, at
+// 255 registers a thread).
+constexpr int THREADS = 32 * (2 + EPI_WARPS + 2);
+static_assert(THREADS == wgsimt::NT, "the fallback runs the SIMT tile with every thread");
 constexpr int SEG_GROUP = 2;  // partial-sum segments the fixup loads at once
 
 // Kernel shape: BN columns of C per CTA, BK floats of K per pipeline stage
@@ -164,19 +171,55 @@ struct MmaArgs {
   unsigned *next_unit;       // work counter: units handed out beyond the first gridDim.x
   int units;                 // dp_tiles + sk_tiles * sk_split
   int uplo;                  // WG_UPLO_*: tiles with no element in the triangle are skipped
+  // The caller's operands, for the FFMA fallback.
+  const float *A, *B;
+  int64_t lda, ldb;
+  int transA, transB;
 };
+
+// C for a call whose operands the split ruled out, on the FFMA pipe: the SIMT
+// GEMM's 128 x 128 tiles, grid-stride, every thread of the block, shared memory
+// from the (unused) operand ring.
+__device__ __forceinline__ void ffma_fallback(const MmaArgs &a, uint8_t *smem) {
+  using namespace wgsimt;
+  float *As = reinterpret_cast<float *>(smem);
+  float *Bs = As + 2 * wgsimt::BK * lda_s<float>();
+  const int64_t kk = a.alpha == 0.0f ? 0 : a.k;
+  const int64_t tiles_m = (a.m + wgsimt::BM - 1) / wgsimt::BM, tiles = tiles_m * ((a.n + wgsimt::BN - 1) / wgsimt::BN);
+  const wg_tile_mask all{nullptr, 1, 1, 0u};
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t m0 = (t % tiles_m) * wgsimt::BM, n0 = (t / tiles_m) * wgsimt::BN;
+    if (wg_tile_outside(a.uplo, m0, wgsimt::BM, n0, wgsimt::BN)) continue;
+    if (a.transA) {
+      if (a.transB)
+        tile<float, 1, 1>(m0, n0, a.m, a.n, kk, a.alpha, a.A, a.lda, a.B, a.ldb, a.beta, a.C, a.ldc, all, a.uplo, As, Bs);
+      else
+        tile<float, 1, 0>(m0, n0, a.m, a.n, kk, a.alpha, a.A, a.lda, a.B, a.ldb, a.beta, a.C, a.ldc, all, a.uplo, As, Bs);
+    } else {
+      if (a.transB)
+        tile<float, 0, 1>(m0, n0, a.m, a.n, kk, a.alpha, a.A, a.lda, a.B, a.ldb, a.beta, a.C, a.ldc, all, a.uplo, As, Bs);
+      else
+        tile<float, 0, 0>(m0, n0, a.m, a.n, kk, a.alpha, a.A, a.lda, a.B, a.ldb, a.beta, a.C, a.ldc, all, a.uplo, As, Bs);
+    }
+  }
+}
 
 template <class S>
 __global__ void __launch_bounds__(THREADS, 1)
 tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
            const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
            const MmaArgs args) {
-  // Operands ruled out by the pack pass: the FFMA kernel queued next computes C.
-  if (wg_gate_open(args.gate)) return;
-
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = wgtc::smem_addr(smem_raw);
   uint8_t *smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned ring
+
+  // Operands ruled out by the pack pass (the gate, the same for every thread):
+  // C comes from the FFMA pipe instead, with the reference's IEEE semantics.
+  if (wg_gate_open(args.gate)) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(args.dwords + WG_DW_FALLBACKS, 1u);
+    ffma_fallback(args, smem);
+    return;
+  }
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S::STAGES * S::STAGE);
   uint64_t *empty = full + S::STAGES;
   uint64_t *acc_full = empty + S::STAGES;  // [2]: accumulator b holds a finished unit
@@ -325,7 +368,7 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
       }
       wgtc::mma_commit(&acc_full[b]);  // accumulator b complete once all its MMAs finish
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 2 + EPI_WARPS) {
     // ---- epilogue: TMEM -> registers -> C (or a partial-sum slot) ----
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
@@ -507,8 +550,8 @@ wg_status launch_pack(wg_device *d, cudaStream_t s, const PackArgs &pa, const Pa
   return WG_OK;
 }
 
-// The MMA launch over split operands already in place, then the FFMA launch
-// that computes C instead when `gate` is open; both on d->stream. The last
+// The MMA launch over split operands already in place, on d->stream; when
+// `gate` is open it computes C on the FFMA pipe instead. The last
 // wave's tiles are split along k when sk_room bytes at `sk` hold the plan's
 // partial sums and counters (counters at sk + partial_room, zeroed
 // beforehand), whole otherwise. next_unit is the work counter, zeroed beforehand.
@@ -529,19 +572,13 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
     return wg_fail(WG_ERR_CUDA, "cuTensorMapEncodeTiled failed for the 3xTF32 operands");
   MmaArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, gate, L.tiles_m, L.tiles_n, L.kt, plan.dp_tiles,
                plan.sk_tiles, plan.sk_split, partials, counters, next_unit,
-               plan.dp_tiles + plan.sk_tiles * plan.sk_split, uplo};
+               plan.dp_tiles + plan.sk_tiles * plan.sk_split, uplo, A, B, lda, ldb, transA, transB};
   auto kern = tf32x3_mma<Sh>;
   WG_CUDA(wg_kernel_smem(kern, Sh::SMEM));
   {
     wg_launch_scope scope(d, "sgemm_tf32x3_mma");
     kern<<<plan.grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
     WG_CUDA(cudaGetLastError());
-  }
-  {
-    // Device-side fallback: exits at once unless the split flagged these operands.
-    wg_launch_scope scope(d, "sgemm_simt_fallback");
-    WG_CUDA(wg_launch_gemm_simt<float>(d->stream, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc,
-                                       d->dwords, &gate, uplo));
   }
   return WG_OK;
 }
