@@ -30,7 +30,10 @@ gemm_simt_kernel(int64_t m, int64_t n, int64_t k, T alpha, const T *__restrict__
                  const T *__restrict__ B, int64_t ldb, T beta, T *__restrict__ C, int64_t ldc,
                  unsigned *dwords, wg_gate gate, int gated, wg_tile_mask mask, int uplo) {
   if (gated) {
-    // Device-side fallback of the 3xTF32 path: run only if its operand check failed.
+    // Device-side fallback of the 3xTF32 path: run only if its operand check
+    // failed. Launched programmatically, it may be resident before the kernel
+    // that sets the gate has finished: wait for that kernel first.
+    wg_pdl_wait();
     if (!wg_gate_open(gate)) return;
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(dwords + WG_DW_FALLBACKS, 1u);
   }
@@ -423,9 +426,20 @@ cudaError_t launch_tt(cudaStream_t s, int64_t m, int64_t n, int64_t k, T alpha, 
   if (gate && grid > GATED_GRID) grid = GATED_GRID;
   const wg_gate g = gate ? *gate : wg_gate{nullptr, nullptr, 0u, 0u};
   const wg_tile_mask mk = mask ? *mask : wg_tile_mask{nullptr, 1, 1, 0u};
-  kern<<<(unsigned)grid, NT, smem_bytes<T>(), s>>>(m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, g,
-                                                   gate ? 1 : 0, mk, uplo);
-  return cudaGetLastError();
+  // A gated launch follows the kernel that sets its gate: it is launched
+  // programmatically, so its launch overlaps that kernel's end.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem_bytes<T>();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = gate ? 1 : 0;
+  const int gated = gate ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, dwords, g, gated, mk, uplo);
 }
 
 }  // namespace

@@ -49,6 +49,14 @@ inline bool wg_tile_outside(int uplo, int64_t i0, int64_t h, int64_t j0, int64_t
   return (uplo == WG_UPLO_LOWER && j0 > i0 + h - 1) || (uplo == WG_UPLO_UPPER && j0 + w - 1 < i0);
 }
 #ifdef __CUDACC__
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start once every CTA of the kernel before it in the stream
+// has run wg_pdl_trigger (or exited); wg_pdl_wait then blocks until that kernel
+// has completed and its memory operations are visible. Without the launch
+// attribute the wait returns at once.
+__device__ __forceinline__ void wg_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wg_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ bool wg_gate_open(const wg_gate &g) {
   return *(volatile const unsigned *)g.a == g.ea || *(volatile const unsigned *)g.b == g.eb;
 }

@@ -207,6 +207,7 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile unsigned *last_flag = reinterpret_cast<volatile unsigned *>(tmem_slot + 2);
   volatile unsigned *seg_bad = reinterpret_cast<volatile unsigned *>(tmem_slot + 3);
+  wg_pdl_trigger();  // the gated FFMA launch after this one may be scheduled early; it waits for this kernel
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -623,6 +624,7 @@ tf32x3_fused_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile unsigned *last_flag = reinterpret_cast<volatile unsigned *>(tmem_slot + 2);
   volatile unsigned *seg_bad = reinterpret_cast<volatile unsigned *>(tmem_slot + 3);
+  wg_pdl_trigger();  // the gated FFMA launch after this one may be scheduled early; it waits for this kernel
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = wgtc::cluster_ctarank();

@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(256) tf32x3_pack(PackArgs a, PackArgs b, int64
                                                    int64_t tiles_a, unsigned *counters, int64_t n_counters,
                                                    unsigned *next_unit) {
   __shared__ float tile[32][33];
+  wg_pdl_trigger();  // the MMA kernel may set itself up while the last blocks split
   // The split-tile counters and the work counter of the MMA launch that follows start at zero.
   if (blockIdx.x == 0) {
     for (int64_t i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
@@ -212,14 +213,6 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = wgtc::smem_addr(smem_raw);
   uint8_t *smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned ring
-
-  // Operands ruled out by the pack pass (the gate, the same for every thread):
-  // C comes from the FFMA pipe instead, with the reference's IEEE semantics.
-  if (wg_gate_open(args.gate)) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(args.dwords + WG_DW_FALLBACKS, 1u);
-    ffma_fallback(args, smem);
-    return;
-  }
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S::STAGES * S::STAGE);
   uint64_t *empty = full + S::STAGES;
   uint64_t *acc_full = empty + S::STAGES;  // [2]: accumulator b holds a finished unit
@@ -264,7 +257,15 @@ tf32x3_mma(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ 
   wgtc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
+  // The setup above overlaps the split pass's last blocks (programmatic
+  // launch); everything below reads what it wrote: operands, counters, gate.
+  wg_pdl_wait();
+  if (wg_gate_open(args.gate)) {
+    // Operands ruled out by the split (the gate, the same for every thread): C
+    // comes from the FFMA pipe instead, with the reference's IEEE semantics.
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(args.dwords + WG_DW_FALLBACKS, 1u);
+    ffma_fallback(args, smem);
+  } else if (warp == 0 && lane == 0) {
     // ---- TMA producer: takes units (its first is blockIdx.x, later ones from the
     // work counter, so SMs slowed by other kernels take fewer), hands each to the
     // other roles, and streams its k-blocks into one continuous ring ----
@@ -551,14 +552,16 @@ wg_status launch_pack(wg_device *d, cudaStream_t s, const PackArgs &pa, const Pa
 }
 
 // The MMA launch over split operands already in place, on d->stream; when
-// `gate` is open it computes C on the FFMA pipe instead. The last
+// `gate` is open it computes C on the FFMA pipe instead. With `pdl` the split
+// pass is the launch right before it on the stream, and the kernel sets itself
+// up while that pass finishes (programmatic dependent launch). The last
 // wave's tiles are split along k when sk_room bytes at `sk` hold the plan's
 // partial sums and counters (counters at sk + partial_room, zeroed
 // beforehand), whole otherwise. next_unit is the work counter, zeroed beforehand.
 wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n, int64_t k, float alpha,
                      const float *A, int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
                      float *ahi, float *alo, float *bhi, float *blo, char *sk, size_t partial_room,
-                     int64_t counter_room, unsigned *next_unit, const wg_gate &gate, int uplo) {
+                     int64_t counter_room, unsigned *next_unit, const wg_gate &gate, int uplo, bool pdl) {
   const Layout L = layout_of(m, n, k);
   const int G = d->sm_count;
   Plan plan = plan_of(G, L, true);
@@ -577,8 +580,17 @@ wg_status launch_mma(wg_device *d, int transA, int transB, int64_t m, int64_t n,
   WG_CUDA(wg_kernel_smem(kern, Sh::SMEM));
   {
     wg_launch_scope scope(d, "sgemm_tf32x3_mma");
-    kern<<<plan.grid, THREADS, Sh::SMEM, d->stream>>>(maps[0], maps[1], maps[2], maps[3], args);
-    WG_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)plan.grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = Sh::SMEM;
+    cfg.stream = d->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    WG_CUDA(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], args));
   }
   return WG_OK;
 }
@@ -706,7 +718,7 @@ wg_status wg_sgemm_tf32x3(wg_device *d, int transA, int transB, int64_t m, int64
   if (st != WG_OK) return st;
   const wg_gate gate{flag, flag, epoch, epoch};
   return launch_mma(d, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, ahi, alo, bhi, blo, sk,
-                    partial_room, plan.sk_tiles, next_unit, gate, uplo);
+                    partial_room, plan.sk_tiles, next_unit, gate, uplo, /*pdl=*/true);
 }
 
 // ---- panelled products ----------------------------------------------------
@@ -826,7 +838,8 @@ wg_status wg_tc_product_panel(wg_tc_product *p, int64_t cols, const float *B, in
   char *sk = p->ws + p->a_region + 2 * p->slot_bytes;
   const wg_gate gate{d->dwords + WG_DW_FALLBACK_A, flag_b, p->epoch_a, epoch_b};
   st = launch_mma(d, p->transA, p->transB, p->m, cols, p->k, p->alpha, p->A, p->lda, B, ldb, p->beta, C, ldc, ahi,
-                  alo, bhi, blo, sk, p->partial_room, p->counter_room, next_unit, gate, WG_UPLO_FULL);
+                  alo, bhi, blo, sk, p->partial_room, p->counter_room, next_unit, gate, WG_UPLO_FULL,
+                  /*pdl=*/false);  // an event wait, not the split, precedes it on the stream
   if (st != WG_OK) return st;
   WG_CUDA(cudaEventRecord(d->tc_ev[EV_SLOT0 + slot], d->stream));
   d->stats.tf32x3_launches++;
