@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_dot_kernel(int64_t m, int64_t n, const T *__restrict__ A, int64_t lda, const T *__restrict__ x,
                     int64_t incx, int64_t rows, int chunks, T alpha, T beta, T *__restrict__ y, int64_t incy,
                     T *__restrict__ partial) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   __shared__ T red[GEMV_THREADS / 32];
   const int64_t i0 = (int64_t)blockIdx.y * rows;
   const int64_t i1 = i0 + rows < m ? i0 + rows : m;
@@ -111,6 +113,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2)
     gemv_dot_vec_kernel(int64_t m, int64_t n, const T *__restrict__ A, int64_t lda, const T *__restrict__ x,
                         int64_t rows, int chunks, T alpha, T beta, T *__restrict__ y, int64_t incy,
                         T *__restrict__ partial) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   using V = typename V16<T>::type;
   constexpr int W = V16<T>::N, U = 8;
   const int lane = threadIdx.x & 31;
@@ -168,6 +172,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_axpy_vec_kernel(int64_t mv, int64_t n, const T *__restrict__ A, int64_t lda, const T *__restrict__ x,
                          int64_t incx, int64_t cols, int chunks, int64_t ylen, T alpha, T beta, T *__restrict__ y,
                          int64_t incy, T *__restrict__ partial) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   using V = typename V16<T>::type;
   constexpr int W = V16<T>::N;
   const int64_t t = (int64_t)blockIdx.x * GEMV_THREADS + threadIdx.x;  // vector row index
@@ -234,6 +240,8 @@ template <typename T, int L, bool UNIT_X>
 __global__ void __launch_bounds__(ROWS_THREADS)
     gemv_rows_kernel(int64_t m, int64_t n, const T *__restrict__ A, int64_t lda, const T *__restrict__ x,
                      int64_t incx, T alpha, T beta, T *__restrict__ y, int64_t incy) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   using V = typename V16<T>::type;
   constexpr int W = V16<T>::N, G = ROWS_THREADS / L, R = W * L, S = ROWS_THREADS / R, U = 8;
   static_assert(G % S == 0, "slices must split the column groups evenly");
@@ -324,6 +332,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_axpy_kernel(int64_t i_begin, int64_t m, int64_t n, const T *__restrict__ A, int64_t lda,
                      const T *__restrict__ x, int64_t incx, int64_t cols, int chunks, T alpha, T beta,
                      T *__restrict__ y, int64_t incy, T *__restrict__ partial) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   const int64_t i = i_begin + (int64_t)blockIdx.x * GEMV_THREADS + threadIdx.x;
   if (i >= m) return;  // no barriers below
   const int64_t j0 = (int64_t)blockIdx.y * cols;
@@ -358,6 +368,8 @@ template <typename T>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_reduce_kernel(int64_t len, int chunks, const T *__restrict__ partial, T alpha, T beta, T *__restrict__ y,
                        int64_t incy) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   for (int64_t i = (int64_t)blockIdx.x * GEMV_THREADS + threadIdx.x; i < len;
        i += (int64_t)gridDim.x * GEMV_THREADS) {
     T s = T(0);
@@ -377,6 +389,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 // alpha = 0: y := beta * y (0 when beta = 0, y not read).
 template <typename T>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_scale_kernel(int64_t len, T beta, T *__restrict__ y, int64_t incy) {
+  wg_pdl_wait();     // launched programmatically: the kernel before this one has finished
+  wg_pdl_trigger();  // and the next gemv launch may be scheduled
   for (int64_t i = (int64_t)blockIdx.x * GEMV_THREADS + threadIdx.x; i < len;
        i += (int64_t)gridDim.x * GEMV_THREADS) {
     T *p = y + i * incy;
@@ -409,16 +423,20 @@ void launch_rows(int lanes, unsigned g, cudaStream_t s, int64_t m, int64_t n, co
                  int64_t incx, T alpha, T beta, T *y, int64_t incy) {
   switch (lanes) {
     case 32:
-      gemv_rows_kernel<T, 32, UNIT_X><<<g, ROWS_THREADS, 0, s>>>(m, n, A, lda, x, incx, alpha, beta, y, incy);
+      wg_launch_pdl(gemv_rows_kernel<T, 32, UNIT_X>, dim3(g), dim3(ROWS_THREADS), 0, s, m, n, A, lda, x, incx, alpha,
+                    beta, y, incy);
       break;
     case 16:
-      gemv_rows_kernel<T, 16, UNIT_X><<<g, ROWS_THREADS, 0, s>>>(m, n, A, lda, x, incx, alpha, beta, y, incy);
+      wg_launch_pdl(gemv_rows_kernel<T, 16, UNIT_X>, dim3(g), dim3(ROWS_THREADS), 0, s, m, n, A, lda, x, incx, alpha,
+                    beta, y, incy);
       break;
     case 8:
-      gemv_rows_kernel<T, 8, UNIT_X><<<g, ROWS_THREADS, 0, s>>>(m, n, A, lda, x, incx, alpha, beta, y, incy);
+      wg_launch_pdl(gemv_rows_kernel<T, 8, UNIT_X>, dim3(g), dim3(ROWS_THREADS), 0, s, m, n, A, lda, x, incx, alpha,
+                    beta, y, incy);
       break;
     default:
-      gemv_rows_kernel<T, 4, UNIT_X><<<g, ROWS_THREADS, 0, s>>>(m, n, A, lda, x, incx, alpha, beta, y, incy);
+      wg_launch_pdl(gemv_rows_kernel<T, 4, UNIT_X>, dim3(g), dim3(ROWS_THREADS), 0, s, m, n, A, lda, x, incx, alpha,
+                    beta, y, incy);
       break;
   }
 }
@@ -430,7 +448,7 @@ wg_status gemv_enqueue(wg_device *d, int trans, int64_t m, int64_t n, T alpha, c
   const int64_t ylen = trans ? n : m;
   if (alpha == T(0)) {
     wg_launch_scope scope(d, "gemv_scale");
-    gemv_scale_kernel<T><<<grid_for(d, ylen), GEMV_THREADS, 0, s>>>(ylen, beta, y, incy);
+    wg_launch_pdl(gemv_scale_kernel<T>, dim3(grid_for(d, ylen)), dim3(GEMV_THREADS), 0, s, ylen, beta, y, incy);
     WG_CUDA(cudaGetLastError());
     return WG_OK;
   }
@@ -500,33 +518,33 @@ wg_status gemv_enqueue(wg_device *d, int trans, int64_t m, int64_t n, T alpha, c
   const dim3 grid(gx, (unsigned)chunks);
   if (trans && vec) {
     wg_launch_scope scope(d, "gemv_dot");
-    gemv_dot_vec_kernel<T><<<grid, GEMV_THREADS, 0, s>>>(m, n, A, lda, x, span, (int)chunks, alpha, beta, y, incy,
-                                                         partial);
+    wg_launch_pdl(gemv_dot_vec_kernel<T>, grid, dim3(GEMV_THREADS), 0, s, m, n, A, lda, x, span, (int)chunks, alpha,
+                  beta, y, incy, partial);
     WG_CUDA(cudaGetLastError());
   } else if (trans) {
     wg_launch_scope scope(d, "gemv_dot");
-    gemv_dot_kernel<T><<<grid, GEMV_THREADS, 0, s>>>(m, n, A, lda, x, incx, span, (int)chunks, alpha, beta, y, incy,
-                                                     partial);
+    wg_launch_pdl(gemv_dot_kernel<T>, grid, dim3(GEMV_THREADS), 0, s, m, n, A, lda, x, incx, span, (int)chunks, alpha,
+                  beta, y, incy, partial);
     WG_CUDA(cudaGetLastError());
   } else {
     wg_launch_scope scope(d, "gemv_axpy");
     if (vec) {
-      gemv_axpy_vec_kernel<T><<<grid, GEMV_THREADS, 0, s>>>(mv, n, A, lda, x, incx, span, (int)chunks, ylen, alpha,
-                                                            beta, y, incy, partial);
+      wg_launch_pdl(gemv_axpy_vec_kernel<T>, grid, dim3(GEMV_THREADS), 0, s, mv, n, A, lda, x, incx, span, (int)chunks,
+                    ylen, alpha, beta, y, incy, partial);
       WG_CUDA(cudaGetLastError());
     }
     const int64_t rest = m - mv * (int64_t)vb;  // rows no vector covers
     if (rest > 0) {
       const dim3 g2((unsigned)ceil_div(rest, GEMV_THREADS), (unsigned)chunks);
-      gemv_axpy_kernel<T><<<g2, GEMV_THREADS, 0, s>>>(mv * (int64_t)vb, m, n, A, lda, x, incx, span, (int)chunks,
-                                                      alpha, beta, y, incy, partial);
+      wg_launch_pdl(gemv_axpy_kernel<T>, g2, dim3(GEMV_THREADS), 0, s, mv * (int64_t)vb, m, n, A, lda, x, incx, span,
+                    (int)chunks, alpha, beta, y, incy, partial);
       WG_CUDA(cudaGetLastError());
     }
   }
   if (chunks > 1) {
     wg_launch_scope scope(d, "gemv_reduce");
-    gemv_reduce_kernel<T><<<grid_for(d, ylen), GEMV_THREADS, 0, s>>>(ylen, (int)chunks, partial, alpha, beta, y,
-                                                                     incy);
+    wg_launch_pdl(gemv_reduce_kernel<T>, dim3(grid_for(d, ylen)), dim3(GEMV_THREADS), 0, s, ylen, (int)chunks, partial,
+                  alpha, beta, y, incy);
     WG_CUDA(cudaGetLastError());
   }
   return WG_OK;

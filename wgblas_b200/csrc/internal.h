@@ -152,6 +152,26 @@ cudaError_t wg_kernel_smem(F *fn, size_t bytes, bool max_carveout = false) {
   return wg_kernel_smem_raw(reinterpret_cast<const void *>(fn), bytes, max_carveout);
 }
 
+// Launches `kern` with programmatic stream serialization: it may be scheduled
+// while the kernel before it on the stream finishes, so it must call
+// wg_pdl_wait before it touches memory (gemv.cu, which also triggers its own
+// dependents right after that wait).
+template <class... KArgs, class... Args>
+cudaError_t wg_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                          Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+}
+
 // Makes `ordinal` current for the lifetime of the guard.
 struct wg_device_guard {
   int prev;
