@@ -39,6 +39,7 @@
 #include <cuda.h>
 
 #include "internal.h"
+#include "simt_tile.cuh"
 #include "tcgen05.cuh"
 #include "tf32x3_common.cuh"
 
@@ -84,7 +85,45 @@ struct FArgs {
   uint32_t epoch;
   int units;
   int uplo;
+  // The caller's operands, for tiles computed on the FFMA pipe (one-CTA form).
+  const float *A, *B;
+  int64_t lda, ldb;
 };
+
+// Row i of the C tile at column n0, bn wide, on the FFMA pipe: each element one
+// sequential fused multiply-add chain over p = 0..k-1 and then the SIMT GEMM's
+// epilogue, so the bits are the FFMA kernel's (and the oracle's). Used for a tile
+// whose operands the split ruled out; one thread per row, op(A) loads coalesced
+// across the rows, op(B) loads the same address across the warp.
+template <int A_K, int B_K>
+__device__ __forceinline__ void ffma_tile_row(const FArgs &a, int64_t i, int64_t n0, int bn) {
+  constexpr int J = 4;
+  const int64_t kk = a.alpha == 0.0f ? 0 : a.k;
+  for (int c = 0; c < bn && n0 + c < a.n; c += J) {
+    const int64_t j0 = n0 + c;
+    float acc[J];
+#pragma unroll
+    for (int j = 0; j < J; j++) acc[j] = 0.0f;
+    for (int64_t p = 0; p < kk; p++) {
+      const float av = A_K ? a.A[p + i * a.lda] : a.A[i + p * a.lda];
+#pragma unroll
+      for (int j = 0; j < J; j++) {
+        const int64_t jj = j0 + j;
+        const float bv = jj < a.n ? (B_K ? a.B[p + jj * a.ldb] : a.B[jj + p * a.ldb]) : 0.0f;
+        acc[j] = __fmaf_rn(av, bv, acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+      const int64_t jj = j0 + j;
+      if (jj < a.n && wg_in_triangle(a.uplo, i, jj)) {
+        float *cp = a.C + i + jj * a.ldc;
+        const float old = a.beta != 0.0f ? *cp : 0.0f;
+        *cp = wgsimt::epilogue(acc[j], a.alpha, a.beta, old);
+      }
+    }
+  }
+}
 
 // True when x is outside the split's exact range (wg3::split_ok, on the bits:
 // |x| as an integer is 0, or within [2^-50, 2^50]; NaN and Inf are above).
@@ -500,11 +539,12 @@ tf32x3_fused(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ 
         }
       }
       if (finish && ruled_out) {
-        // Leave C untouched: the gated FFMA kernel computes this tile.
-        if (threadIdx.x == 64) {
-          args.tile_flags[tm + (int64_t)tn * args.tiles_m] = args.epoch;
-          atomicExch(args.dwords + WG_DW_FALLBACK, args.epoch);
-        }
+        // Operands the split cannot carry: this tile's C on the FFMA pipe, with
+        // the reference's IEEE semantics. The call's first such tile counts one
+        // fallback.
+        if (threadIdx.x == 64 && atomicExch(args.dwords + WG_DW_FALLBACK, args.epoch) != args.epoch)
+          atomicAdd(args.dwords + WG_DW_FALLBACKS, 1u);
+        if (row < args.m) ffma_tile_row<A_K, B_K>(args, row, n0, BN);
       } else if (finish) {
         const int nseg = whole ? 1 : args.sk_split;
         const int own = whole ? 0 : u.seg;
@@ -1133,22 +1173,16 @@ wg_status wg_sgemm_tf32x3_fused(wg_device *d, cudaStream_t st, int transA, int t
   const wg3::Plan &p = L.plan;
   FArgs args{m, n, k, alpha, beta, C, ldc, d->dwords, L.tiles_m, L.tiles_n, L.kt, p.dp_tiles, p.sk_tiles,
              p.sk_split, p.sk_tiles ? reinterpret_cast<float *>(w) : nullptr, zero, zero + 1,
-             zero + 1 + p.sk_tiles, zero + 1 + 2 * p.sk_tiles, epoch, p.dp_tiles + p.sk_tiles * p.sk_split, uplo};
+             zero + 1 + p.sk_tiles, zero + 1 + 2 * p.sk_tiles, epoch, p.dp_tiles + p.sk_tiles * p.sk_split, uplo,
+             A, B, lda, ldb};
   {
+    // One launch: tiles whose operands the split rules out are computed by the
+    // same kernel on the FFMA pipe.
     wg_launch_scope scope(d, "sgemm_tf32x3_fused", st);
     cudaError_t e = L.bn == 256 ? launch_bn<256>(st, p.grid, a_k, b_k, maps[0], maps[1], args)
                   : L.bn == 128 ? launch_bn<128>(st, p.grid, a_k, b_k, maps[0], maps[1], args)
                                 : launch_bn<64>(st, p.grid, a_k, b_k, maps[0], maps[1], args);
     WG_CUDA(e);
-  }
-  {
-    // Computes the tiles the kernel left to it (operands outside the split's
-    // exact range); a closed gate exits at once.
-    wg_launch_scope scope(d, "sgemm_simt_fallback", st);
-    const wg_gate gate{d->dwords + WG_DW_FALLBACK, d->dwords + WG_DW_FALLBACK, epoch, epoch};
-    const wg_tile_mask mask{args.tile_flags, L.tiles_m, L.bn, epoch};
-    WG_CUDA(wg_launch_gemm_simt_masked(st, transA, transB, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, d->dwords,
-                                       &gate, &mask, uplo));
   }
   return WG_OK;
 }
