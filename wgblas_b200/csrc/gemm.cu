@@ -72,13 +72,15 @@ wg_status wg_gemm_enqueue(wg_device *d, int transA, int transB, int64_t m, int64
 namespace {
 
 // Small products on the FFMA pipe: the 32 x 64-tile kernel beats the 3xTF32
-// kernels while each SM runs at most 80 of its 16-deep k-tiles (one CTA per
-// SM per wave). Measured per call on B200 with L2 flushed between calls:
-// 256^3 22 vs 38 us, 512^3 28 vs 41 us, 640^3 43 vs 45 us; 768^3 51 vs 47 us
-// and 256 x 256 x 4096 127 vs 57 us go to the tensor cores.
+// kernels while its tiles take at most two waves over the SMs and each SM runs
+// at most 80 of its 16-deep k-tiles. Measured per call on B200 with L2 flushed
+// between calls: 256^3 22 vs 38 us, 512^3 28 vs 41 us, 640^3 43 vs 45 us,
+// 64 x 4096 x 64 8.8 vs 13.3 us; 768^3 51 vs 47 us, 256 x 256 x 4096 127 vs
+// 57 us and 256 x 4096 x 256 (four waves) 33.6 vs 19.3 us go to the tensor cores.
 bool small_ffma_wins(const wg_device *d, int64_t m, int64_t n, int64_t k) {
   const int64_t tiles = ((m + 31) / 32) * ((n + 63) / 64), sm = d->sm_count > 0 ? d->sm_count : 1;
-  return (tiles + sm - 1) / sm * ((k + 15) / 16) <= 80;
+  const int64_t waves = (tiles + sm - 1) / sm;
+  return waves <= 2 && waves * ((k + 15) / 16) <= 80;
 }
 
 // FFMA work (no tensor cores) goes to the 32 x 64-tile kernel when asked, when

@@ -18,7 +18,7 @@
 //
 // so the m*n*order multiply-adds run almost entirely in a few large GEMMs
 // (the 3xTF32 tensor-core path for the deep updates of the upper levels, the
-// FFMA kernel for shallow updates, small shapes and non-finite operands), and
+// FFMA kernels for shallow updates, small shapes and non-finite operands), and
 // the diagonal blocks in `strsm_leaf`. The reference instead
 // walks 64-row blocks one at a time with a k=64 update GEMM after each
 // (strsm.mjs:399-432) and, above eight blocks, applies explicit block inverses
@@ -40,11 +40,6 @@ namespace {
 constexpr int LEAF = 64;      // rows of a diagonal block
 constexpr int LEAF_RHS = 64;  // right-hand sides per CTA, one per thread
 constexpr int LS = LEAF + 4;  // shared row stride: keeps 16-byte alignment of each column
-// Updates at most this deep (the lower levels of the recursion) run on the FFMA
-// kernel: the tensor-core path costs a split pass plus a fixed time per call in
-// its MMA kernel (68 us for a 512^3 product, measured with per-kernel events)
-// that a k <= 256 update does not amortise.
-constexpr int64_t SIMT_MAX_K = 256;
 // Right-hand sides up to which `auto` takes the flow form.
 constexpr int64_t FLOW_AUTO_MAX_RHS = 1024;
 
@@ -413,18 +408,13 @@ struct Trsm {
     return WG_OK;
   }
 
-  // C := -op(X) op(Y) + beta C, on the FFMA kernel when k is shallow.
+  // C := -op(X) op(Y) + beta C through the sgemm dispatcher: the shallow updates
+  // of the lower levels go to the small-tile FFMA kernel (a 64 x 4096 x 64
+  // update: 8.8 us against 19.1 on the 128 x 128-tile FFMA kernel, which gives
+  // it 32 CTAs), the deeper ones to the tensor cores.
   wg_status gemm(int tX, int tY, int64_t m, int64_t n, int64_t k, const float *X, int64_t ldx, const float *Y,
                  int64_t ldy, float beta, float *C, int64_t ldc) const {
-    if (k > SIMT_MAX_K || d->sgemm_path == WG_SGEMM_TF32X3)
-      return wg_gemm_enqueue<float>(d, tX, tY, m, n, k, -1.0f, X, ldx, Y, ldy, beta, C, ldc);
-    if (m == 0 || n == 0) return WG_OK;
-    d->stats.calls++;
-    d->stats.simt_launches++;
-    wg_launch_scope scope(d, "sgemm_simt");
-    WG_CUDA(wg_launch_gemm_simt<float>(d->stream, tX, tY, m, n, k, -1.0f, X, ldx, Y, ldy, beta, C, ldc, d->dwords,
-                                       nullptr));
-    return WG_OK;
+    return wg_gemm_enqueue<float>(d, tX, tY, m, n, k, -1.0f, X, ldx, Y, ldy, beta, C, ldc);
   }
 
   // Bt[R] := beta * Bt[R] - Lt[R, J] * Xt[J], R = [r0, r0 + nr), J = [j0, j0 + nj).
