@@ -62,20 +62,25 @@ __global__ void __launch_bounds__(LEAF_RHS) strsm_leaf(LeafArgs a) {
   __shared__ float rd[LEAF];
   const int nb = a.nb;
   // Only the referenced triangle is read (the other one may hold anything);
-  // everything else in the tile is zero.
-  for (int e = threadIdx.x; e < LEAF * LEAF; e += blockDim.x) {
-    int i, k;
-    if (a.l_rs == 1) {  // Lt(i, k) contiguous in i
-      i = e % LEAF;
-      k = e / LEAF;
-    } else {
-      k = e % LEAF;
-      i = e / LEAF;
-    }
+  // everything else in the tile is zero. All of a thread's loads are issued
+  // before its first store (a loop over them one at a time paid a memory
+  // latency per element).
+  constexpr int PER = LEAF * LEAF / LEAF_RHS;
+  float v[PER];
+#pragma unroll
+  for (int q = 0; q < PER; q++) {
+    const int e = threadIdx.x + q * LEAF_RHS;
+    const int i = a.l_rs == 1 ? e % LEAF : e / LEAF;  // Lt(i, k) contiguous in i, or in k
+    const int k = a.l_rs == 1 ? e / LEAF : e % LEAF;
     const bool below = FORWARD ? i > k : i < k;
-    float v = 0.0f;
-    if (i < nb && k < nb && below) v = a.L[i * a.l_rs + k * a.l_cs];
-    Ls[k][i] = v;
+    v[q] = (i < nb && k < nb && below) ? a.L[i * a.l_rs + k * a.l_cs] : 0.0f;
+  }
+#pragma unroll
+  for (int q = 0; q < PER; q++) {
+    const int e = threadIdx.x + q * LEAF_RHS;
+    const int i = a.l_rs == 1 ? e % LEAF : e / LEAF;
+    const int k = a.l_rs == 1 ? e / LEAF : e % LEAF;
+    Ls[k][i] = v[q];
   }
   for (int k = threadIdx.x; k < LEAF; k += blockDim.x)
     rd[k] = (k < nb && !a.unit) ? 1.0f / a.L[k * (a.l_rs + a.l_cs)] : 1.0f;
