@@ -31,11 +31,14 @@
 // kernel. gemmtr calls skip tiles with no element in the triangle.
 //
 // IEEE semantics: a tile whose operands include an element outside the
-// split's exact range is not written; its entry in a per-tile flag array gets
-// the call's epoch (and the device's fallback word too), and the FFMA kernel
-// launched after this one, gated on those words, computes exactly the flagged
-// tiles from the untouched C. Every wait is clock-bounded (a stalled pipeline
-// sets a bit in the device error word, the roles drain, TMEM is freed).
+// split's exact range is computed on the FFMA pipe instead, by the epilogue
+// warps of the CTA that finishes it (ffma_tile_row: the FFMA kernel's
+// arithmetic, so its bits) from the untouched C. The CTA-pair form leaves such
+// a tile unwritten, gives its entry in a per-tile flag array the call's epoch
+// (and the device's fallback word too), and the FFMA kernel launched after it,
+// gated on those words, computes exactly the flagged tiles. Every wait is
+// clock-bounded (a stalled pipeline sets a bit in the device error word, the
+// roles drain, TMEM is freed).
 #include <cuda.h>
 
 #include "internal.h"
@@ -81,7 +84,7 @@ struct FArgs {
   unsigned *next_unit;   // work counter (zero at launch)
   unsigned *counters;    // split tiles: arrivals (zero at launch, reset by the finishing segment)
   unsigned *tile_bad;    // split tiles: a segment saw ruled-out operands (zero at launch)
-  unsigned *tile_flags;  // [tiles_m * tiles_n]: `epoch` where the FFMA kernel computes the tile
+  unsigned *tile_flags;  // CTA-pair form: [tiles]: `epoch` where the FFMA kernel computes the tile
   uint32_t epoch;
   int units;
   int uplo;
