@@ -105,9 +105,10 @@ wg_status wg_selftest_bounded_wait(wg_device *dev, unsigned budget_us);
 typedef struct wg_sgemm_stats {
   uint64_t calls;           /* sgemm calls that reached a kernel */
   uint64_t tf32x3_launches; /* calls dispatched to the 3xTF32 tensor-core kernel */
-  uint64_t simt_launches;   /* calls dispatched straight to the FFMA kernel */
+  uint64_t simt_launches;   /* calls dispatched straight to an FFMA kernel (either tile size) */
   uint64_t fallbacks;       /* 3xTF32 calls that found non-finite or out-of-range
-                               operands on the device and ran the FFMA kernel instead */
+                               operands on the device and computed C (or the affected
+                               tiles) on the FFMA pipe instead, with the FFMA kernel's bits */
 } wg_sgemm_stats;
 wg_status wg_device_sgemm_stats(wg_device *dev, wg_sgemm_stats *stats);
 
