@@ -5,47 +5,122 @@
 // this library's kernels. Also the device-to-device block copy the in-place
 // strmm result needs.
 //
-// Both passes are HBM-bound elementwise copies (one read, one write per element
-// of the n x n result; reads of the mirrored triangle are strided but stay in L2
-// for the sizes these routines see), grid-stride over column-major output so
-// every warp writes 32 consecutive elements of one column.
+// Both passes are HBM-bound copies (one read, one write per element of the
+// n x n result) over 32 x 32 tiles staged in shared memory: a tile whose values
+// come from the mirrored triangle (symmetrize) or from the transpose (trmm's
+// transposed operand) is read as the mirror tile, coalesced along its columns,
+// and written transposed, coalesced along the output's columns. Only the
+// referenced triangle of A is ever read. At 4096 x 4096 symmetrize takes 56 us
+// and triangularize 52 us (62 and 58 elementwise, with the mirrored reads
+// strided), about 2.3 TB/s of read plus write.
 #include "internal.h"
 
 namespace {
 
+constexpr int TT = 32;  // tile edge; 256 threads = 32 x 8
+// Tiles per block step, all loaded before any is stored. Four (16 loads per
+// thread in flight) measured no faster than one at 4096 (60 against 58 us for
+// symmetrize): the pass is not bound by loads in flight.
+constexpr int TQ = 1;
+
 // out(i, j) = A(i, j) where (i, j) is in the stored triangle (lower: i >= j,
 // upper: i <= j, column-major frame), A(j, i) elsewhere.
 template <typename T>
-__global__ void symmetrize_kernel(int64_t n, int lower, const T *__restrict__ A, int64_t lda, T *__restrict__ out,
-                                  int64_t ldo) {
-  const int64_t total = n * n;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = e % n, j = e / n;
-    const bool stored = lower ? i >= j : i <= j;
-    out[i + j * ldo] = stored ? A[i + j * lda] : A[j + i * lda];
+__global__ void __launch_bounds__(256) symmetrize_kernel(int64_t n, int lower, const T *__restrict__ A, int64_t lda,
+                                                         T *__restrict__ out, int64_t ldo) {
+  __shared__ T S[TQ][TT][TT + 1];  // S[q][c][r] = A(si*TT + r, sj*TT + c) of the q-th tile
+  const int tx = threadIdx.x % TT, ty = threadIdx.x / TT;
+  const int64_t tiles = (n + TT - 1) / TT, total = tiles * tiles;
+  for (int64_t t0 = (int64_t)blockIdx.x * TQ; t0 < total; t0 += (int64_t)gridDim.x * TQ) {
+    __syncthreads();  // the previous tiles' reads of S are done
+#pragma unroll
+    for (int q = 0; q < TQ; q++) {  // every load of the TQ tiles before any store
+      const int64_t t = t0 + q;
+      if (t >= total) break;
+      const int64_t bi = t % tiles, bj = t / tiles;  // output tile: rows bi*TT.., columns bj*TT..
+      const bool diag = bi == bj, stored_tile = lower ? bi > bj : bi < bj;
+      // The tile holding these values: this one (stored side, or the diagonal), else its mirror.
+      const int64_t si = (stored_tile || diag) ? bi : bj, sj = (stored_tile || diag) ? bj : bi;
+#pragma unroll
+      for (int c = ty; c < TT; c += 8) {
+        const int64_t gi = si * TT + tx, gj = sj * TT + c;
+        const bool in = gi < n && gj < n && (!diag || (lower ? gi >= gj : gi <= gj));
+        S[q][c][tx] = in ? A[gi + gj * lda] : T(0);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < TQ; q++) {
+      const int64_t t = t0 + q;
+      if (t >= total) break;
+      const int64_t bi = t % tiles, bj = t / tiles;
+      const bool diag = bi == bj, stored_tile = lower ? bi > bj : bi < bj;
+#pragma unroll
+      for (int c = ty; c < TT; c += 8) {
+        const int64_t i = bi * TT + tx, j = bj * TT + c;
+        if (i >= n || j >= n) continue;
+        T v;
+        if (diag)
+          v = (lower ? i >= j : i <= j) ? S[q][c][tx] : S[q][tx][c];  // A(i, j), or A(j, i) from the same tile
+        else
+          v = stored_tile ? S[q][c][tx] : S[q][tx][c];
+        out[i + j * ldo] = v;
+      }
+    }
   }
 }
 
 // T(i, j) = 1 on the diagonal when `unit` (A's diagonal is not read), A(i, j)
 // inside the stored triangle, 0 outside; out = T, or T^T when `trans`.
 template <typename T>
-__global__ void triangularize_kernel(int64_t n, int lower, int unit, int trans, const T *__restrict__ A, int64_t lda,
-                                     T *__restrict__ out, int64_t ldo) {
-  const int64_t total = n * n;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = e % n, c = e / n;
-    const int64_t i = trans ? c : r, j = trans ? r : c;  // the element of T that lands at out(r, c)
-    T v;
-    if (i == j)
-      v = unit ? T(1) : A[i + j * lda];
-    else
-      v = (lower ? i > j : i < j) ? A[i + j * lda] : T(0);
-    out[r + c * ldo] = v;
+__global__ void __launch_bounds__(256) triangularize_kernel(int64_t n, int lower, int unit, int trans,
+                                                            const T *__restrict__ A, int64_t lda, T *__restrict__ out,
+                                                            int64_t ldo) {
+  __shared__ T S[TQ][TT][TT + 1];  // S[q][c][r] = A(si*TT + r, sj*TT + c) of the q-th tile
+  const int tx = threadIdx.x % TT, ty = threadIdx.x / TT;
+  const int64_t tiles = (n + TT - 1) / TT, total = tiles * tiles;
+  for (int64_t t0 = (int64_t)blockIdx.x * TQ; t0 < total; t0 += (int64_t)gridDim.x * TQ) {
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < TQ; q++) {  // every load of the TQ tiles before any store
+      const int64_t t = t0 + q;
+      if (t >= total) break;
+      const int64_t br = t % tiles, bc = t / tiles;              // output tile: rows br*TT.., columns bc*TT..
+      const int64_t si = trans ? bc : br, sj = trans ? br : bc;  // the tile of T (and of A) they come from
+      if (lower ? si < sj : si > sj) continue;                   // wholly outside the triangle: zeros
+#pragma unroll
+      for (int c = ty; c < TT; c += 8) {
+        const int64_t gi = si * TT + tx, gj = sj * TT + c;
+        T v = T(0);
+        if (gi < n && gj < n) {
+          if (gi == gj)
+            v = unit ? T(1) : A[gi + gj * lda];
+          else if (lower ? gi > gj : gi < gj)
+            v = A[gi + gj * lda];
+        }
+        S[q][c][tx] = v;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < TQ; q++) {
+      const int64_t t = t0 + q;
+      if (t >= total) break;
+      const int64_t br = t % tiles, bc = t / tiles;
+      const int64_t si = trans ? bc : br, sj = trans ? br : bc;
+      const bool outside = lower ? si < sj : si > sj;
+#pragma unroll
+      for (int c = ty; c < TT; c += 8) {
+        const int64_t r = br * TT + tx, cc = bc * TT + c;
+        if (r >= n || cc >= n) continue;
+        out[r + cc * ldo] = outside ? T(0) : (trans ? S[q][tx][c] : S[q][c][tx]);
+      }
+    }
   }
 }
 
-unsigned blocks_for(wg_device *d, int64_t total) {
-  const int64_t want = (total + 255) / 256;
+unsigned blocks_for(wg_device *d, int64_t n) {
+  const int64_t tiles = (n + TT - 1) / TT, want = (tiles * tiles + TQ - 1) / TQ;
   const int64_t cap = (int64_t)d->sm_count * 16;
   return (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
 }
@@ -80,10 +155,10 @@ extern "C" wg_status wg_symmetrize(wg_device *d, int elem_bytes, int uplo, int64
   wg_launch_scope scope(d, "symmetrize");
   const int lower = uplo == WG_UPLO_LOWER;
   if (elem_bytes == 4)
-    symmetrize_kernel<float><<<blocks_for(d, n * n), 256, 0, d->stream>>>(
+    symmetrize_kernel<float><<<blocks_for(d, n), 256, 0, d->stream>>>(
         n, lower, static_cast<const float *>(A->ptr) + offA, lda, static_cast<float *>(out->ptr) + offO, ldo);
   else
-    symmetrize_kernel<double><<<blocks_for(d, n * n), 256, 0, d->stream>>>(
+    symmetrize_kernel<double><<<blocks_for(d, n), 256, 0, d->stream>>>(
         n, lower, static_cast<const double *>(A->ptr) + offA, lda, static_cast<double *>(out->ptr) + offO, ldo);
   WG_CUDA(cudaGetLastError());
   return WG_OK;
@@ -100,11 +175,11 @@ extern "C" wg_status wg_triangularize(wg_device *d, int elem_bytes, int uplo, in
   wg_launch_scope scope(d, "triangularize");
   const int lower = uplo == WG_UPLO_LOWER;
   if (elem_bytes == 4)
-    triangularize_kernel<float><<<blocks_for(d, n * n), 256, 0, d->stream>>>(
+    triangularize_kernel<float><<<blocks_for(d, n), 256, 0, d->stream>>>(
         n, lower, unit, trans, static_cast<const float *>(A->ptr) + offA, lda, static_cast<float *>(out->ptr) + offO,
         ldo);
   else
-    triangularize_kernel<double><<<blocks_for(d, n * n), 256, 0, d->stream>>>(
+    triangularize_kernel<double><<<blocks_for(d, n), 256, 0, d->stream>>>(
         n, lower, unit, trans, static_cast<const double *>(A->ptr) + offA, lda,
         static_cast<double *>(out->ptr) + offO, ldo);
   WG_CUDA(cudaGetLastError());
