@@ -44,6 +44,16 @@ class Adapter:
         return f"<wgblas Adapter cuda:{self.ordinal} {self.info.get('device', '')}>"
 
 
+# Device.set_sgemm_path's names for the WG_SGEMM_* codes of include/wgblas.h.
+SGEMM_PATHS = {"auto": nat.WG_SGEMM_AUTO, "simt": nat.WG_SGEMM_SIMT, "tf32x3": nat.WG_SGEMM_TF32X3,
+               "tf32x3_packed": nat.WG_SGEMM_TF32X3_PACKED,
+               "tf32x3_fused_bn256": nat.WG_SGEMM_TF32X3_FUSED_BN256,
+               "tf32x3_fused_bn128": nat.WG_SGEMM_TF32X3_FUSED_BN128,
+               "tf32x3_fused_bn64": nat.WG_SGEMM_TF32X3_FUSED_BN64,
+               "tf32x3_pair": nat.WG_SGEMM_TF32X3_PAIR,
+               "simt_small": nat.WG_SGEMM_SIMT_SMALL}
+
+
 class Device:
     """A CUDA device handle: the counterpart of the reference's GPUDevice."""
 
@@ -100,14 +110,7 @@ class Device:
         'tf32x3_packed' (split pass + MMA kernel) or 'tf32x3_fused_bn256' / '_bn128' /
         '_bn64' (the fused kernel with one tile width) or 'tf32x3_pair' (its CTA-pair form),
         or 'simt_small' (the FFMA kernel's arithmetic on 32 x 64 tiles)."""
-        code = {"auto": nat.WG_SGEMM_AUTO, "simt": nat.WG_SGEMM_SIMT, "tf32x3": nat.WG_SGEMM_TF32X3,
-                "tf32x3_packed": nat.WG_SGEMM_TF32X3_PACKED,
-                "tf32x3_fused_bn256": nat.WG_SGEMM_TF32X3_FUSED_BN256,
-                "tf32x3_fused_bn128": nat.WG_SGEMM_TF32X3_FUSED_BN128,
-                "tf32x3_fused_bn64": nat.WG_SGEMM_TF32X3_FUSED_BN64,
-                "tf32x3_pair": nat.WG_SGEMM_TF32X3_PAIR,
-                "simt_small": nat.WG_SGEMM_SIMT_SMALL}[path]
-        nat.check(nat.lib.wg_device_set_sgemm_path(self.handle, code))
+        nat.check(nat.lib.wg_device_set_sgemm_path(self.handle, SGEMM_PATHS[path]))
 
     def set_dgemm_path(self, path: str) -> None:
         """'auto' (default), 'simt' (DFMA kernel) or 'dmma' (FP64 tensor-core kernel)."""
