@@ -252,9 +252,9 @@ __device__ __forceinline__ VCopy v_copy(int e, int rows, int kcontig, const floa
   return c;
 }
 
-// Issues a copy for k-tile t: elements at p >= kk are zero-filled.
-__device__ __forceinline__ void v_issue(float *tile, const VCopy &c, int64_t t, int64_t kk) {
-  const int64_t k0 = t * S_BK;
+// Issues a copy for the k-tile starting at k0, whose source is `src` (the
+// copy's source advanced by k0 / S_BK steps): elements at p >= kk are zero-filled.
+__device__ __forceinline__ void v_issue(float *tile, const VCopy &c, const float *src, int64_t k0, int64_t kk) {
   int bytes;
   if (c.pk >= 0) {
     const int64_t left = kk - (k0 + c.pk);
@@ -262,7 +262,7 @@ __device__ __forceinline__ void v_issue(float *tile, const VCopy &c, int64_t t, 
   } else {
     bytes = k0 + c.p < kk ? c.valid * 4 : 0;
   }
-  cp_async16(tile + c.dst, bytes ? c.src + t * c.step : c.src, bytes);
+  cp_async16(tile + c.dst, bytes ? src : c.src, bytes);
 }
 
 template <int TA, int TB>
@@ -282,11 +282,21 @@ gemm_simt_small_vec_kernel(int64_t m, int64_t n, int64_t k, float alpha, const f
   const VCopy ca = v_copy(tid, S_BM, TA, A, lda, m0, m, S_LDA);
   const VCopy cb0 = v_copy(tid, S_BN, TB ? 0 : 1, B, ldb, n0, n, S_LDB);
   const VCopy cb1 = v_copy(tid + S_NT, S_BN, TB ? 0 : 1, B, ldb, n0, n, S_LDB);
-  auto issue = [&](int64_t t) {
-    float *as = sm + (t % V_STAGES) * V_STAGE, *bs = as + V_A;
-    v_issue(as, ca, t, kk);
-    v_issue(bs, cb0, t, kk);
-    v_issue(bs, cb1, t, kk);
+  // The next k-tile to issue: its ring stage, first k and the copies' sources
+  // (advanced by one step per tile, so no per-tile index arithmetic).
+  int ws = 0;
+  int64_t kw = 0;
+  const float *pa = ca.src, *pb0 = cb0.src, *pb1 = cb1.src;
+  auto issue = [&]() {
+    float *as = sm + ws * V_STAGE, *bs = as + V_A;
+    v_issue(as, ca, pa, kw, kk);
+    v_issue(bs, cb0, pb0, kw, kk);
+    v_issue(bs, cb1, pb1, kw, kk);
+    pa += ca.step;
+    pb0 += cb0.step;
+    pb1 += cb1.step;
+    kw += S_BK;
+    ws = ws + 1 == V_STAGES ? 0 : ws + 1;
   };
 
   float acc[4][4];
@@ -297,16 +307,18 @@ gemm_simt_small_vec_kernel(int64_t m, int64_t n, int64_t k, float alpha, const f
 
 #pragma unroll
   for (int s = 0; s < V_STAGES - 1; s++) {
-    if (s < ntiles) issue(s);
+    if (s < ntiles) issue();
     cp_async_commit();
   }
-  for (int64_t t = 0; t < ntiles; t++) {
+  int rs = 0;       // the ring stage of k-tile t
+  int64_t rem = kk;  // k values from k-tile t on
+  for (int64_t t = 0; t < ntiles; t++, rem -= S_BK) {
     cp_async_wait<V_STAGES - 2>();
     __syncthreads();
-    if (t + V_STAGES - 1 < ntiles) issue(t + V_STAGES - 1);
+    if (t + V_STAGES - 1 < ntiles) issue();
     cp_async_commit();
-    const float *as = sm + (t % V_STAGES) * V_STAGE, *bs = as + V_A;
-    const int64_t rem = kk - t * S_BK;
+    const float *as = sm + rs * V_STAGE, *bs = as + V_A;
+    rs = rs + 1 == V_STAGES ? 0 : rs + 1;
     // Four p at a time: a[i][q], b[j][q] for rows 4tx+i, columns 4ty+j, p = p0+q.
     auto group = [&](int p0, int np) {
       float a[4][4], b[4][4];
