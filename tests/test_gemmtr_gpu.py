@@ -189,3 +189,41 @@ def test_dgemmtr_quick_return_and_alpha_zero(wg, device):
     mask = triangle_mask(case)
     assert bits_equal(got[mask], (np.float32(2.0) * case["C"][mask]).astype(np.float32))
     assert bits_equal(got[~mask], case["C"][~mask])
+
+
+@pytest.mark.parametrize("path", ["tf32x3_packed", "tf32x3"])
+@pytest.mark.parametrize("uplo", ["lower", "upper"])
+@pytest.mark.parametrize("bad", [np.inf, np.nan])
+def test_tensor_core_fallback_keeps_the_triangle(wg, device, oracle, path, uplo, bad):
+    """A non-finite operand on the tensor-core paths: the split pass + MMA kernel
+    computes the whole call's C on the FFMA pipe itself, the fused kernel ('tf32x3'
+    at this size) the flagged tiles (the 128-row band holding the bad row of op(A)).
+    Those come out bit for bit as the FMA restatement, the rest within the fp32
+    bound, and nothing outside the triangle is touched."""
+    case = random_case("sgemmtr", uplo, "column-major", n=520, k=200, m=600, pad=0, seed=29)
+    case["A"][7 + 3 * case["lda"]] = bad  # op(A) row 7
+    before = device.sgemm_stats()
+    device.set_sgemm_path(path)
+    try:
+        got = call(wg, device, case, case["A"], case["B"], case["C"])["C"]
+    finally:
+        device.set_sgemm_path("auto")
+    after = device.sgemm_stats()
+    assert after["tf32x3_launches"] > before["tf32x3_launches"]
+    assert after["fallbacks"] == before["fallbacks"] + 1
+    mask = triangle_mask(case)
+    assert bits_equal(got[~mask], case["C"][~mask]), "an element outside the triangle changed"
+    want = oracle_result(oracle, case, lambda *a: oracle.sgemmtr(*a, variant=1))
+    if path == "tf32x3_packed":
+        assert bits_equal(got, want)
+        return
+    rows = np.arange(case["C"].size) % case["ldc"]
+    band = mask & (rows < 128)
+    assert bits_equal(got[band], want[band]), "the flagged tiles differ from the FMA restatement"
+    rest = mask & (rows >= 128)
+    c64 = dict(case, A=case["A"].astype(np.float64), B=case["B"].astype(np.float64), C=case["C"].astype(np.float64))
+    truth = oracle_result(oracle, c64, oracle.dgemmtr_fma)
+    absc = dict(c64, A=np.abs(c64["A"]), B=np.abs(c64["B"]), C=np.abs(c64["C"]), alpha=abs(case["alpha"]),
+                beta=abs(case["beta"]))
+    bound = 2.0**-24 * 2 * case["k"] * oracle_result(oracle, absc, oracle.dgemmtr_fma)
+    assert np.all(np.abs(got[rest].astype(np.float64) - truth[rest]) <= bound[rest])
